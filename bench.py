@@ -1,0 +1,381 @@
+"""Benchmark of the quantized-weight hot path on B200.
+
+Headline (one JSON line on rank 0): batch-1 greedy decode tok/s of the
+BitNet-b1.58-2B-shaped ternary+LoRA model (I2_S weights, rank-16 LoRA alpha 32,
+merged on the device to F16), after a 32-token prompt, seed 0.  A "step" is
+one decoded token: all 30 layers + lm_head + argmax on the device.
+
+  value  -- K chained decode steps timed with CUDA events on the context
+            stream (weights, KV cache and token ids resident in HBM)
+  e2e    -- the same K steps through the reference-facing C ABI
+            (tvb_decode_step: host token/pos in, host logits out, synchronous)
+  roofline -- the dominant kernel (the streaming F16 GEMV) timed live here on
+            the gate-projection shape, rotating over all 30 layers
+  cpu_baseline -- the reference's own --no-gpu decode (oracle/_ref, built from
+            the reference sources) on this host's cores, on a bounded sample
+
+``--impl reference`` times the reference's CPU decode alone (the reference
+has no B200 path; its CPU implementation is the arm the ratio is taken on).
+
+Multi-GPU: the 2B shape has 5 KV heads, so it does not shard by heads; N GPUs
+run N independent replicas (weak scaling), value = total tok/s, timed as the
+max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+
+import numpy as np  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML (read-only) while running."""
+
+    def __init__(self, cuda_index: int = 0, period: float = 0.2):
+        self.period = period
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.h = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nv = pynvml
+        except Exception as e:   # NVML unavailable: report what we can
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8): "hw_slowdown",
+            getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40): "hw_thermal_slowdown",
+            getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20): "sw_thermal_slowdown",
+            getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4): "sw_power_cap",
+            getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80): "hw_power_brake_slowdown",
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in names.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def report(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def reference_model_random(shape, seed=0):
+    """The reference Model (oracle/_ref) on the 2B shape with random F16
+    weights of merged-weight magnitude, generated on the host."""
+    from oracle.oracle import PROJ_DIMS, ReferenceModel, Reference
+    rng = np.random.default_rng(seed)
+
+    def f16(n, k):
+        # sign | exponent in [2^-10, 2^-3) | mantissa: F16 values of the merged weights' range
+        b = rng.integers(0, 1 << 15, size=(n, k), dtype=np.uint16)
+        return ((b & 0x83FF) | (((b >> 10) % 7 + 5) << 10)).astype(np.uint16)
+
+    w = {"tok_embd": f16(shape.vocab, shape.hidden), "output_norm": np.ones(shape.hidden, np.float32),
+         "layers": []}
+    for _ in range(shape.layers):
+        lw = {n: f16(*d) for n, d in PROJ_DIMS(shape).items()}
+        for n, length in (("attn_norm", shape.hidden), ("attn_sub_norm", shape.heads * shape.head_dim),
+                          ("ffn_norm", shape.hidden), ("ffn_sub_norm", shape.inter)):
+            lw[n] = np.ones(length, np.float32)
+        w["layers"].append(lw)
+    return ReferenceModel(Reference(), shape, w)
+
+
+def time_reference_decode(rm, steps: int, pos0: int = 32, budget_s: float = 20.0):
+    """Seconds per token of the reference's CPU decode (Model::forward with
+    prefill=false, model.cpp:851-1066), on a bounded sample of `steps`."""
+    t1 = rm.time_decode(1, pos0, 1)   # warm-up + estimate
+    n = max(1, min(steps, int(budget_s / max(t1, 1e-3))))
+    t = rm.time_decode(1, pos0 + 1, n)
+    return t / n, n
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from oracle.oracle import ModelShape
+    from ternative_b200.model import SHAPES
+    cfg = SHAPES[args.config]
+    shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                       cfg.num_kv_heads, cfg.intermediate_size, 512)
+    rm = reference_model_random(shape)
+    threads = rm.ref.L.tvref_omp_threads() if hasattr(rm.ref.L, "tvref_omp_threads") else None
+    for _ in range(max(0, min(args.warmup, 2))):
+        rm.time_decode(1, 32, 1)
+    sec, n = time_reference_decode(rm, args.steps, pos0=40, budget_s=args.cpu_seconds * 3)
+    tps = 1.0 / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16-weights/f32-compute",
+        "data": "synthetic", "config": config_block(args, cfg),
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": f"{n} decode tokens at positions 41..{40 + n} (Model::forward, "
+                                   f"prefill=false) of the 2B shape, random F16 weights"},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    rm.close()
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "batch-1 decode tok/s (BitNet-2B ternary+LoRA, F16-merged)"
+
+
+def config_block(args, cfg):
+    return {"workload": f"{args.config} batch-1 greedy decode after a {args.prompt}-token prompt "
+                        "(I2_S + rank-16 LoRA alpha 32 merged to F16; hidden 2560, 30 layers, "
+                        "20/5 heads, FFN 6912, vocab 128256)",
+            "batch": 1, "prompt": args.prompt, "lora_rank": 16,
+            "l2": "weights stream 4.83 GB per step (> 126 MB L2); no flush needed",
+            "parallelism": "replicas" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "single"}
+
+
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    from ternative_b200 import TVB_F16, TVB_I8_ROW, CUDABackend
+    from ternative_b200.model import PROJ, SHAPES, Model, SyntheticModel, proj_shape
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    cfg = SHAPES[args.config]
+    synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0)
+    be = CUDABackend()
+    m = Model.load(synth, backend=be)
+    stream = torch.cuda.ExternalStream(be.stream)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed decode (value) ---------------------------------------------
+    be.clear_kv_d()
+    _, tok = be.prefill(prompt, want_logits=False)
+    pos = len(prompt)
+    be.decode_enqueue(tok, pos, args.warmup)
+    be.sync_d()
+    pos += args.warmup
+    st = be.lib  # noqa: F841
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        be.decode_enqueue(tok, pos, args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- e2e through the C ABI with host buffers ---------------------------------
+    be.clear_kv_d()
+    _, tok = be.prefill(prompt, want_logits=False)
+    pos = len(prompt)
+    for _ in range(min(args.warmup, 4)):
+        _, tok = be.decode_step(tok, pos)
+        pos += 1
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, tok = be.decode_step(tok, pos)   # H2D token/pos, D2H logits, synchronous
+        pos += 1
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
+           "h2d_bytes_per_step": 8, "d2h_bytes_per_step": cfg.vocab_size * 4 + 4 * 76}
+
+    # ---- dominant kernel: streaming F16 GEMV, gate shape, rotating layers ---------
+    N, K = proj_shape(cfg, "w_gate")
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    ws = [m.weights[li]["w_gate"] for li in range(cfg.num_layers)]
+    for i in range(3):
+        be.gemv_d2d(y, x, ws[i], K, N)
+    be.sync_d()
+    reps = 3 * cfg.num_layers
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for i in range(reps):
+        be.gemv_d2d(y, x, ws[i % len(ws)], K, N)
+    g1.record(stream)
+    g1.synchronize()
+    gemv_us = g0.elapsed_time(g1) * 1e3 / reps
+    gemv_bytes = N * K * 2 + 4 * K + 4 * N
+    hbm, peak_kind = peaks()
+    achieved = gemv_bytes / (gemv_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "kernel": "stream_gemv_kernel<PLAIN,F16> 6912x2560",
+                "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "peak_kind": peak_kind, "bytes_per_launch": gemv_bytes, "us_per_launch": gemv_us,
+                "traffic": None}
+    step_bytes = sum(2 * proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) \
+        * cfg.num_layers + cfg.vocab_size * cfg.hidden_size * 2
+    step_gbs = step_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---- load-time merge: all 210 projections, F16 and per-row INT8 ---------------
+    merge = {}
+    outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.float16, device="cuda") for n in PROJ}
+            for _ in range(cfg.num_layers)]
+    descs = synth.merge_descs(outs)
+    for _ in range(2):
+        be.merge_batch(descs, TVB_F16)
+    be.sync_d()
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0.record(stream)
+    be.merge_batch(descs, TVB_F16)
+    m1.record(stream)
+    m1.synchronize()
+    ms_f16 = m0.elapsed_time(m1)
+    n_w = sum(proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) * cfg.num_layers
+    lora_b = sum(4 * 16 * (proj_shape(cfg, n)[0] + proj_shape(cfg, n)[1]) for n in PROJ) * cfg.num_layers
+    merge["r16_f16"] = {"ms": ms_f16, "GB/s": (n_w / 4 + lora_b + 2 * n_w) / (ms_f16 * 1e6),
+                        "GFLOP/s": 2 * 16 * n_w / (ms_f16 * 1e6)}
+    del outs
+    outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.int8, device="cuda") for n in PROJ}
+            for _ in range(cfg.num_layers)]
+    scs = [{n: torch.empty(proj_shape(cfg, n)[0], dtype=torch.float32, device="cuda") for n in PROJ}
+           for _ in range(cfg.num_layers)]
+    descs = synth.merge_descs(outs, scs)
+    be.merge_batch(descs, TVB_I8_ROW)
+    be.sync_d()
+    m0.record(stream)
+    be.merge_batch(descs, TVB_I8_ROW)
+    m1.record(stream)
+    m1.synchronize()
+    ms_i8 = m0.elapsed_time(m1)
+    merge["r16_i8row"] = {"ms": ms_i8, "GB/s": (n_w / 4 + lora_b + n_w) / (ms_i8 * 1e6)}
+    del outs, scs
+
+    # ---- CPU baseline: the reference's own decode on this host --------------------
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        try:
+            from oracle.oracle import ModelShape, Reference, ReferenceModel
+            shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                               cfg.num_kv_heads, cfg.intermediate_size, 512)
+            rm = ReferenceModel(Reference(), shape, m.host_weights())
+            sec, n = time_reference_decode(rm, 64, pos0=40, budget_s=args.cpu_seconds)
+            cpu = {"value": 1.0 / sec, "unit": "tok/s", "cores": rm.ref.L.tvref_omp_threads(),
+                   "kind": "reference",
+                   "sample": f"{n} decode tokens (Model::forward, prefill=false) of the same merged "
+                             "2B model, oracle/_ref built from the reference sources"}
+            rm.close()
+        except Exception as e:
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {e!r}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16-weights/f32-compute",
+            "data": "synthetic", "config": config_block(args, cfg),
+            "roofline": roofline,
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_GBps": step_gbs,
+                              "frac": step_gbs / hbm, "peak": hbm, "peak_kind": peak_kind},
+            "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": (5 * cfg.num_layers + 1) * args.steps,
+            "clocks": clk.report(), "merge": merge,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="bitnet-2b")
+    ap.add_argument("--prompt", type=int, default=32)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,250 @@
+/*
+ * tvb200 — B200-native (sm_100a) quantized-weight hot path for ternative.
+ *
+ * Plain C ABI: device pointers, host pointers and sizes only; no C++ or torch
+ * types.  Every call returns a tvb_status and never throws.  A failed call
+ * leaves a message readable with tvb_last_error() (per host thread).
+ *
+ * All device work is asynchronous on the stream passed in (`stream` is a
+ * cudaStream_t; NULL = the legacy default stream), except where a function
+ * says it synchronises.
+ *
+ * Reference interfaces replaced (paths inside the ternative project):
+ *   - CUDABackend (include/ternative/ops.h:47-168, cuda/ops_cuda.cu:597-823):
+ *     every device method has a tvb_* counterpart below, cited one by one.
+ *   - apply_lora (src/model.cpp:205-258) and the INT8 quantizer of
+ *     init_gpu_backend (src/model.cpp:374-410), which have no backend hook in
+ *     the reference: tvb_merge_i2s_lora / tvb_merge_batch / tvb_quantize_int8.
+ *   - Model::forward_gpu (src/model.cpp:1354-1582) and
+ *     Model::forward_prefill (src/model.cpp:1139-1234): tvb_decode_step and
+ *     tvb_prefill run the same layer order as fused, graph-captured kernels.
+ */
+#ifndef TVB200_H
+#define TVB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    TVB_OK = 0,
+    TVB_ERR_INVALID = 1,      /* bad argument (null pointer, size, alignment) */
+    TVB_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+    TVB_ERR_OOM = 3,          /* device or pinned allocation failed */
+    TVB_ERR_UNSUPPORTED = 4,  /* shape/dtype this build does not handle */
+    TVB_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up */
+    TVB_ERR_COMM = 6,         /* tensor-parallel communicator failure */
+    TVB_ERR_STATE = 7         /* call out of order (e.g. step before weights set) */
+} tvb_status;
+
+/* Weight / output element types. */
+typedef enum {
+    TVB_F32 = 0,
+    TVB_F16 = 1,          /* IEEE half; merge output is the reference's truncating cast */
+    TVB_I8_ROW = 2,       /* int8 codes + one F32 scale per output row */
+    TVB_I8_TENSOR = 3     /* int8 codes + one F32 scale per tensor (reference INT8) */
+} tvb_dtype;
+
+int         tvb_version(void);
+const char* tvb_status_string(tvb_status s);
+const char* tvb_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Device memory helpers — CUDABackend::free_vram_bytes / alloc_gpu_mem /   */
+/* upload / release_gpu_mem (ops.h:82-92, ops_cuda.cu:673-692).             */
+/* ------------------------------------------------------------------------ */
+tvb_status tvb_free_vram_bytes(size_t* free_bytes);
+tvb_status tvb_alloc(size_t bytes, void** dptr);
+tvb_status tvb_upload(void* dst, const void* src, size_t bytes);   /* synchronous */
+/* upload_pinned / download_pinned (ops.h:120-121): synchronous copies. */
+tvb_status tvb_download(void* dst_host, const void* src_dev, size_t bytes);
+tvb_status tvb_release(void* dptr);
+
+/* ------------------------------------------------------------------------ */
+/* Part 1: load-time merge (replaces apply_lora, model.cpp:205-258, and the  */
+/* INT8 pass of init_gpu_backend, model.cpp:374-410).                       */
+/*                                                                          */
+/* One projection W of GGUF ne = [K, N] (stored [N][K], out-major):          */
+/*   i2s   : K*N/4 bytes of I2_S codes (K % 128 == 0), the per-tensor scale  */
+/*           passed separately (it trails the codes in GGUF, model.cpp:157)  */
+/*   A     : lora_a, ne = [K, r], stored [r][K], F32                         */
+/*   B     : lora_b, ne = [r, N], stored [N][r], F32                         */
+/*   W'    = scale*map(code) + (B.A)*(alpha/r), summed over r in order with  */
+/*           unfused F32 multiply/add, exactly as matmul_lora (:192-201)     */
+/*   out   : TVB_F32 (merged F32), TVB_F16 (truncating cast, tensor.cpp:33), */
+/*           TVB_I8_ROW (per-row absmax/127 of the F16 values, round half    */
+/*           away from zero, clip +-127; row_scales gets N floats)           */
+/* A == NULL or r == 0 merges nothing (plain unpack + cast).                 */
+/* dst must be 16-byte aligned.                                              */
+/* ------------------------------------------------------------------------ */
+tvb_status tvb_merge_i2s_lora(const uint8_t* i2s, float scale, int K, int N,
+                              const float* A, const float* B, int r, float alpha,
+                              tvb_dtype out, void* dst, float* row_scales, void* stream);
+
+typedef struct {
+    const uint8_t* i2s;
+    float scale;
+    int K, N;
+    const float* A;
+    const float* B;
+    int r;
+    float alpha;
+    void* dst;
+    float* row_scales;   /* TVB_I8_ROW only */
+} tvb_merge_desc;
+
+/* All descriptors in one launch (descs is a HOST array of n entries; the
+ * device addresses inside it are read on the device).  This is the
+ * sharded-by-tensor load-time merge: give each rank its own subset. */
+tvb_status tvb_merge_batch(const tvb_merge_desc* descs, int n, tvb_dtype out, void* stream);
+
+/* tensor.cpp:1006-1050: I2_S codes -> F32 (n % 128 == 0). */
+tvb_status tvb_i2s_unpack(const uint8_t* i2s, int64_t n, float scale, float* out, void* stream);
+
+/* F16 [N][K] -> int8 codes.  per_row != 0: TVB_I8_ROW (scales gets N floats);
+ * per_row == 0: the reference's per-tensor quantizer (model.cpp:381-401,
+ * scales gets 1 float).  Needs no workspace beyond `scales`. */
+tvb_status tvb_quantize_int8(const uint16_t* w_f16, int N, int K, int per_row,
+                             int8_t* q, float* scales, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Part 2 building blocks: the CUDABackend device-pointer API.              */
+/* ------------------------------------------------------------------------ */
+/* gemv_d2d (ops.h:112-113, ops_cuda.cu:734-740): y[N] = W_f16[N][K] . x[K] */
+tvb_status tvb_gemv_f16(float* y, const float* x, const void* W, int K, int N, void* stream);
+/* gemv_d2d_int8 (ops.h:116-117, ops_cuda.cu:741-744): y = scale * W_i8 . x */
+tvb_status tvb_gemv_int8(float* y, const float* x, const void* W, float scale, int K, int N,
+                         void* stream);
+/* Per-row INT8 variant: y[n] = row_scales[n] * (W_i8[n] . x). */
+tvb_status tvb_gemv_int8_rows(float* y, const float* x, const void* W, const float* row_scales,
+                              int K, int N, void* stream);
+/* rms_norm_d (ops.h:107-108, ops_cuda.cu:729-733): out = x / sqrt(mean(x^2)+eps) * w */
+tvb_status tvb_rms_norm(float* out, const float* x, const float* w, float eps, int N,
+                        void* stream);
+/* add_d / mul_d / relu2_d (ops.h:102-104, ops_cuda.cu:714-728) */
+tvb_status tvb_add(float* out, const float* a, const float* b, int N, void* stream);
+tvb_status tvb_mul(float* out, const float* a, const float* b, int N, void* stream);
+tvb_status tvb_relu2(float* out, const float* x, int N, void* stream);
+/* rope_inplace_d (ops.h:130-131, ops_cuda.cu:757-763): NeoX halves, in place. */
+tvb_status tvb_rope_inplace(float* q, float* k, int pos, float theta, int n_heads,
+                            int n_kv_heads, int head_dim, void* stream);
+/* kv_write_d (ops.h:135, ops_cuda.cu:765-774) on explicit layer slices
+ * (k_cache/v_cache point at row 0 of this layer; row stride Hk floats). */
+tvb_status tvb_kv_write(const float* k, const float* v, float* k_cache, float* v_cache, int pos,
+                        int Hk, void* stream);
+/* attention_d (ops.h:141-142, ops_cuda.cu:776-789): one query row against
+ * kv_len cached rows, GQA (kv head = h / (n_heads/n_kv_heads)). */
+tvb_status tvb_attention_decode(const float* q, const float* k_cache, const float* v_cache,
+                                int kv_len, float* out, int n_heads, int n_kv_heads,
+                                int head_dim, float scale, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Context: the state CUDABackend::Impl owns (ops_cuda.cu:309-591):         */
+/* stream, activation buffers, KV cache, pinned staging, workspace, plus    */
+/* the fused decode/prefill step over a registered weight table.            */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    int vocab_size;
+    int hidden_size;
+    int num_layers;
+    int num_heads;
+    int num_kv_heads;
+    int head_dim;
+    int intermediate_size;
+    int max_seq_len;     /* device KV capacity (the reference hard-codes 1024) */
+    float rope_theta;
+    float rms_norm_eps;
+    int max_prefill;     /* largest prefill batch (0 -> 1024) */
+} tvb_model_config;
+
+typedef struct tvb_context tvb_context;
+
+/* init_gpu_activations (ops.h:93, ops_cuda.cu:355-395).  Allocates on the
+ * current device; creates its own non-blocking stream. */
+tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out);
+tvb_status tvb_context_destroy(tvb_context* ctx);
+void*      tvb_context_stream(tvb_context* ctx);
+
+/* d_x()/d_norm()/d_q()/d_k()/d_v()/d_gate()/d_up() and h_qkv()/h_attn()/
+ * h_logit() (ops.h:94-110). */
+typedef struct {
+    float* d_x;
+    float* d_norm;
+    float* d_q;
+    float* d_k;
+    float* d_v;
+    float* d_gate;
+    float* d_up;
+    float* h_qkv;
+    float* h_attn;
+    float* h_logit;
+} tvb_buffers;
+tvb_status tvb_context_buffers(tvb_context* ctx, tvb_buffers* out);
+
+/* clear_kv_d / has_gpu_kv / gpu_kv_max_seq / upload_kv_layer_d /
+ * download_kv_slot_d (ops.h:145-162).  KV layout: [layer][pos][Hk] F32. */
+tvb_status tvb_kv_clear(tvb_context* ctx);
+int        tvb_kv_capacity(tvb_context* ctx);
+tvb_status tvb_kv_layer_ptrs(tvb_context* ctx, int layer, float** k, float** v);
+tvb_status tvb_kv_upload_layer(tvb_context* ctx, int layer, int n_positions, const float* h_k,
+                               const float* h_v);
+tvb_status tvb_kv_download_slot(tvb_context* ctx, int layer, int pos, int n_floats, float* h_dst);
+/* sync_d (ops.h:123). */
+tvb_status tvb_context_sync(tvb_context* ctx);
+
+/* Weight table for the fused step.  Device pointers stay owned by the caller
+ * (Tensor::gpu_ptr is non-owning, tensor.h:39-43). */
+typedef struct {
+    const void* w;          /* weights [N][K] */
+    tvb_dtype dtype;        /* TVB_F16, TVB_I8_ROW or TVB_I8_TENSOR */
+    const float* row_scales;/* TVB_I8_ROW */
+    float tensor_scale;     /* TVB_I8_TENSOR */
+} tvb_weight;
+
+typedef struct {
+    const float* attn_norm;     /* [H]  */
+    tvb_weight wq, wk, wv;      /* [Hq][H], [Hk][H], [Hk][H] */
+    const float* attn_sub_norm; /* [Hq] */
+    tvb_weight wo;              /* [H][Hq] */
+    const float* ffn_norm;      /* [H]  */
+    tvb_weight w_gate, w_up;    /* [I][H] */
+    const float* ffn_sub_norm;  /* [I]  */
+    tvb_weight w_down;          /* [H][I] */
+} tvb_layer_weights;
+
+tvb_status tvb_set_layer(tvb_context* ctx, int layer, const tvb_layer_weights* lw);
+/* tok_embd F16 [V][H] (tied lm_head, model.cpp:1579) and output_norm F32 [H]. */
+tvb_status tvb_set_output(tvb_context* ctx, const void* tok_embd_f16, const float* output_norm);
+
+/* Model::forward_gpu (model.cpp:1354-1582) for one token at position `pos`
+ * (KV rows [0, pos) must be filled): embedding, all layers, final norm and
+ * the lm_head on the device.  logits_host (V floats, may be NULL) and
+ * argmax_host (may be NULL) are filled from pinned staging; this call
+ * synchronises its stream. */
+tvb_status tvb_decode_step(tvb_context* ctx, int token, int pos, float* logits_host,
+                           int* argmax_host);
+
+/* Greedy decode of n_steps tokens entirely on the device: step i feeds the
+ * argmax of step i-1 back as its token.  Starts from `token` at `pos`.
+ * tokens_host receives n_steps argmax ids.  Synchronises. */
+tvb_status tvb_generate_greedy(tvb_context* ctx, int token, int pos, int n_steps,
+                               int* tokens_host);
+
+/* Enqueue n_steps chained greedy steps (as tvb_generate_greedy) on the
+ * context stream and return without synchronising; argmax ids accumulate in
+ * device memory.  For timing and for overlapping host work. */
+tvb_status tvb_decode_enqueue(tvb_context* ctx, int token, int pos, int n_steps);
+
+/* Model::forward_prefill (model.cpp:1139-1234) over S tokens starting at
+ * position 0: fills KV rows [0, S) and returns the logits of the last row
+ * (and its argmax).  Synchronises. */
+tvb_status tvb_prefill(tvb_context* ctx, const int* tokens_host, int S, float* last_logits_host,
+                       int* argmax_host);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TVB200_H */

@@ -1,0 +1,640 @@
+// Context (the state CUDABackend::Impl owns, cuda/ops_cuda.cu:309-591) and the
+// fused, graph-captured decode step replacing Model::forward_gpu
+// (src/model.cpp:1354-1582).
+//
+// One decode step = per layer [QKV+RoPE+KV append] -> [attention] ->
+// [sub-norm + o_proj + residual] -> [ffn_norm + gate/up + relu^2*up] ->
+// [sub-norm + down + residual], then [output_norm + lm_head + argmax]:
+// 5 kernels per layer + 1, launched with programmatic dependent launch and
+// captured once into a CUDA graph.  Position and token live in device memory
+// (StepState), so the same graph serves every position and greedy decode can
+// chain steps without the host.
+#include "attention.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#define TVB_TRY(x)                   \
+    do {                             \
+        tvb_status _s = (x);         \
+        if (_s != TVB_OK) return _s; \
+    } while (0)
+
+namespace tvb {
+
+__device__ unsigned g_standalone_status;
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, bool pdl, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+constexpr int kSlotBudget = 96 * 1024;
+constexpr int kMaxDynSmem = 227 * 1024;
+
+template <int MODE, int WT, int R>
+static tvb_status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
+    const int esz = (WT == WT_F16) ? 2 : 1;
+    const int stage_bytes = R * a.K * esz;
+    int stages = std::max(2, std::min(16, kSlotBudget / stage_bytes));
+    GemvSmem L = gemv_smem_layout(R, a.K, stages, stage_bytes);
+    while (L.total > kMaxDynSmem && stages > 2) L = gemv_smem_layout(R, a.K, --stages, stage_bytes);
+    if (L.total > kMaxDynSmem)
+        return set_error(TVB_ERR_UNSUPPORTED, "gemv: K=%d too large for shared-memory staging", a.K);
+    const int groups = gemv_groups<MODE>(a, R);
+    if (groups <= 0) return TVB_OK;
+    const int grid = std::min(groups, num_sms());
+    auto kern = stream_gemv_kernel<MODE, WT, R>;
+    TVB_CUDA(launch_ex(kern, dim3(grid), dim3(kGemvThreads), (size_t)L.total, st, pdl, a, stages));
+    return TVB_OK;
+}
+
+// Opt every GEMV instantiation into the full dynamic shared memory once, before
+// any launch (and outside stream capture).
+template <int MODE, int WT, int R>
+static cudaError_t allow_smem() {
+    return cudaFuncSetAttribute(stream_gemv_kernel<MODE, WT, R>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+}
+
+tvb_status prepare_kernels() {
+    static int done = 0;
+    if (done) return TVB_OK;
+    cudaError_t e = cudaSuccess;
+    cudaError_t r[] = {
+        allow_smem<GM_PLAIN, WT_F16, 4>(), allow_smem<GM_PLAIN, WT_I8, 4>(),
+        allow_smem<GM_QKV, WT_F16, 2>(),   allow_smem<GM_QKV, WT_I8, 2>(),
+        allow_smem<GM_RESID, WT_F16, 2>(), allow_smem<GM_RESID, WT_I8, 2>(),
+        allow_smem<GM_RESID, WT_F16, 1>(), allow_smem<GM_RESID, WT_I8, 1>(),
+        allow_smem<GM_GATEUP, WT_F16, 2>(), allow_smem<GM_GATEUP, WT_I8, 2>(),
+        allow_smem<GM_LMHEAD, WT_F16, 8>(),
+    };
+    for (cudaError_t x : r)
+        if (x != cudaSuccess) e = x;
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
+    num_sms();
+    done = 1;
+    return TVB_OK;
+}
+
+// Weight-type dispatch for the fused modes.
+template <int MODE, int R>
+static tvb_status launch_gemv_wt(int wt, const GemvArgs& a, cudaStream_t st, bool pdl) {
+    return wt == WT_F16 ? launch_gemv<MODE, WT_F16, R>(a, st, pdl)
+                        : launch_gemv<MODE, WT_I8, R>(a, st, pdl);
+}
+
+static tvb_status launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
+    TVB_CUDA(launch_ex(attn_decode_kernel, dim3(a.nkv, a.nsplit), dim3(kAttnThreads), 0, st, pdl, a));
+    return TVB_OK;
+}
+
+static bool wt_of(tvb_dtype d, int* wt) {
+    if (d == TVB_F16) { *wt = WT_F16; return true; }
+    if (d == TVB_I8_ROW || d == TVB_I8_TENSOR) { *wt = WT_I8; return true; }
+    return false;
+}
+
+static void fill_weight(GemvArgs& a, int slot, const tvb_weight& w) {
+    a.w[slot] = w.w;
+    a.row_scale[slot] = (w.dtype == TVB_I8_ROW) ? w.row_scales : nullptr;
+    a.tscale[slot] = (w.dtype == TVB_I8_TENSOR) ? w.tensor_scale : 1.0f;
+}
+
+}  // namespace tvb
+
+using namespace tvb;
+
+struct tvb_context {
+    tvb_model_config cfg;
+    int H, Hq, Hk, I, V, L;
+    int device;
+    cudaStream_t stream = nullptr;
+    // reference-API activation buffers (ops.h:94-110)
+    float *d_x = nullptr, *d_norm = nullptr, *d_q = nullptr, *d_k = nullptr, *d_v = nullptr,
+          *d_gate = nullptr, *d_up = nullptr;
+    float *h_qkv = nullptr, *h_attn = nullptr, *h_logit = nullptr;
+    // fused-step buffers
+    float *e_x = nullptr, *e_q = nullptr, *e_attn = nullptr, *e_h = nullptr, *e_logits = nullptr;
+    float* attn_part = nullptr;
+    int nsplit = 16;
+    float *kcache = nullptr, *vcache = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    StepState* st = nullptr;
+    int* hist = nullptr;
+    // pinned staging
+    StepState* h_st = nullptr;
+    int* h_io = nullptr;       // [max_seq][2] (pos, token) staging for prefill steps
+    int* h_hist = nullptr;
+    // weights
+    std::vector<tvb_layer_weights> layers;
+    std::vector<bool> layer_set;
+    const void* tok_embd = nullptr;
+    const float* output_norm = nullptr;
+    // graphs
+    cudaGraphExec_t g_step = nullptr;    // layers + lm_head
+    cudaGraphExec_t g_layers = nullptr;  // layers only (prefill rows before the last)
+    bool dirty = true;
+};
+
+namespace {
+
+tvb_status alloc_dev(void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc");
+    return TVB_OK;
+}
+
+tvb_status record_layers(tvb_context* c, bool with_head) {
+    cudaStream_t st = c->stream;
+    const float scale = 1.0f / std::sqrt((float)c->cfg.head_dim);
+    for (int l = 0; l < c->L; ++l) {
+        const tvb_layer_weights& lw = c->layers[l];
+        int wt;
+        if (!wt_of(lw.wq.dtype, &wt)) return set_error(TVB_ERR_UNSUPPORTED, "layer %d: dtype", l);
+        float* kl = c->kcache + (size_t)l * c->cfg.max_seq_len * c->Hk;
+        float* vl = c->vcache + (size_t)l * c->cfg.max_seq_len * c->Hk;
+        // (a)-(c): attn_norm, q/k/v, RoPE, KV append
+        {
+            GemvArgs a = {};
+            fill_weight(a, 0, lw.wq);
+            fill_weight(a, 1, lw.wk);
+            fill_weight(a, 2, lw.wv);
+            a.K = c->H;
+            a.x = c->e_x;
+            a.embd = static_cast<const uint16_t*>(c->tok_embd);
+            a.x_out = c->e_x;
+            a.gather_token = (l == 0);
+            a.norm_w = lw.attn_norm;
+            a.eps = c->cfg.rms_norm_eps;
+            a.nh = c->cfg.num_heads;
+            a.nkv = c->cfg.num_kv_heads;
+            a.hd = c->cfg.head_dim;
+            a.q_out = c->e_q;
+            a.kcache = kl;
+            a.vcache = vl;
+            a.rope_cos = c->rope_cos;
+            a.rope_sin = c->rope_sin;
+            a.st = c->st;
+            a.status = &c->st->status;
+            TVB_TRY((launch_gemv_wt<GM_QKV, 2>(wt, a, st, l > 0)));
+        }
+        // (d): attention over kv_len = pos + 1
+        {
+            AttnArgs a = {};
+            a.q = c->e_q;
+            a.kcache = kl;
+            a.vcache = vl;
+            a.out = c->e_attn;
+            a.part = c->attn_part;
+            a.nh = c->cfg.num_heads;
+            a.nkv = c->cfg.num_kv_heads;
+            a.hd = c->cfg.head_dim;
+            a.nsplit = c->nsplit;
+            a.scale = scale;
+            a.kv_len = -1;
+            a.st = c->st;
+            a.status = &c->st->status;
+            TVB_TRY(launch_attn(a, st, true));
+        }
+        // (e)-(f): attn_sub_norm, wo, residual
+        {
+            GemvArgs a = {};
+            fill_weight(a, 0, lw.wo);
+            a.N = c->H;
+            a.K = c->Hq;
+            a.x = c->e_attn;
+            a.norm_w = lw.attn_sub_norm;
+            a.eps = c->cfg.rms_norm_eps;
+            a.y = c->e_x;
+            a.st = c->st;
+            a.status = &c->st->status;
+            TVB_TRY((launch_gemv_wt<GM_RESID, 2>(wt, a, st, true)));
+        }
+        // (g)-(h): ffn_norm, gate/up, relu^2 * up
+        {
+            GemvArgs a = {};
+            fill_weight(a, 0, lw.w_gate);
+            fill_weight(a, 1, lw.w_up);
+            a.N = c->I;
+            a.K = c->H;
+            a.x = c->e_x;
+            a.norm_w = lw.ffn_norm;
+            a.eps = c->cfg.rms_norm_eps;
+            a.y = c->e_h;
+            a.st = c->st;
+            a.status = &c->st->status;
+            TVB_TRY((launch_gemv_wt<GM_GATEUP, 2>(wt, a, st, true)));
+        }
+        // (i): ffn_sub_norm, down, residual
+        {
+            GemvArgs a = {};
+            fill_weight(a, 0, lw.w_down);
+            a.N = c->H;
+            a.K = c->I;
+            a.x = c->e_h;
+            a.norm_w = lw.ffn_sub_norm;
+            a.eps = c->cfg.rms_norm_eps;
+            a.y = c->e_x;
+            a.st = c->st;
+            a.status = &c->st->status;
+            TVB_TRY((launch_gemv_wt<GM_RESID, 1>(wt, a, st, true)));
+        }
+    }
+    if (with_head) {
+        GemvArgs a = {};
+        a.w[0] = c->tok_embd;
+        a.tscale[0] = 1.0f;
+        a.N = c->V;
+        a.K = c->H;
+        a.x = c->e_x;
+        a.norm_w = c->output_norm;
+        a.eps = c->cfg.rms_norm_eps;
+        a.y = c->e_logits;
+        a.st = c->st;
+        a.status = &c->st->status;
+        TVB_TRY((launch_gemv<GM_LMHEAD, WT_F16, 8>(a, st, true)));
+    }
+    return TVB_OK;
+}
+
+tvb_status capture(tvb_context* c, bool with_head, cudaGraphExec_t* out) {
+    if (*out) {
+        cudaGraphExecDestroy(*out);
+        *out = nullptr;
+    }
+    TVB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    tvb_status s = record_layers(c, with_head);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (s != TVB_OK) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+    }
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGraphInstantiate");
+    return TVB_OK;
+}
+
+tvb_status ensure_graphs(tvb_context* c) {
+    if (!c->dirty) return TVB_OK;
+    for (int l = 0; l < c->L; ++l)
+        if (!c->layer_set[l]) return set_error(TVB_ERR_STATE, "layer %d weights not set", l);
+    if (!c->tok_embd || !c->output_norm) return set_error(TVB_ERR_STATE, "output weights not set");
+    TVB_TRY(capture(c, true, &c->g_step));
+    TVB_TRY(capture(c, false, &c->g_layers));
+    c->dirty = false;
+    return TVB_OK;
+}
+
+tvb_status check_status(tvb_context* c) {
+    if (c->h_st->status & kStatusTimeout)
+        return set_error(TVB_ERR_TIMEOUT, "a device-side wait exceeded its limit");
+    if (c->h_st->status) return set_error(TVB_ERR_CUDA, "device status 0x%x", c->h_st->status);
+    return TVB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
+    TVB_REQUIRE(cfg && out, "context_create: null argument");
+    *out = nullptr;
+    const tvb_model_config& m = *cfg;
+    TVB_REQUIRE(m.hidden_size > 0 && m.num_layers > 0 && m.num_heads > 0 && m.num_kv_heads > 0 &&
+                    m.intermediate_size > 0 && m.vocab_size > 0 && m.max_seq_len > 0,
+                "context_create: non-positive dimension");
+    TVB_REQUIRE(m.head_dim == 128, "context_create: head_dim %d (only 128 is built)", m.head_dim);
+    TVB_REQUIRE(m.num_heads % m.num_kv_heads == 0, "context_create: heads %% kv_heads != 0");
+    TVB_REQUIRE(m.num_kv_heads <= kMaxKvHeads, "context_create: too many kv heads");
+    TVB_REQUIRE(m.hidden_size % 16 == 0 && m.intermediate_size % 16 == 0,
+                "context_create: hidden/intermediate must be multiples of 16");
+    {
+        tvb_status ps = prepare_kernels();
+        if (ps != TVB_OK) return ps;
+    }
+    tvb_context* c = new (std::nothrow) tvb_context();
+    if (!c) return set_error(TVB_ERR_OOM, "context_create: host allocation");
+    c->cfg = m;
+    if (c->cfg.max_prefill <= 0) c->cfg.max_prefill = 1024;
+    c->H = m.hidden_size;
+    c->Hq = m.num_heads * m.head_dim;
+    c->Hk = m.num_kv_heads * m.head_dim;
+    c->I = m.intermediate_size;
+    c->V = m.vocab_size;
+    c->L = m.num_layers;
+    c->layers.assign(c->L, tvb_layer_weights{});
+    c->layer_set.assign(c->L, false);
+    cudaGetDevice(&c->device);
+    auto fail = [&](tvb_status s) {
+        tvb_context_destroy(c);
+        return s;
+    };
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(cuda_error(cudaGetLastError(), "cudaStreamCreate"));
+    const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, V = c->V;
+    const size_t kv = (size_t)c->L * m.max_seq_len * Hk;
+    struct { void** p; size_t b; } allocs[] = {
+        {(void**)&c->d_x, H * 4ull}, {(void**)&c->d_norm, std::max(H, I) * 4ull},
+        {(void**)&c->d_q, Hq * 4ull}, {(void**)&c->d_k, Hk * 4ull}, {(void**)&c->d_v, Hk * 4ull},
+        {(void**)&c->d_gate, I * 4ull}, {(void**)&c->d_up, I * 4ull},
+        {(void**)&c->e_x, H * 4ull}, {(void**)&c->e_q, Hq * 4ull}, {(void**)&c->e_attn, Hq * 4ull},
+        {(void**)&c->e_h, I * 4ull}, {(void**)&c->e_logits, V * 4ull},
+        {(void**)&c->attn_part, (size_t)m.num_heads * c->nsplit * (m.head_dim + 4) * 4ull},
+        {(void**)&c->kcache, kv * 4}, {(void**)&c->vcache, kv * 4},
+        {(void**)&c->rope_cos, (size_t)m.max_seq_len * (m.head_dim / 2) * 4},
+        {(void**)&c->rope_sin, (size_t)m.max_seq_len * (m.head_dim / 2) * 4},
+        {(void**)&c->st, sizeof(StepState)}, {(void**)&c->hist, (size_t)m.max_seq_len * 4},
+    };
+    for (auto& a : allocs) {
+        tvb_status s = alloc_dev(a.p, a.b);
+        if (s != TVB_OK) return fail(s);
+    }
+    struct { void** p; size_t b; } pins[] = {
+        {(void**)&c->h_qkv, (Hq + 2ull * Hk) * 4}, {(void**)&c->h_attn, std::max(H, Hq) * 4ull},
+        {(void**)&c->h_logit, V * 4ull}, {(void**)&c->h_st, sizeof(StepState)},
+        {(void**)&c->h_io, (size_t)m.max_seq_len * 8}, {(void**)&c->h_hist, (size_t)m.max_seq_len * 4},
+    };
+    for (auto& a : pins) {
+        cudaError_t e = cudaMallocHost(a.p, a.b);
+        if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
+    }
+    // RoPE factors with the CPU formulas (tensor.cpp:830-838), once per context.
+    {
+        const int half = m.head_dim / 2;
+        std::vector<float> cs((size_t)m.max_seq_len * half), sn((size_t)m.max_seq_len * half);
+        for (int p = 0; p < m.max_seq_len; ++p)
+            for (int ic = 0; ic < half; ++ic) {
+                float freq = 1.0f / std::pow(m.rope_theta, (float)(2 * ic) / (float)m.head_dim);
+                cs[(size_t)p * half + ic] = std::cos(p * freq);
+                sn[(size_t)p * half + ic] = std::sin(p * freq);
+            }
+        if (cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(cuda_error(cudaGetLastError(), "rope table upload"));
+    }
+    if (cudaMemset(c->st, 0, sizeof(StepState)) != cudaSuccess ||
+        cudaMemset(c->kcache, 0, kv * 4) != cudaSuccess || cudaMemset(c->vcache, 0, kv * 4) != cudaSuccess)
+        return fail(cuda_error(cudaGetLastError(), "context memset"));
+    std::memset(c->h_st, 0, sizeof(StepState));
+    *out = c;
+    return TVB_OK;
+}
+
+tvb_status tvb_context_destroy(tvb_context* c) {
+    if (!c) return TVB_OK;
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->g_step) cudaGraphExecDestroy(c->g_step);
+    if (c->g_layers) cudaGraphExecDestroy(c->g_layers);
+    void* dev[] = {c->d_x, c->d_norm, c->d_q, c->d_k, c->d_v, c->d_gate, c->d_up, c->e_x, c->e_q,
+                   c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
+                   c->rope_cos, c->rope_sin, c->st, c->hist};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
+    for (void* p : pin)
+        if (p) cudaFreeHost(p);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return TVB_OK;
+}
+
+void* tvb_context_stream(tvb_context* c) { return c ? (void*)c->stream : nullptr; }
+
+tvb_status tvb_context_buffers(tvb_context* c, tvb_buffers* o) {
+    TVB_REQUIRE(c && o, "context_buffers: null argument");
+    *o = tvb_buffers{c->d_x, c->d_norm, c->d_q, c->d_k, c->d_v, c->d_gate, c->d_up,
+                     c->h_qkv, c->h_attn, c->h_logit};
+    return TVB_OK;
+}
+
+tvb_status tvb_kv_clear(tvb_context* c) {
+    TVB_REQUIRE(c, "kv_clear: null context");
+    const size_t b = (size_t)c->L * c->cfg.max_seq_len * c->Hk * 4;
+    TVB_CUDA(cudaMemsetAsync(c->kcache, 0, b, c->stream));
+    TVB_CUDA(cudaMemsetAsync(c->vcache, 0, b, c->stream));
+    return TVB_OK;
+}
+
+int tvb_kv_capacity(tvb_context* c) { return c ? c->cfg.max_seq_len : 0; }
+
+tvb_status tvb_kv_layer_ptrs(tvb_context* c, int layer, float** k, float** v) {
+    TVB_REQUIRE(c && k && v, "kv_layer_ptrs: null argument");
+    TVB_REQUIRE(layer >= 0 && layer < c->L, "kv_layer_ptrs: layer %d", layer);
+    *k = c->kcache + (size_t)layer * c->cfg.max_seq_len * c->Hk;
+    *v = c->vcache + (size_t)layer * c->cfg.max_seq_len * c->Hk;
+    return TVB_OK;
+}
+
+tvb_status tvb_kv_upload_layer(tvb_context* c, int layer, int n, const float* hk, const float* hv) {
+    TVB_REQUIRE(c && hk && hv, "kv_upload_layer: null argument");
+    TVB_REQUIRE(layer >= 0 && layer < c->L, "kv_upload_layer: layer %d", layer);
+    if (n <= 0) return TVB_OK;
+    n = std::min(n, c->cfg.max_seq_len);
+    float *k, *v;
+    tvb_kv_layer_ptrs(c, layer, &k, &v);
+    TVB_CUDA(cudaMemcpyAsync(k, hk, (size_t)n * c->Hk * 4, cudaMemcpyHostToDevice, c->stream));
+    TVB_CUDA(cudaMemcpyAsync(v, hv, (size_t)n * c->Hk * 4, cudaMemcpyHostToDevice, c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    return TVB_OK;
+}
+
+tvb_status tvb_kv_download_slot(tvb_context* c, int layer, int pos, int n_floats, float* dst) {
+    TVB_REQUIRE(c && dst, "kv_download_slot: null argument");
+    TVB_REQUIRE(layer >= 0 && layer < c->L && pos >= 0 && pos < c->cfg.max_seq_len,
+                "kv_download_slot: layer %d pos %d", layer, pos);
+    TVB_REQUIRE(n_floats >= 0 && n_floats <= c->Hk, "kv_download_slot: n_floats %d", n_floats);
+    float *k, *v;
+    tvb_kv_layer_ptrs(c, layer, &k, &v);
+    TVB_CUDA(cudaMemcpyAsync(dst, k + (size_t)pos * c->Hk, (size_t)n_floats * 4, cudaMemcpyDeviceToHost,
+                             c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    return TVB_OK;
+}
+
+tvb_status tvb_context_sync(tvb_context* c) {
+    TVB_REQUIRE(c, "context_sync: null context");
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    return TVB_OK;
+}
+
+tvb_status tvb_set_layer(tvb_context* c, int layer, const tvb_layer_weights* lw) {
+    TVB_REQUIRE(c && lw, "set_layer: null argument");
+    TVB_REQUIRE(layer >= 0 && layer < c->L, "set_layer: layer %d of %d", layer, c->L);
+    const tvb_weight* ws[] = {&lw->wq, &lw->wk, &lw->wv, &lw->wo, &lw->w_gate, &lw->w_up, &lw->w_down};
+    int wt0 = -1;
+    for (const tvb_weight* w : ws) {
+        int wt;
+        TVB_REQUIRE(w->w, "set_layer %d: null weight", layer);
+        TVB_REQUIRE(wt_of(w->dtype, &wt), "set_layer %d: dtype %d not a weight type", layer, (int)w->dtype);
+        TVB_REQUIRE(w->dtype != TVB_I8_ROW || w->row_scales, "set_layer %d: TVB_I8_ROW needs row_scales", layer);
+        TVB_REQUIRE((reinterpret_cast<uintptr_t>(w->w) & 15) == 0, "set_layer %d: weights must be 16-byte aligned", layer);
+        if (wt0 < 0) wt0 = wt;
+        TVB_REQUIRE(wt == wt0, "set_layer %d: mixed F16/INT8 projections in one layer", layer);
+    }
+    TVB_REQUIRE(lw->attn_norm && lw->ffn_norm, "set_layer %d: missing norm weights", layer);
+    c->layers[layer] = *lw;
+    c->layer_set[layer] = true;
+    c->dirty = true;
+    return TVB_OK;
+}
+
+tvb_status tvb_set_output(tvb_context* c, const void* tok_embd, const float* output_norm) {
+    TVB_REQUIRE(c && tok_embd && output_norm, "set_output: null argument");
+    TVB_REQUIRE((reinterpret_cast<uintptr_t>(tok_embd) & 15) == 0, "set_output: tok_embd must be 16-byte aligned");
+    c->tok_embd = tok_embd;
+    c->output_norm = output_norm;
+    c->dirty = true;
+    return TVB_OK;
+}
+
+tvb_status tvb_decode_step(tvb_context* c, int token, int pos, float* logits_host, int* argmax_host) {
+    TVB_REQUIRE(c, "decode_step: null context");
+    TVB_REQUIRE(token >= 0 && token < c->V, "decode_step: token %d outside vocab %d", token, c->V);
+    TVB_REQUIRE(pos >= 0 && pos < c->cfg.max_seq_len, "decode_step: pos %d outside KV capacity %d", pos,
+                c->cfg.max_seq_len);
+    TVB_TRY(ensure_graphs(c));
+    c->h_io[0] = pos;
+    c->h_io[1] = token;
+    TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io, 8, cudaMemcpyHostToDevice, c->stream));
+    TVB_CUDA(cudaGraphLaunch(c->g_step, c->stream));
+    TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    if (logits_host)
+        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_TRY(check_status(c));
+    if (logits_host) std::memcpy(logits_host, c->h_logit, (size_t)c->V * 4);
+    if (argmax_host) *argmax_host = c->h_st->next_token;
+    return TVB_OK;
+}
+
+tvb_status tvb_generate_greedy(tvb_context* c, int token, int pos, int n_steps, int* tokens_host) {
+    TVB_REQUIRE(c && tokens_host, "generate_greedy: null argument");
+    TVB_REQUIRE(token >= 0 && token < c->V, "generate_greedy: token %d", token);
+    TVB_REQUIRE(pos >= 0 && n_steps >= 0 && pos + n_steps <= c->cfg.max_seq_len,
+                "generate_greedy: positions [%d, %d) exceed KV capacity %d", pos, pos + n_steps,
+                c->cfg.max_seq_len);
+    if (!n_steps) return TVB_OK;
+    TVB_TRY(ensure_graphs(c));
+    c->h_io[0] = pos;
+    c->h_io[1] = token;
+    TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io, 8, cudaMemcpyHostToDevice, c->stream));
+    for (int i = 0; i < n_steps; ++i) {
+        TVB_CUDA(cudaGraphLaunch(c->g_step, c->stream));
+        TVB_CUDA(cudaMemcpyAsync(c->hist + pos + i, &c->st->next_token, 4, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    TVB_CUDA(cudaMemcpyAsync(c->h_hist, c->hist + pos, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_TRY(check_status(c));
+    std::memcpy(tokens_host, c->h_hist, (size_t)n_steps * 4);
+    return TVB_OK;
+}
+
+tvb_status tvb_decode_enqueue(tvb_context* c, int token, int pos, int n_steps) {
+    TVB_REQUIRE(c, "decode_enqueue: null context");
+    TVB_REQUIRE(token >= 0 && token < c->V, "decode_enqueue: token %d", token);
+    TVB_REQUIRE(pos >= 0 && n_steps >= 0 && pos + n_steps <= c->cfg.max_seq_len,
+                "decode_enqueue: positions [%d, %d) exceed KV capacity %d", pos, pos + n_steps,
+                c->cfg.max_seq_len);
+    TVB_TRY(ensure_graphs(c));
+    c->h_io[0] = pos;
+    c->h_io[1] = token;
+    TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io, 8, cudaMemcpyHostToDevice, c->stream));
+    for (int i = 0; i < n_steps; ++i) TVB_CUDA(cudaGraphLaunch(c->g_step, c->stream));
+    return TVB_OK;
+}
+
+tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_logits, int* argmax_host) {
+    TVB_REQUIRE(c && tokens, "prefill: null argument");
+    TVB_REQUIRE(S > 0 && S <= c->cfg.max_seq_len, "prefill: S=%d outside (0, %d]", S, c->cfg.max_seq_len);
+    for (int i = 0; i < S; ++i)
+        TVB_REQUIRE(tokens[i] >= 0 && tokens[i] < c->V, "prefill: token[%d]=%d outside vocab", i, tokens[i]);
+    TVB_TRY(ensure_graphs(c));
+    // Row-at-a-time causal prefill: row s attends to KV rows [0, s], the same
+    // function as the batched forward_prefill (model.cpp:1084 kv_len = s + 1).
+    for (int s = 0; s < S; ++s) {
+        c->h_io[2 * s] = s;
+        c->h_io[2 * s + 1] = tokens[s];
+        TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io + 2 * s, 8, cudaMemcpyHostToDevice, c->stream));
+        TVB_CUDA(cudaGraphLaunch(s + 1 < S ? c->g_layers : c->g_step, c->stream));
+    }
+    TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    if (last_logits)
+        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_TRY(check_status(c));
+    if (last_logits) std::memcpy(last_logits, c->h_logit, (size_t)c->V * 4);
+    if (argmax_host) *argmax_host = c->h_st->next_token;
+    return TVB_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Standalone device-pointer ops (the CUDABackend per-op API).
+// ---------------------------------------------------------------------------
+namespace tvb {
+
+tvb_status standalone_gemv(float* y, const float* x, const void* W, int wt, const float* row_scales,
+                           float tscale, int K, int N, cudaStream_t st) {
+    TVB_REQUIRE(y && x && W, "gemv: null pointer");
+    TVB_REQUIRE(K > 0 && N > 0, "gemv: bad shape K=%d N=%d", K, N);
+    TVB_REQUIRE(wt == WT_F16 ? K % 8 == 0 : K % 16 == 0, "gemv: K=%d must be a multiple of %d", K,
+                wt == WT_F16 ? 8 : 16);
+    TVB_REQUIRE((reinterpret_cast<uintptr_t>(W) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+                "gemv: W and x must be 16-byte aligned");
+    TVB_TRY(prepare_kernels());
+    unsigned* status = nullptr;
+    TVB_CUDA(cudaGetSymbolAddress((void**)&status, g_standalone_status));
+    GemvArgs a = {};
+    a.w[0] = W;
+    a.row_scale[0] = row_scales;
+    a.tscale[0] = tscale;
+    a.N = N;
+    a.K = K;
+    a.x = x;
+    a.y = y;
+    a.status = status;
+    return wt == WT_F16 ? launch_gemv<GM_PLAIN, WT_F16, 4>(a, st, false)
+                        : launch_gemv<GM_PLAIN, WT_I8, 4>(a, st, false);
+}
+
+tvb_status standalone_attention(const float* q, const float* kc, const float* vc, int kv_len, float* out,
+                                int nh, int nkv, int hd, float scale, cudaStream_t st) {
+    TVB_REQUIRE(q && kc && vc && out, "attention: null pointer");
+    TVB_REQUIRE(hd == 128, "attention: head_dim %d (only 128 is built)", hd);
+    TVB_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0, "attention: heads %d / kv heads %d", nh, nkv);
+    TVB_REQUIRE(kv_len > 0, "attention: kv_len %d", kv_len);
+    AttnArgs a = {};
+    a.q = q;
+    a.kcache = kc;
+    a.vcache = vc;
+    a.out = out;
+    a.nh = nh;
+    a.nkv = nkv;
+    a.hd = hd;
+    a.nsplit = 1;
+    a.scale = scale;
+    a.kv_len = kv_len;
+    return launch_attn(a, st, false);
+}
+
+}  // namespace tvb
