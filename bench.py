@@ -201,7 +201,30 @@ def run_ours(args, world, rank, local):
     cfg = SHAPES[args.config]
     synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0)
     be = CUDABackend()
+    if args.only == "merge":
+        # profiling: one F16 merge launch over layer 0's 7 projections
+        outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.float16, device="cuda")
+                 for n in PROJ}]
+        for _ in range(args.warmup + args.steps):
+            be.merge_batch(synth.merge_descs(outs, layers=[0]), TVB_F16, stream=0)
+        torch.cuda.synchronize()
+        return
     m = Model.load(synth, backend=be)
+    if args.only == "gemv":
+        # profiling: standalone streaming GEMV on the gate shape, rotating layers
+        N, K = proj_shape(cfg, "w_gate")
+        x = torch.randn(K, device="cuda")
+        y = torch.empty(N, device="cuda")
+        for i in range(args.warmup + args.steps):
+            be.gemv_d2d(y, x, m.weights[i % cfg.num_layers]["w_gate"], K, N)
+        be.sync_d()
+        return
+    if args.only == "decode":
+        # profiling: W + K chained decode steps from position 32 (KV rows zero), nothing else
+        be.clear_kv_d()
+        be.decode_enqueue(1, 32, args.warmup + args.steps)
+        be.sync_d()
+        return
     stream = torch.cuda.ExternalStream(be.stream)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
@@ -367,8 +390,10 @@ def main():
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["decode", "gemv", "merge"], default=None,
+                    help="profiling: run only W+K launches of one part, print nothing")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and args.only is None:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_setup()
     if args.impl == "reference":

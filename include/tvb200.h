@@ -141,6 +141,20 @@ tvb_status tvb_attention_decode(const float* q, const float* k_cache, const floa
                                 int kv_len, float* out, int n_heads, int n_kv_heads,
                                 int head_dim, float scale, void* stream);
 
+/* Weight descriptor (device pointers stay owned by the caller; Tensor::gpu_ptr
+ * is non-owning, tensor.h:39-43). */
+typedef struct {
+    const void* w;          /* weights [N][K] */
+    tvb_dtype dtype;        /* TVB_F16, TVB_I8_ROW or TVB_I8_TENSOR */
+    const float* row_scales;/* TVB_I8_ROW */
+    float tensor_scale;     /* TVB_I8_TENSOR */
+} tvb_weight;
+
+/* CUDABackend::matmul / Impl::gemm (ops_cuda.cu:440-491, 600-631) on device
+ * buffers: y[M][N] = x[M][K] . W[N][K]^T with F32 activations. */
+tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* w, int N,
+                      void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Context: the state CUDABackend::Impl owns (ops_cuda.cu:309-591):         */
 /* stream, activation buffers, KV cache, pinned staging, workspace, plus    */
@@ -195,15 +209,7 @@ tvb_status tvb_kv_download_slot(tvb_context* ctx, int layer, int pos, int n_floa
 /* sync_d (ops.h:123). */
 tvb_status tvb_context_sync(tvb_context* ctx);
 
-/* Weight table for the fused step.  Device pointers stay owned by the caller
- * (Tensor::gpu_ptr is non-owning, tensor.h:39-43). */
-typedef struct {
-    const void* w;          /* weights [N][K] */
-    tvb_dtype dtype;        /* TVB_F16, TVB_I8_ROW or TVB_I8_TENSOR */
-    const float* row_scales;/* TVB_I8_ROW */
-    float tensor_scale;     /* TVB_I8_TENSOR */
-} tvb_weight;
-
+/* Weight table for the fused step. */
 typedef struct {
     const float* attn_norm;     /* [H]  */
     tvb_weight wq, wk, wv;      /* [Hq][H], [Hk][H], [Hk][H] */

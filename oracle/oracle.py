@@ -21,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 RESTATED_SO = os.path.join(HERE, "libtvoracle.so")
 REFERENCE_SO = os.path.join(HERE, "_ref", "libtvref.so")
+DROPIN_SO = os.path.join(HERE, "_ref", "libtvref_dropin.so")
 REFERENCE_SRC = "/root/reference"
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -36,7 +37,7 @@ def build(reference: bool = True) -> None:
     reference harness) with oracle/Makefile."""
     targets = ["libtvoracle.so"]
     if reference and os.path.isdir(REFERENCE_SRC):
-        targets.append("ref")
+        targets += ["ref", "dropin"]
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
 
@@ -196,6 +197,11 @@ class Reference:
         L.tvref_time_decode.restype = C.c_double
         L.tvref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         self.L = L
+
+        if hasattr(L, "tvref_init_gpu"):   # drop-in build only
+            L.tvref_init_gpu.argtypes = [C.c_void_p]
+            L.tvref_init_gpu.restype = C.c_int
+            L.tvref_sync_kv_to_gpu.argtypes = [C.c_void_p, C.c_int]
 
     def f32_to_f16(self, x):
         x = _c(x, np.float32)
@@ -360,6 +366,14 @@ class ReferenceModel:
         v = np.empty(n * row, np.float32)
         self.ref.L.tvref_kv_read(self.h, layer, n, k, v)
         return k.reshape(n, row), v.reshape(n, row)
+
+    def init_gpu(self) -> int:
+        """Drop-in build: the reference's init_gpu_backend on the tvb200 shim."""
+        return self.ref.L.tvref_init_gpu(self.h)
+
+    def sync_kv_to_gpu(self, n):
+        self.ref.L.tvref_kv_set_seq_len(self.h, n)
+        self.ref.L.tvref_sync_kv_to_gpu(self.h, n)
 
     def time_decode(self, token, pos0, steps):
         return self.ref.L.tvref_time_decode(self.h, int(token), int(pos0), int(steps))

@@ -287,6 +287,20 @@ double tvref_time_decode(tvref_model* h, int token, int pos0, int steps) {
     return std::chrono::duration<double>(t1 - t0).count();
 }
 
+#ifdef TERNATIVE_USE_CUDA
+// Drop-in build (libtvref_dropin.so): the reference host compiled with
+// TERNATIVE_USE_CUDA against ternative_b200/shim/ops_tvb200.cpp instead of
+// cuda/ops_cuda.cu.  init_gpu_backend (model.cpp:264-472) uploads the layers
+// through the shim; Model::forward then takes forward_gpu (model.cpp:863-867).
+int tvref_init_gpu(tvref_model* h) {
+    init_gpu_backend(h->m);
+    return h->m.n_gpu_layers;
+}
+
+// model.cpp:1322-1331
+void tvref_sync_kv_to_gpu(tvref_model* h, int n) { h->m.sync_kv_to_gpu(n); }
+#endif
+
 int tvref_omp_threads() {
 #ifdef _OPENMP
     return omp_get_max_threads();

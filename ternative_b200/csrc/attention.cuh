@@ -114,20 +114,21 @@ attn_decode_kernel(const __grid_constant__ AttnArgs a) {
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // Merge: lane s owns split s (nsplit <= 32) for the running max and the
+    // normaliser; the partial vectors are then summed with independent loads.
     for (int hh = warp; hh < group; hh += kAttnWarps) {
         const int h = kvh * group + hh;
         const float* pb = a.part + (size_t)h * a.nsplit * (hd + 4);
-        float M = -INFINITY;
-        for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(pb + s * (hd + 4) + hd));
-        float L = 0.f;
+        const float ms = lane < a.nsplit ? __ldcg(pb + lane * (hd + 4) + hd) : -INFINITY;
+        const float ls = lane < a.nsplit ? __ldcg(pb + lane * (hd + 4) + hd + 1) : 0.f;
+        const float M = warp_max(ms);
+        const float ws = (ms == -INFINITY) ? 0.f : expf(ms - M);
+        const float L = warp_sum(ls * ws);
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s = 0; s < a.nsplit; ++s) {
-            const float* ps = pb + s * (hd + 4);
-            const float ms = __ldcg(ps + hd);
-            if (ms == -INFINITY) continue;
-            const float w = expf(ms - M);
-            L = fmaf(__ldcg(ps + hd + 1), w, L);
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + lane * 4));
+#pragma unroll 8
+        for (int s2 = 0; s2 < a.nsplit; ++s2) {
+            const float w = __shfl_sync(0xffffffffu, ws, s2);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(pb + s2 * (hd + 4) + lane * 4));
             o.x = fmaf(v.x, w, o.x);
             o.y = fmaf(v.y, w, o.y);
             o.z = fmaf(v.z, w, o.z);

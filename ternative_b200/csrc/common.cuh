@@ -86,23 +86,6 @@ __device__ __forceinline__ int8_t int8_code(float v, float s) {
 
 // ---- small PTX wrappers ---------------------------------------------------------
 
-// Packed F32x2 arithmetic with IEEE round-to-nearest (sm_100 `add/mul.rn.f32x2`).
-// Each lane is an independently rounded F32 operation, never contracted to FMA.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-    uint64_t d;
-    uint64_t ua = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
-    uint64_t ub = (uint64_t)__float_as_uint(b.x) | ((uint64_t)__float_as_uint(b.y) << 32);
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
-    return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-    uint64_t d;
-    uint64_t ua = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
-    uint64_t ub = (uint64_t)__float_as_uint(b.x) | ((uint64_t)__float_as_uint(b.y) << 32);
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
-    return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
-}
-
 // 16-byte streaming load that bypasses L1 (weights are read exactly once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
     uint4 v;

@@ -1,0 +1,257 @@
+// The whole decode step (Model::forward_gpu, src/model.cpp:1354-1582) as one
+// persistent kernel: one CTA of 16 warps per SM, launched cooperatively so all
+// CTAs are resident, walking a table of phases
+//
+//   per layer: QKV+RoPE+KV append | attention | sub-norm+o_proj+residual |
+//              ffn_norm+gate/up+relu^2*up | sub-norm+down+residual
+//   then:      output_norm + lm_head + argmax
+//
+// separated by grid-wide barriers.  Before a CTA enters a barrier its warps
+// have already requested their first weight chunks of the next phase (weights
+// do not depend on the barrier), so HBM keeps streaming while the grid
+// synchronises and the next phase's activations are being read.
+//
+// Every spin is bounded: a barrier that waits about a second sets the abort
+// flag and the timeout status, and every CTA then leaves at its next barrier.
+#pragma once
+
+#include "attention.cuh"
+
+namespace tvb {
+
+enum PhaseKind { PK_GEMV = 0, PK_ATTN = 1 };
+
+struct alignas(16) Phase {
+    int kind;   // PhaseKind
+    int mode;   // GemvMode (PK_GEMV)
+    int wt;     // WType (PK_GEMV)
+    GemvArgs g;
+    AttnArgs at;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier, split so a CTA can do input-independent work between its
+// arrival and its wait.  Arrival: release-add on the counter (no round trip).
+__device__ __forceinline__ void grid_arrive(StepState* st) {
+    __syncthreads();
+    if (threadIdx.x == 0)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&st->bar_ctr) : "memory");
+}
+
+// Wait until `target` arrivals (barrier n of this launch: n * gridDim.x).
+// Returns false on abort or after ~1 s (then sets abort and the timeout bit).
+__device__ __forceinline__ bool grid_wait(StepState* st, unsigned target) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const long long t0 = clock64();
+        while (ld_acquire_gpu(&st->bar_ctr) < target) {
+            if (ld_acquire_gpu(&st->abort)) {
+                ok = 0;
+                break;
+            }
+            if (clock64() - t0 > kSpinLimitCycles) {
+                atomicOr(&st->abort, 1u);
+                atomicOr(&st->status, kStatusTimeout);
+                ok = 0;
+                break;
+            }
+        }
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    return s_ok != 0;
+}
+
+#define TVB_GEMV_CASES(X)                                                     \
+    X(GM_QKV, WT_F16, 2) X(GM_QKV, WT_I8, 2) X(GM_RESID, WT_F16, 1)           \
+    X(GM_RESID, WT_I8, 1) X(GM_GATEUP, WT_F16, 2) X(GM_GATEUP, WT_I8, 2)      \
+    X(GM_LMHEAD, WT_F16, 1)
+
+// Input-independent work for a phase: request its first weight chunks and
+// stage its constants (norm weight, row scales, RoPE row) in shared memory.
+__device__ __forceinline__ void phase_prepare(const Phase& ph, unsigned char* smem, int G, int b, int warp,
+                                             int pos, ChunkBuf& buf) {
+    if (ph.kind != PK_GEMV) return;
+#define X(M, W, R)                                          \
+    if (ph.mode == M && ph.wt == W) {                       \
+        gemv_prefetch<M, W, R>(ph.g, G, b, warp, buf);      \
+        gemv_stage<M, W, R>(ph.g, smem, G, pos);            \
+        return;                                             \
+    }
+    TVB_GEMV_CASES(X)
+#undef X
+}
+
+__device__ __forceinline__ void phase_gemv(const Phase& ph, unsigned char* smem, int G, int pos, int token,
+                                           ChunkBuf& buf, GemvArgmax& best) {
+#define X(M, W, R) \
+    if (ph.mode == M && ph.wt == W) { gemv_run<M, W, R>(ph.g, smem, G, pos, token, buf, best); return; }
+    TVB_GEMV_CASES(X)
+#undef X
+}
+
+// Copy a phase descriptor into shared memory (all threads, 16-byte words).
+__device__ __forceinline__ void load_phase(Phase* dst, const Phase* src) {
+    const int4* s4 = reinterpret_cast<const int4*>(src);
+    int4* d4 = reinterpret_cast<int4*>(dst);
+    for (int i = threadIdx.x; i < (int)(sizeof(Phase) / 16); i += blockDim.x) d4[i] = __ldg(s4 + i);
+}
+
+// Attention work item `b` = (kv head b / nsplit, split b % nsplit) for one CTA:
+// the positions of the split are shared by the 16 warps (warps per head =
+// 16 / group), each keeping an online softmax; the warps of a head merge in
+// shared memory and write one partial (acc[hd], max, sum) per (head, split).
+// The o_proj phase merges the splits while it loads its input.
+__device__ __forceinline__ void attn_item(const AttnArgs& a, int b, unsigned char* smem, int pos) {
+    const int kvh = b / a.nsplit, split = b - kvh * a.nsplit;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hd = a.hd, group = a.nh / a.nkv;
+    const int wph = kGemvWarps / group;                 // warps per head
+    const int hh = warp / wph, sub = warp - hh * wph;
+    const int kv_len = pos + 1;
+    const int chunk = (kv_len + a.nsplit - 1) / a.nsplit;
+    const int c0 = split * chunk, c1 = min(kv_len, c0 + chunk);
+    const int sub_len = (max(c1 - c0, 0) + wph - 1) / wph;
+    const int t0 = c0 + sub * sub_len, t1 = min(c1, t0 + sub_len);
+    const size_t row = (size_t)a.nkv * hd;
+    float* red = reinterpret_cast<float*>(smem);        // [warp][hd + 4]
+    float m = -INFINITY, l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (hh < group) {
+        const int h = kvh * group + hh;
+        const float4 q4 = __ldcg(reinterpret_cast<const float4*>(a.q + h * hd + lane * 4));
+        const float* kb = a.kcache + kvh * hd + lane * 4;
+        const float* vb = a.vcache + kvh * hd + lane * 4;
+        // batches of 4 positions; the next batch's K/V rows load while this one computes
+        float4 kc[4], vc[4], kn[4], vn[4];
+        auto load = [&](int t, float4* kk, float4* vv) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (t + u < t1) {
+                    kk[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(t + u) * row));
+                    vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(t + u) * row));
+                } else {
+                    kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vv[u] = kk[u];
+                }
+            }
+        };
+        load(t0, kc, vc);
+        for (int t = t0; t < t1; t += 4) {
+            load(t + 4, kn, vn);
+            float s[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s[u] = q4.x * kc[u].x + q4.y * kc[u].y + q4.z * kc[u].z + q4.w * kc[u].w;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s[u] = (t + u < t1) ? warp_sum(s[u]) * a.scale : -INFINITY;
+            const float mn = fmaxf(fmaxf(fmaxf(m, s[0]), fmaxf(s[1], s[2])), s[3]);
+            const float corr = expf(m - mn);
+            l *= corr;
+            acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float p = expf(s[u] - mn);
+                l += p;
+                acc.x = fmaf(p, vc[u].x, acc.x);
+                acc.y = fmaf(p, vc[u].y, acc.y);
+                acc.z = fmaf(p, vc[u].z, acc.z);
+                acc.w = fmaf(p, vc[u].w, acc.w);
+            }
+            m = mn;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                kc[u] = kn[u];
+                vc[u] = vn[u];
+            }
+        }
+        float* rw = red + warp * (hd + 4);
+        *reinterpret_cast<float4*>(rw + lane * 4) = acc;
+        if (lane == 0) {
+            rw[hd] = m;
+            rw[hd + 1] = l;
+        }
+    }
+    __syncthreads();
+    // merge the wph sub-splits of each head (warp `sub == 0` of the head)
+    if (hh < group && sub == 0) {
+        const int h = kvh * group + hh;
+        float M = -INFINITY;
+        for (int w = 0; w < wph; ++w) M = fmaxf(M, red[(warp + w) * (hd + 4) + hd]);
+        float L = 0.f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < wph; ++w) {
+            const float* rw = red + (warp + w) * (hd + 4);
+            const float mw = rw[hd];
+            const float s = (mw == -INFINITY) ? 0.f : expf(mw - M);
+            L = fmaf(rw[hd + 1], s, L);
+            const float4 v = *reinterpret_cast<const float4*>(rw + lane * 4);
+            o = make_float4(fmaf(v.x, s, o.x), fmaf(v.y, s, o.y), fmaf(v.z, s, o.z), fmaf(v.w, s, o.w));
+        }
+        float* pp = a.part + ((size_t)h * a.nsplit + split) * (hd + 4);
+        *reinterpret_cast<float4*>(pp + lane * 4) = o;
+        if (lane == 0) {
+            pp[hd] = M;
+            pp[hd + 1] = L;
+        }
+    }
+}
+
+// Shared memory of the step kernel: [0, 1024) two phase descriptors (double
+// buffered), then the per-phase layouts (gemv_smem_layout / attention scratch).
+static_assert(2 * sizeof(Phase) <= 1024, "phase descriptors must fit the reserved area");
+
+__global__ void __launch_bounds__(kGemvThreads, 1)
+decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    Phase* desc = reinterpret_cast<Phase*>(smem);   // desc[p & 1]
+    const int warp = threadIdx.x >> 5;
+    const int G = gridDim.x, b = blockIdx.x;
+    // the step's position and token are fixed until the lm_head's last CTA
+    // advances them at the very end
+    const int pos = __ldcg(&st->pos);
+    const int token = __ldcg(&st->token);
+
+    ChunkBuf buf;
+    load_phase(&desc[0], &phases[0]);
+    __syncthreads();
+    phase_prepare(desc[0], smem, G, b, warp, pos, buf);
+    __syncthreads();
+    bool ok = true;
+    for (int p = 0; p < n_phases && ok; ++p) {
+        const Phase& ph = desc[p & 1];
+        if (ph.kind == PK_GEMV) {
+            GemvArgmax best{-INFINITY, 0};
+            phase_gemv(ph, smem, G, pos, token, buf, best);
+            if (ph.mode == GM_LMHEAD) lmhead_finish(ph.g, best);
+        } else if (b < ph.at.nkv * ph.at.nsplit) {
+            attn_item(ph.at, b, smem + 1024, pos);
+        }
+        if (p + 1 < n_phases) {
+            grid_arrive(st);   // this phase's outputs are written (includes __syncthreads)
+            // input-independent work for the next phase overlaps the barrier
+            load_phase(&desc[(p + 1) & 1], &phases[p + 1]);
+            __syncthreads();
+            phase_prepare(desc[(p + 1) & 1], smem, G, b, warp, pos, buf);
+            ok = grid_wait(st, (unsigned)(p + 1) * (unsigned)G);
+        }
+    }
+    // last CTA out resets the barrier for the next launch
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&st->exit_ctr, 1u) == (unsigned)G - 1u) {
+            st->bar_ctr = 0u;
+            st->exit_ctr = 0u;
+            __threadfence();
+        }
+    }
+}
+
+}  // namespace tvb

@@ -9,10 +9,11 @@
 // captured once into a CUDA graph.  Position and token live in device memory
 // (StepState), so the same graph serves every position and greedy decode can
 // chain steps without the host.
-#include "attention.cuh"
+#include "decode.cuh"
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -27,6 +28,10 @@ namespace tvb {
 
 __device__ unsigned g_standalone_status;
 
+// TVB_DISABLE_PDL=1 launches the fused step without programmatic dependent
+// launch (for profilers and A/B timing); read once when a context is created.
+static bool g_disable_pdl = false;
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                              cudaStream_t st, bool pdl, Args&&... args) {
@@ -39,27 +44,24 @@ static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = (pdl && !g_disable_pdl) ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-constexpr int kSlotBudget = 96 * 1024;
-constexpr int kMaxDynSmem = 227 * 1024;
+// Largest dynamic shared memory a GEMV launch may request: the device's
+// opt-in per-block limit minus a margin for the kernels' static shared memory.
+static int g_max_dyn_smem = 0;
 
 template <int MODE, int WT, int R>
 static tvb_status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
-    const int esz = (WT == WT_F16) ? 2 : 1;
-    const int stage_bytes = R * a.K * esz;
-    int stages = std::max(2, std::min(16, kSlotBudget / stage_bytes));
-    GemvSmem L = gemv_smem_layout(R, a.K, stages, stage_bytes);
-    while (L.total > kMaxDynSmem && stages > 2) L = gemv_smem_layout(R, a.K, --stages, stage_bytes);
-    if (L.total > kMaxDynSmem)
+    const int units = gemv_units<MODE>(a, R);
+    if (units <= 0) return TVB_OK;
+    const int grid = std::min(units, num_sms());
+    const GemvSmem L = gemv_smem_layout(a.K, WT == WT_F16 ? 2 : 1, gemv_rows_cap(units, grid, R));
+    if (L.total > g_max_dyn_smem)
         return set_error(TVB_ERR_UNSUPPORTED, "gemv: K=%d too large for shared-memory staging", a.K);
-    const int groups = gemv_groups<MODE>(a, R);
-    if (groups <= 0) return TVB_OK;
-    const int grid = std::min(groups, num_sms());
     auto kern = stream_gemv_kernel<MODE, WT, R>;
-    TVB_CUDA(launch_ex(kern, dim3(grid), dim3(kGemvThreads), (size_t)L.total, st, pdl, a, stages));
+    TVB_CUDA(launch_ex(kern, dim3(grid), dim3(kGemvThreads), (size_t)L.total, st, pdl, a));
     return TVB_OK;
 }
 
@@ -68,20 +70,23 @@ static tvb_status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
 template <int MODE, int WT, int R>
 static cudaError_t allow_smem() {
     return cudaFuncSetAttribute(stream_gemv_kernel<MODE, WT, R>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, g_max_dyn_smem);
 }
 
 tvb_status prepare_kernels() {
     static int done = 0;
     if (done) return TVB_OK;
+    int dev = 0, optin = 0;
+    TVB_CUDA(cudaGetDevice(&dev));
+    TVB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    g_max_dyn_smem = optin - 1024;
     cudaError_t e = cudaSuccess;
     cudaError_t r[] = {
-        allow_smem<GM_PLAIN, WT_F16, 4>(), allow_smem<GM_PLAIN, WT_I8, 4>(),
+        allow_smem<GM_PLAIN, WT_F16, 1>(), allow_smem<GM_PLAIN, WT_I8, 1>(),
         allow_smem<GM_QKV, WT_F16, 2>(),   allow_smem<GM_QKV, WT_I8, 2>(),
-        allow_smem<GM_RESID, WT_F16, 2>(), allow_smem<GM_RESID, WT_I8, 2>(),
         allow_smem<GM_RESID, WT_F16, 1>(), allow_smem<GM_RESID, WT_I8, 1>(),
         allow_smem<GM_GATEUP, WT_F16, 2>(), allow_smem<GM_GATEUP, WT_I8, 2>(),
-        allow_smem<GM_LMHEAD, WT_F16, 8>(),
+        allow_smem<GM_LMHEAD, WT_F16, 1>(),
     };
     for (cudaError_t x : r)
         if (x != cudaSuccess) e = x;
@@ -131,7 +136,7 @@ struct tvb_context {
     // fused-step buffers
     float *e_x = nullptr, *e_q = nullptr, *e_attn = nullptr, *e_h = nullptr, *e_logits = nullptr;
     float* attn_part = nullptr;
-    int nsplit = 16;
+    int nsplit = 8;    // attention splits per KV head, merged by the o_proj phase
     float *kcache = nullptr, *vcache = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
     StepState* st = nullptr;
@@ -145,6 +150,10 @@ struct tvb_context {
     std::vector<bool> layer_set;
     const void* tok_embd = nullptr;
     const float* output_norm = nullptr;
+    // the decode step as a phase table for decode_step_kernel
+    Phase* d_phases = nullptr;
+    int n_phases = 0;
+    int step_smem = 0;
     // graphs
     cudaGraphExec_t g_step = nullptr;    // layers + lm_head
     cudaGraphExec_t g_layers = nullptr;  // layers only (prefill rows before the last)
@@ -159,131 +168,144 @@ tvb_status alloc_dev(void** p, size_t bytes) {
     return TVB_OK;
 }
 
-tvb_status record_layers(tvb_context* c, bool with_head) {
-    cudaStream_t st = c->stream;
+// The decode step as phases (src/model.cpp:1399-1451, 1571-1580).
+std::vector<Phase> build_phases(tvb_context* c) {
+    std::vector<Phase> ph;
     const float scale = 1.0f / std::sqrt((float)c->cfg.head_dim);
+    auto gemv = [&](int mode, int wt) {
+        Phase p = {};
+        p.kind = PK_GEMV;
+        p.mode = mode;
+        p.wt = wt;
+        p.g.eps = c->cfg.rms_norm_eps;
+        p.g.st = c->st;
+        p.g.status = &c->st->status;
+        return p;
+    };
     for (int l = 0; l < c->L; ++l) {
         const tvb_layer_weights& lw = c->layers[l];
-        int wt;
-        if (!wt_of(lw.wq.dtype, &wt)) return set_error(TVB_ERR_UNSUPPORTED, "layer %d: dtype", l);
+        int wt = WT_F16;
+        wt_of(lw.wq.dtype, &wt);
         float* kl = c->kcache + (size_t)l * c->cfg.max_seq_len * c->Hk;
         float* vl = c->vcache + (size_t)l * c->cfg.max_seq_len * c->Hk;
-        // (a)-(c): attn_norm, q/k/v, RoPE, KV append
-        {
-            GemvArgs a = {};
-            fill_weight(a, 0, lw.wq);
-            fill_weight(a, 1, lw.wk);
-            fill_weight(a, 2, lw.wv);
-            a.K = c->H;
-            a.x = c->e_x;
-            a.embd = static_cast<const uint16_t*>(c->tok_embd);
-            a.x_out = c->e_x;
-            a.gather_token = (l == 0);
-            a.norm_w = lw.attn_norm;
-            a.eps = c->cfg.rms_norm_eps;
-            a.nh = c->cfg.num_heads;
-            a.nkv = c->cfg.num_kv_heads;
-            a.hd = c->cfg.head_dim;
-            a.q_out = c->e_q;
-            a.kcache = kl;
-            a.vcache = vl;
-            a.rope_cos = c->rope_cos;
-            a.rope_sin = c->rope_sin;
-            a.st = c->st;
-            a.status = &c->st->status;
-            TVB_TRY((launch_gemv_wt<GM_QKV, 2>(wt, a, st, l > 0)));
+        {   // (a)-(c): attn_norm, q/k/v, RoPE, KV append
+            Phase p = gemv(GM_QKV, wt);
+            fill_weight(p.g, 0, lw.wq);
+            fill_weight(p.g, 1, lw.wk);
+            fill_weight(p.g, 2, lw.wv);
+            p.g.K = c->H;
+            p.g.x = c->e_x;
+            p.g.embd = static_cast<const uint16_t*>(c->tok_embd);
+            p.g.x_out = c->e_x;
+            p.g.gather_token = (l == 0);
+            p.g.norm_w = lw.attn_norm;
+            p.g.nh = c->cfg.num_heads;
+            p.g.nkv = c->cfg.num_kv_heads;
+            p.g.hd = c->cfg.head_dim;
+            p.g.q_out = c->e_q;
+            p.g.kcache = kl;
+            p.g.vcache = vl;
+            p.g.rope_cos = c->rope_cos;
+            p.g.rope_sin = c->rope_sin;
+            ph.push_back(p);
         }
-        // (d): attention over kv_len = pos + 1
-        {
-            AttnArgs a = {};
-            a.q = c->e_q;
-            a.kcache = kl;
-            a.vcache = vl;
-            a.out = c->e_attn;
-            a.part = c->attn_part;
-            a.nh = c->cfg.num_heads;
-            a.nkv = c->cfg.num_kv_heads;
-            a.hd = c->cfg.head_dim;
-            a.nsplit = c->nsplit;
-            a.scale = scale;
-            a.kv_len = -1;
-            a.st = c->st;
-            a.status = &c->st->status;
-            TVB_TRY(launch_attn(a, st, true));
+        {   // (d): attention over kv_len = pos + 1
+            Phase p = {};
+            p.kind = PK_ATTN;
+            p.at.q = c->e_q;
+            p.at.kcache = kl;
+            p.at.vcache = vl;
+            p.at.out = c->e_attn;
+            p.at.part = c->attn_part;
+            p.at.nh = c->cfg.num_heads;
+            p.at.nkv = c->cfg.num_kv_heads;
+            p.at.hd = c->cfg.head_dim;
+            p.at.nsplit = c->nsplit;
+            p.at.scale = scale;
+            p.at.kv_len = -1;
+            p.at.st = c->st;
+            p.at.status = &c->st->status;
+            ph.push_back(p);
         }
-        // (e)-(f): attn_sub_norm, wo, residual
-        {
-            GemvArgs a = {};
-            fill_weight(a, 0, lw.wo);
-            a.N = c->H;
-            a.K = c->Hq;
-            a.x = c->e_attn;
-            a.norm_w = lw.attn_sub_norm;
-            a.eps = c->cfg.rms_norm_eps;
-            a.y = c->e_x;
-            a.st = c->st;
-            a.status = &c->st->status;
-            TVB_TRY((launch_gemv_wt<GM_RESID, 2>(wt, a, st, true)));
+        {   // (e)-(f): attn_sub_norm, wo, residual
+            Phase p = gemv(GM_RESID, wt);
+            fill_weight(p.g, 0, lw.wo);
+            p.g.N = c->H;
+            p.g.K = c->Hq;
+            p.g.x = c->e_attn;
+            p.g.attn_part = c->attn_part;   // input: merge of the attention splits
+            p.g.attn_nsplit = c->nsplit;
+            p.g.hd = c->cfg.head_dim;
+            p.g.norm_w = lw.attn_sub_norm;
+            p.g.y = c->e_x;
+            ph.push_back(p);
         }
-        // (g)-(h): ffn_norm, gate/up, relu^2 * up
-        {
-            GemvArgs a = {};
-            fill_weight(a, 0, lw.w_gate);
-            fill_weight(a, 1, lw.w_up);
-            a.N = c->I;
-            a.K = c->H;
-            a.x = c->e_x;
-            a.norm_w = lw.ffn_norm;
-            a.eps = c->cfg.rms_norm_eps;
-            a.y = c->e_h;
-            a.st = c->st;
-            a.status = &c->st->status;
-            TVB_TRY((launch_gemv_wt<GM_GATEUP, 2>(wt, a, st, true)));
+        {   // (g)-(h): ffn_norm, gate/up, relu^2 * up
+            Phase p = gemv(GM_GATEUP, wt);
+            fill_weight(p.g, 0, lw.w_gate);
+            fill_weight(p.g, 1, lw.w_up);
+            p.g.N = c->I;
+            p.g.K = c->H;
+            p.g.x = c->e_x;
+            p.g.norm_w = lw.ffn_norm;
+            p.g.y = c->e_h;
+            ph.push_back(p);
         }
-        // (i): ffn_sub_norm, down, residual
-        {
-            GemvArgs a = {};
-            fill_weight(a, 0, lw.w_down);
-            a.N = c->H;
-            a.K = c->I;
-            a.x = c->e_h;
-            a.norm_w = lw.ffn_sub_norm;
-            a.eps = c->cfg.rms_norm_eps;
-            a.y = c->e_x;
-            a.st = c->st;
-            a.status = &c->st->status;
-            TVB_TRY((launch_gemv_wt<GM_RESID, 1>(wt, a, st, true)));
+        {   // (i): ffn_sub_norm, down, residual
+            Phase p = gemv(GM_RESID, wt);
+            fill_weight(p.g, 0, lw.w_down);
+            p.g.N = c->H;
+            p.g.K = c->I;
+            p.g.x = c->e_h;
+            p.g.norm_w = lw.ffn_sub_norm;
+            p.g.y = c->e_x;
+            ph.push_back(p);
         }
     }
-    if (with_head) {
-        GemvArgs a = {};
-        a.w[0] = c->tok_embd;
-        a.tscale[0] = 1.0f;
-        a.N = c->V;
-        a.K = c->H;
-        a.x = c->e_x;
-        a.norm_w = c->output_norm;
-        a.eps = c->cfg.rms_norm_eps;
-        a.y = c->e_logits;
-        a.st = c->st;
-        a.status = &c->st->status;
-        TVB_TRY((launch_gemv<GM_LMHEAD, WT_F16, 8>(a, st, true)));
+    {   // final norm + tied lm_head + argmax
+        Phase p = gemv(GM_LMHEAD, WT_F16);
+        p.g.w[0] = c->tok_embd;
+        p.g.tscale[0] = 1.0f;
+        p.g.N = c->V;
+        p.g.K = c->H;
+        p.g.x = c->e_x;
+        p.g.norm_w = c->output_norm;
+        p.g.y = c->e_logits;
+        ph.push_back(p);
     }
-    return TVB_OK;
+    return ph;
 }
 
-tvb_status capture(tvb_context* c, bool with_head, cudaGraphExec_t* out) {
+int phase_units(const Phase& p) {
+    const int R = (p.mode == GM_QKV || p.mode == GM_GATEUP) ? 2 : 1;
+    if (p.mode == GM_QKV) return (p.g.nh + 2 * p.g.nkv) * (p.g.hd >> 1);
+    if (p.mode == GM_GATEUP) return p.g.N;
+    return (p.g.N + R - 1) / R;
+}
+
+tvb_status capture(tvb_context* c, int n_phases, cudaGraphExec_t* out) {
     if (*out) {
         cudaGraphExecDestroy(*out);
         *out = nullptr;
     }
     TVB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    tvb_status s = record_layers(c, with_head);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = (size_t)c->step_smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaLaunchKernelEx(&cfg, decode_step_kernel, (const Phase*)c->d_phases, n_phases,
+                                        c->st);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
-    if (s != TVB_OK) {
+    if (le != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
-        return s;
+        return cuda_error(le, "launch decode_step_kernel");
     }
     if (e != cudaSuccess) return cuda_error(e, "cudaStreamEndCapture");
     e = cudaGraphInstantiate(out, g, 0);
@@ -297,17 +319,43 @@ tvb_status ensure_graphs(tvb_context* c) {
     for (int l = 0; l < c->L; ++l)
         if (!c->layer_set[l]) return set_error(TVB_ERR_STATE, "layer %d weights not set", l);
     if (!c->tok_embd || !c->output_norm) return set_error(TVB_ERR_STATE, "output weights not set");
-    TVB_TRY(capture(c, true, &c->g_step));
-    TVB_TRY(capture(c, false, &c->g_layers));
+    std::vector<Phase> ph = build_phases(c);
+    // shared memory: the largest per-phase layout, and the attention scratch
+    const int G = num_sms();
+    int smem = 1024 + kGemvWarps * (c->cfg.head_dim + 4) * 4;
+    for (const Phase& p : ph) {
+        if (p.kind != PK_GEMV) continue;
+        const int R = (p.mode == GM_QKV || p.mode == GM_GATEUP) ? 2 : 1;
+        const int units = phase_units(p);
+        const GemvSmem L = gemv_smem_layout(p.g.K, p.wt == WT_F16 ? 2 : 1, gemv_rows_cap(units, G, R));
+        smem = std::max(smem, L.total);
+    }
+    if (smem > g_max_dyn_smem)
+        return set_error(TVB_ERR_UNSUPPORTED, "decode step needs %d B of shared memory", smem);
+    TVB_CUDA(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int per_sm = 0;
+    TVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kGemvThreads, smem));
+    if (per_sm < 1) return set_error(TVB_ERR_UNSUPPORTED, "decode step kernel cannot be resident");
+    if (c->d_phases) cudaFree(c->d_phases);
+    c->d_phases = nullptr;
+    TVB_TRY(alloc_dev((void**)&c->d_phases, ph.size() * sizeof(Phase)));
+    TVB_CUDA(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    c->n_phases = (int)ph.size();
+    c->step_smem = smem;
+    TVB_TRY(capture(c, c->n_phases, &c->g_step));
+    TVB_TRY(capture(c, c->n_phases - 1, &c->g_layers));
     c->dirty = false;
     return TVB_OK;
 }
 
 tvb_status check_status(tvb_context* c) {
-    if (c->h_st->status & kStatusTimeout)
-        return set_error(TVB_ERR_TIMEOUT, "a device-side wait exceeded its limit");
-    if (c->h_st->status) return set_error(TVB_ERR_CUDA, "device status 0x%x", c->h_st->status);
-    return TVB_OK;
+    const unsigned s = c->h_st->status;
+    if (!s) return TVB_OK;
+    // clear counters, flags and the abort latch so the next call starts clean
+    cudaMemsetAsync(c->st, 0, sizeof(StepState), c->stream);
+    cudaStreamSynchronize(c->stream);
+    if (s & kStatusTimeout) return set_error(TVB_ERR_TIMEOUT, "a device-side wait exceeded its limit");
+    return set_error(TVB_ERR_CUDA, "device status 0x%x", s);
 }
 
 }  // namespace
@@ -329,6 +377,8 @@ tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
     {
         tvb_status ps = prepare_kernels();
         if (ps != TVB_OK) return ps;
+        const char* e = std::getenv("TVB_DISABLE_PDL");
+        g_disable_pdl = e && e[0] == '1';
     }
     tvb_context* c = new (std::nothrow) tvb_context();
     if (!c) return set_error(TVB_ERR_OOM, "context_create: host allocation");
@@ -340,6 +390,7 @@ tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
     c->I = m.intermediate_size;
     c->V = m.vocab_size;
     c->L = m.num_layers;
+    c->nsplit = std::max(1, std::min(kMaxAttnSplits, num_sms() / m.num_kv_heads));
     c->layers.assign(c->L, tvb_layer_weights{});
     c->layer_set.assign(c->L, false);
     cudaGetDevice(&c->device);
@@ -357,7 +408,7 @@ tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
         {(void**)&c->d_gate, I * 4ull}, {(void**)&c->d_up, I * 4ull},
         {(void**)&c->e_x, H * 4ull}, {(void**)&c->e_q, Hq * 4ull}, {(void**)&c->e_attn, Hq * 4ull},
         {(void**)&c->e_h, I * 4ull}, {(void**)&c->e_logits, V * 4ull},
-        {(void**)&c->attn_part, (size_t)m.num_heads * c->nsplit * (m.head_dim + 4) * 4ull},
+        {(void**)&c->attn_part, (size_t)m.num_heads * 32 * (m.head_dim + 4) * 4ull},
         {(void**)&c->kcache, kv * 4}, {(void**)&c->vcache, kv * 4},
         {(void**)&c->rope_cos, (size_t)m.max_seq_len * (m.head_dim / 2) * 4},
         {(void**)&c->rope_sin, (size_t)m.max_seq_len * (m.head_dim / 2) * 4},
@@ -405,7 +456,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
     if (c->g_layers) cudaGraphExecDestroy(c->g_layers);
     void* dev[] = {c->d_x, c->d_norm, c->d_q, c->d_k, c->d_v, c->d_gate, c->d_up, c->e_x, c->e_q,
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
-                   c->rope_cos, c->rope_sin, c->st, c->hist};
+                   c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
@@ -613,8 +664,8 @@ tvb_status standalone_gemv(float* y, const float* x, const void* W, int wt, cons
     a.x = x;
     a.y = y;
     a.status = status;
-    return wt == WT_F16 ? launch_gemv<GM_PLAIN, WT_F16, 4>(a, st, false)
-                        : launch_gemv<GM_PLAIN, WT_I8, 4>(a, st, false);
+    return wt == WT_F16 ? launch_gemv<GM_PLAIN, WT_F16, 1>(a, st, false)
+                        : launch_gemv<GM_PLAIN, WT_I8, 1>(a, st, false);
 }
 
 tvb_status standalone_attention(const float* q, const float* kc, const float* vc, int kv_len, float* out,

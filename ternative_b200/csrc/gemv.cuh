@@ -9,14 +9,22 @@
 //   GM_GATEUP  rms_norm(x) -> relu(gate)^2 * up                   :1433-1439
 //   GM_LMHEAD  rms_norm(x) -> logits + greedy argmax              :1571-1580
 //
-// B200 mapping.  A persistent grid (one CTA per SM) splits the output rows
-// into groups of R rows; each CTA streams its groups' rows from HBM into a
-// ring of shared-memory slots with 1-D bulk copies (cp.async.bulk, one per
-// contiguous weight row) completed on mbarriers.  The CTA issues the first
-// slots' copies before griddepcontrol.wait, so under programmatic dependent
-// launch the weight stream of kernel i+1 starts while kernel i drains.  The
-// activation vector is normalised once per CTA into shared memory; the 8 warps
-// split each group's 256-column chunks and reduce across warps in a fixed order.
+// B200 mapping.  A persistent grid (one CTA of 16 warps per SM) gives every CTA
+// a balanced, contiguous range of output units (a unit is one row, or the two
+// rows an epilogue pairs: RoPE halves, gate/up).  The CTA's rows are cut into
+// 2 KB chunks and the (row, chunk) items, in row-major order, are split evenly
+// over the 16 warps, so every warp streams the same number of bytes from one
+// contiguous span of the weight matrix whatever the row length.  A warp keeps
+// kDepth chunks in flight in registers with 128-bit streaming loads (one
+// 512-byte coalesced request per warp instruction, L1 bypassed): measured on
+// this part, plain streaming loads reach a higher fraction of HBM bandwidth
+// than shared-memory staging, whose writes would compete with the reads of the
+// activation vector for shared-memory bandwidth.  The first chunks of a phase
+// are requested before the wait for the phase's inputs (the grid barrier of the
+// decode-step kernel, griddepcontrol.wait in stand-alone launches), so the
+// weight stream never drains across a phase boundary.  The normalised
+// activation vector lives in shared memory; per-(row, chunk) sums go to shared
+// memory and are added in chunk order by the epilogue (deterministic).
 #pragma once
 
 #include "stream.cuh"
@@ -26,9 +34,10 @@ namespace tvb {
 enum GemvMode { GM_PLAIN = 0, GM_QKV = 1, GM_RESID = 2, GM_GATEUP = 3, GM_LMHEAD = 4 };
 enum WType { WT_F16 = 0, WT_I8 = 1 };
 
-constexpr int kGemvThreads = 256;
+constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kMaxKvHeads = 64;
+constexpr int kMaxAttnSplits = 8;   // attention splits merged by the o_proj prologue
 
 // Device-resident per-context step state (read/written by the fused kernels).
 struct StepState {
@@ -40,6 +49,9 @@ struct StepState {
     int next_token;                 // argmax of this step's logits
     float max_logit;
     unsigned attn_done[kMaxKvHeads];
+    unsigned bar_ctr;    // grid-barrier arrivals of the running decode-step launch
+    unsigned exit_ctr;   // CTAs that left the running launch
+    unsigned abort;      // set when a barrier wait gave up; every CTA then leaves
 };
 
 struct GemvArgs {
@@ -63,6 +75,8 @@ struct GemvArgs {
     StepState* st;
     unsigned* status;
     int gather_token;           // GM_QKV: 1 on layer 0
+    const float* attn_part;     // GM_RESID after attention: input = merge of these partials
+    int attn_nsplit;            // splits per head in attn_part ([nh][nsplit][hd + 4])
 };
 
 __device__ __forceinline__ unsigned long long argmax_pack(float v, int idx) {
@@ -103,268 +117,420 @@ __device__ __forceinline__ bool group_row(const GemvArgs& a, int g, int i, int& 
 }
 
 template <int MODE>
-__host__ __device__ inline int gemv_groups(const GemvArgs& a, int R) {
+__host__ __device__ inline int gemv_units(const GemvArgs& a, int R) {
     if (MODE == GM_QKV) return (a.nh + 2 * a.nkv) * (a.hd >> 1);
     if (MODE == GM_GATEUP) return a.N;
     return (a.N + R - 1) / R;
 }
 
-template <int WT>
-__device__ __forceinline__ float dot8(const unsigned char* wp, const float4& xlo, const float4& xhi) {
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    const uint64_t ua = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
+    const uint64_t ub = (uint64_t)__float_as_uint(b.x) | ((uint64_t)__float_as_uint(b.y) << 32);
+    const uint64_t uc = (uint64_t)__float_as_uint(c.x) | ((uint64_t)__float_as_uint(c.y) << 32);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(ua), "l"(ub), "l"(uc));
+    return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+
+// acc (two F32 lanes) += 8 weights . 8 activations, packed F32x2 FMAs.
+__device__ __forceinline__ float2 dot8_h(uint4 u, const float4& xlo, const float4& xhi, float2 acc) {
     float w[8];
-    if (WT == WT_F16) {
-        uint4 u = *reinterpret_cast<const uint4*>(wp);
-        h8_to_f8(u, w);
-    } else {
-        uint2 u = *reinterpret_cast<const uint2*>(wp);
-        i8x4_to_f4(u.x, w);
-        i8x4_to_f4(u.y, w + 4);
-    }
-    float s = w[0] * xlo.x;
-    s = fmaf(w[1], xlo.y, s);
-    s = fmaf(w[2], xlo.z, s);
-    s = fmaf(w[3], xlo.w, s);
-    s = fmaf(w[4], xhi.x, s);
-    s = fmaf(w[5], xhi.y, s);
-    s = fmaf(w[6], xhi.z, s);
-    s = fmaf(w[7], xhi.w, s);
-    return s;
+    h8_to_f8(u, w);
+    acc = ffma2(make_float2(w[0], w[1]), make_float2(xlo.x, xlo.y), acc);
+    acc = ffma2(make_float2(w[2], w[3]), make_float2(xlo.z, xlo.w), acc);
+    acc = ffma2(make_float2(w[4], w[5]), make_float2(xhi.x, xhi.y), acc);
+    acc = ffma2(make_float2(w[6], w[7]), make_float2(xhi.z, xhi.w), acc);
+    return acc;
+}
+__device__ __forceinline__ float2 dot4_i8(uint32_t u, const float4& x, float2 acc) {
+    float w[4];
+    i8x4_to_f4(u, w);
+    acc = ffma2(make_float2(w[0], w[1]), make_float2(x.x, x.y), acc);
+    acc = ffma2(make_float2(w[2], w[3]), make_float2(x.z, x.w), acc);
+    return acc;
 }
 
 // Shared memory layout (bytes):
-//   [0, 64*8)                   mbarriers (up to 64 slots)
-//   [512, 512 + 2*8*R*4)        cross-warp partial sums, double buffered
-//   [.., + K*4)                 activation vector (16-byte aligned)
-//   [.., + S*stage)             weight slots (128-byte aligned)
+//   [0, 1024)       reserved (phase descriptors, step scalars)
+//   [1024, ..)      activation vector, K floats
+//   [.., ..)        norm weight, K floats (staged before the inputs are ready)
+//   [.., ..)        per-(chunk, row) partial sums of this CTA, nc * rows_cap floats
+//   [.., ..)        epilogue operands: row scale and residual per local row
+//                   (2 * rows_cap floats), RoPE cos/sin at this position
+constexpr int kChunkBytes = 2048;   // one item: 4 x 512 B warp requests
+constexpr int kDepth = 3;           // items in flight per warp
+
 struct GemvSmem {
-    int part_off, x_off, stage_off, total;
+    int x_off, nw_off, part_off, pre_off, total;
 };
-__host__ __device__ inline GemvSmem gemv_smem_layout(int R, int K, int stages, int stage_bytes) {
+constexpr int kMaxRopeHalf = 128;
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int esz, int rows_cap) {
     GemvSmem s;
-    s.part_off = 512;
-    s.x_off = s.part_off + ((2 * kGemvWarps * R * 4 + 127) / 128) * 128;
-    s.stage_off = s.x_off + ((K * 4 + 127) / 128) * 128;
-    s.total = s.stage_off + stages * stage_bytes;
+    const int nc = (K * esz + kChunkBytes - 1) / kChunkBytes;
+    s.x_off = 1024;
+    s.nw_off = s.x_off + ((K * 4 + 127) / 128) * 128;
+    s.part_off = s.nw_off + ((K * 4 + 127) / 128) * 128;
+    s.pre_off = s.part_off + ((nc * rows_cap * 4 + 127) / 128) * 128;
+    s.total = s.pre_off + (((2 * rows_cap + 2 * kMaxRopeHalf) * 4 + 127) / 128) * 128;
     return s;
 }
+__host__ __device__ inline int gemv_rows_cap(int n_units, int grid, int R) {
+    return ((n_units + grid - 1) / grid) * R;
+}
+
+// Geometry of one GEMV phase for this CTA/warp: the CTA's units [U0, U1)
+// become local rows [0, nrows); items t = lrow * nc + c (row-major, so a
+// warp's items are one contiguous span of the weight matrix) are split evenly
+// over the warps, this warp owning [t0, t0 + mine).
+struct GemvGeo {
+    int U0, U1, nrows, t0, mine, nc, rows_cap;
+};
 
 template <int MODE, int WT, int R>
-__global__ void __launch_bounds__(kGemvThreads)
-stream_gemv_kernel(const __grid_constant__ GemvArgs a, int stages) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+__device__ __forceinline__ GemvGeo gemv_geo(const GemvArgs& a, int G, int b, int warp) {
+    GemvGeo g;
+    const int esz = (WT == WT_F16) ? 2 : 1;
+    const int n_units = gemv_units<MODE>(a, R);
+    g.nc = (a.K * esz + kChunkBytes - 1) / kChunkBytes;
+    g.rows_cap = gemv_rows_cap(n_units, G, R);
+    g.U0 = (int)((long long)n_units * b / G);
+    g.U1 = (int)((long long)n_units * (b + 1) / G);
+    g.nrows = (g.U1 - g.U0) * R;
+    const int items = g.nrows * g.nc;
+    g.t0 = (int)((long long)items * warp / kGemvWarps);
+    g.mine = (int)((long long)items * (warp + 1) / kGemvWarps) - g.t0;
+    return g;
+}
+
+// A warp's chunks in flight: slot j holds this lane's four 16-byte pieces.
+struct ChunkBuf {
+    uint4 v[kDepth][4];
+};
+
+// Request item k of this warp into slot j (all lanes; out-of-range -> zeros).
+template <int MODE, int WT, int R>
+__device__ __forceinline__ void gemv_load(const GemvArgs& a, const GemvGeo& g, int k, uint4 (&dst)[4]) {
+    const int esz = (WT == WT_F16) ? 2 : 1;
+    const int row_bytes = a.K * esz;
+    const int lane = threadIdx.x & 31;
+    int bytes = 0;
+    const unsigned char* src = nullptr;
+    if (k < g.mine) {
+        const int t = g.t0 + k;
+        const int lrow = t / g.nc, c = t - lrow * g.nc;
+        int m, row;
+        if (group_row<MODE, R>(a, g.U0 + lrow / R, lrow % R, m, row)) {
+            const int off = c * kChunkBytes;
+            bytes = min(kChunkBytes, row_bytes - off);
+            src = static_cast<const unsigned char*>(a.w[m]) + (size_t)row * row_bytes + off;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int o = 512 * i + lane * 16;
+        dst[i] = (o < bytes) ? ld_stream16(src + o) : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// Request this warp's first kDepth items of a phase (no dependence on inputs).
+template <int MODE, int WT, int R>
+__device__ __forceinline__ void gemv_prefetch(const GemvArgs& a, int G, int b, int warp, ChunkBuf& buf) {
+    const GemvGeo g = gemv_geo<MODE, WT, R>(a, G, b, warp);
+#pragma unroll
+    for (int j = 0; j < kDepth; ++j) gemv_load<MODE, WT, R>(a, g, j, buf.v[j]);
+}
+
+struct GemvArgmax {
+    float v;
+    int i;
+};
+
+// Stage the phase's input-independent operands into shared memory: the norm
+// weight, per-row output scales and the RoPE factors of this position.  Runs
+// before the wait for the phase's inputs, so its loads overlap that wait.
+template <int MODE, int WT, int R>
+__device__ __forceinline__ void gemv_stage(const GemvArgs& a, unsigned char* smem, int G, int pos) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int esz = (WT == WT_F16) ? 2 : 1;
+    const GemvGeo g = gemv_geo<MODE, WT, R>(a, G, blockIdx.x, warp);
+    const GemvSmem L = gemv_smem_layout(a.K, esz, g.rows_cap);
+    if (a.norm_w) {
+        const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
+        float4* nw4 = reinterpret_cast<float4*>(smem + L.nw_off);
+        for (int k4 = tid; k4 < (a.K >> 2); k4 += kGemvThreads) nw4[k4] = __ldg(w4 + k4);
+    }
+    float* pre_scale = reinterpret_cast<float*>(smem + L.pre_off);
+    for (int lr = tid; lr < g.nrows; lr += kGemvThreads) {
+        int m, row;
+        float sc = 1.0f;
+        if (group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row))
+            sc = a.row_scale[m] ? __ldg(a.row_scale[m] + row) : a.tscale[m];
+        pre_scale[lr] = sc;
+    }
+    if (MODE == GM_QKV) {
+        float* pre_cos = pre_scale + 2 * g.rows_cap;
+        float* pre_sin = pre_cos + kMaxRopeHalf;
+        const int half = a.hd >> 1;
+        for (int d = tid; d < half; d += kGemvThreads) {
+            pre_cos[d] = __ldg(a.rope_cos + (size_t)pos * half + d);
+            pre_sin[d] = __ldg(a.rope_sin + (size_t)pos * half + d);
+        }
+    }
+}
+
+// One GEMV phase whose constants are staged (gemv_stage), whose first kDepth
+// items are already requested in `buf`, and whose inputs are ready: residual
+// operands, activation prologue, chunk stream, epilogue.
+template <int MODE, int WT, int R>
+__device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem, int G, int pos, int token,
+                                         ChunkBuf& buf, GemvArgmax& best) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, b = blockIdx.x;
     const int K = a.K;
     const int esz = (WT == WT_F16) ? 2 : 1;
-    const int row_bytes = K * esz;
-    const int stage_bytes = R * row_bytes;
-    const GemvSmem L = gemv_smem_layout(R, K, stages, stage_bytes);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-    float* part = reinterpret_cast<float*>(smem + L.part_off);
+    const GemvGeo g = gemv_geo<MODE, WT, R>(a, G, b, warp);
+    const GemvSmem L = gemv_smem_layout(K, esz, g.rows_cap);
     float* xs = reinterpret_cast<float*>(smem + L.x_off);
-    unsigned char* slots = smem + L.stage_off;
+    const float* nws = reinterpret_cast<const float*>(smem + L.nw_off);
+    float* part = reinterpret_cast<float*>(smem + L.part_off);       // [c][lrow]
+    float* pre_scale = reinterpret_cast<float*>(smem + L.pre_off);   // [lrow]
+    float* pre_res = pre_scale + g.rows_cap;                         // [lrow]
+    float* pre_cos = pre_res + g.rows_cap;                           // [hd/2]
+    float* pre_sin = pre_cos + kMaxRopeHalf;
 
-    const int n_groups = gemv_groups<MODE>(a, R);
-    const int G = gridDim.x, b = blockIdx.x;
-    const int g0 = (int)((long long)n_groups * b / G);
-    const int g1 = (int)((long long)n_groups * (b + 1) / G);
-    const int my = g1 - g0;
-
-    auto issue = [&](int g, int slot) {
-        uint32_t bytes = 0;
-        int ms[R], rows[R];
-        bool ok[R];
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            ok[i] = group_row<MODE, R>(a, g, i, ms[i], rows[i]);
-            if (ok[i]) bytes += row_bytes;
+    // ---- residual operands (written by earlier phases) ---------------------------
+    if (MODE == GM_RESID) {
+        for (int lr = tid; lr < g.nrows; lr += kGemvThreads) {
+            int m, row;
+            pre_res[lr] = group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row) ? __ldcg(a.y + row) : 0.f;
         }
-        mbar_expect_tx(&bar[slot], bytes);
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            if (!ok[i]) continue;
-            const unsigned char* src =
-                static_cast<const unsigned char*>(a.w[ms[i]]) + (size_t)rows[i] * row_bytes;
-            bulk_g2s(slots + slot * stage_bytes + i * row_bytes, src, row_bytes, &bar[slot]);
-        }
-    };
-
-    if (tid == 0) {
-        for (int s = 0; s < stages; ++s) mbar_init(&bar[s], 1);
-        fence_barrier_init();
     }
-    __syncthreads();
-    if (tid == 0) {
-        const int pre = my < stages ? my : stages;
-        for (int s = 0; s < pre; ++s) issue(g0 + s, s);
-    }
-    pdl_launch_dependents();
-    pdl_wait();
 
     // ---- prologue: activation vector into shared memory ------------------------
+    // One vectorised pass stores x*w and accumulates sum(x^2); 1/rms is applied
+    // to the dot products in the epilogue, (W.(x*w))*inv, which keeps the
+    // reduction off the critical path.  Activations are read through L2
+    // (ld.global.cg): another CTA or kernel wrote them.
+    __shared__ float red_ss[kGemvWarps];
     {
-        const float* src = a.x;
         const uint16_t* esrc = nullptr;
-        if (MODE == GM_QKV && a.gather_token) esrc = a.embd + (size_t)a.st->token * K;
+        if (MODE == GM_QKV && a.gather_token) esrc = a.embd + (size_t)token * K;
+        const float4* x4 = reinterpret_cast<const float4*>(a.x);
+        const float4* w4 = a.norm_w ? reinterpret_cast<const float4*>(nws) : nullptr;
+        float4* xs4 = reinterpret_cast<float4*>(xs);
+        const int K4 = K >> 2;
         float ss = 0.f;
-        for (int k = tid * 4; k < K; k += kGemvThreads * 4) {
+#pragma unroll 4
+        for (int k4 = tid; k4 < K4; k4 += kGemvThreads) {
             float4 v;
             if (esrc) {
-                uint2 h = *reinterpret_cast<const uint2*>(esrc + k);
-                float2 l0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-                float2 l1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                const uint2 h = __ldg(reinterpret_cast<const uint2*>(esrc) + k4);
+                const float2 l0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                const float2 l1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
                 v = make_float4(l0.x, l0.y, l1.x, l1.y);
-                if (b == 0) *reinterpret_cast<float4*>(a.x_out + k) = v;
+                if (b == 0) reinterpret_cast<float4*>(a.x_out)[k4] = v;
+            } else if (MODE == GM_RESID && a.attn_part) {
+                // attention output = softmax-weighted merge of the per-split partials
+                // (online-softmax rescaling, as in flash decoding)
+                // all split loads are issued together (fixed trip count, predicated)
+                const int hd = a.hd, h = (k4 * 4) / hd, d = (k4 * 4) - h * hd;
+                const float* pb = a.attn_part + (size_t)h * a.attn_nsplit * (hd + 4);
+                float ms[kMaxAttnSplits], ls[kMaxAttnSplits];
+                float4 pv[kMaxAttnSplits];
+#pragma unroll
+                for (int sp = 0; sp < kMaxAttnSplits; ++sp) {
+                    if (sp < a.attn_nsplit) {
+                        const float* ps = pb + sp * (hd + 4);
+                        ms[sp] = __ldcg(ps + hd);
+                        ls[sp] = __ldcg(ps + hd + 1);
+                        pv[sp] = __ldcg(reinterpret_cast<const float4*>(ps + d));
+                    } else {
+                        ms[sp] = -INFINITY;
+                        ls[sp] = 0.f;
+                        pv[sp] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                float M = -INFINITY;
+#pragma unroll
+                for (int sp = 0; sp < kMaxAttnSplits; ++sp) M = fmaxf(M, ms[sp]);
+                float Ls = 0.f;
+                float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int sp = 0; sp < kMaxAttnSplits; ++sp) {
+                    const float w = (ms[sp] == -INFINITY) ? 0.f : expf(ms[sp] - M);
+                    Ls = fmaf(ls[sp], w, Ls);
+                    o = make_float4(fmaf(pv[sp].x, w, o.x), fmaf(pv[sp].y, w, o.y), fmaf(pv[sp].z, w, o.z),
+                                    fmaf(pv[sp].w, w, o.w));
+                }
+                const float inv = 1.0f / Ls;
+                v = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
             } else {
-                v = *reinterpret_cast<const float4*>(src + k);
+                v = __ldcg(x4 + k4);
             }
-            *reinterpret_cast<float4*>(xs + k) = v;
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-        if (a.norm_w) {
-            __shared__ float red[kGemvWarps];
-            __shared__ float inv_s;
-            ss = warp_sum(ss);
-            if (lane == 0) red[warp] = ss;
-            __syncthreads();
-            if (tid == 0) {
-                float t = 0.f;
-                for (int w = 0; w < kGemvWarps; ++w) t += red[w];
-                // tensor.cpp:675-676: rms = sqrt(ss/n + eps); inv = 1/rms
-                float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps));
-                inv_s = __fdiv_rn(1.0f, rms);
+            if (w4) {
+                const float4 w = w4[k4];
+                v = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
             }
-            __syncthreads();
-            const float inv = inv_s;
-            for (int k = tid; k < K; k += kGemvThreads)
-                xs[k] = __fmul_rn(xs[k], __fmul_rn(inv, a.norm_w[k]));   // x * (inv * w)
+            xs4[k4] = v;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red_ss[warp] = ss;
+    }
+    __syncthreads();
+
+    // ---- main loop: kDepth chunks in flight per warp ---------------------------------
+    const int hsel = (lane >> 2) & 1;   // bank-conflict-free order for the F16 x loads
+    for (int k0 = 0; k0 < g.mine; k0 += kDepth) {
+#pragma unroll
+        for (int j = 0; j < kDepth; ++j) {
+            const int k = k0 + j;
+            if (k >= g.mine) break;
+            const int t = g.t0 + k;
+            const int lrow = t / g.nc, c = t - lrow * g.nc;
+            const int e0 = c * (kChunkBytes / esz);   // first column of the chunk
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (WT == WT_F16) {
+                    const int e = e0 + 256 * i + lane * 8;
+                    if (e < K) {
+                        const float* xp = xs + e;
+                        const float4 p0 = *reinterpret_cast<const float4*>(xp + 4 * hsel);
+                        const float4 p1 = *reinterpret_cast<const float4*>(xp + 4 * (1 - hsel));
+                        if (i & 1) acc1 = dot8_h(buf.v[j][i], hsel ? p1 : p0, hsel ? p0 : p1, acc1);
+                        else acc0 = dot8_h(buf.v[j][i], hsel ? p1 : p0, hsel ? p0 : p1, acc0);
+                    }
+                } else {
+                    const int e = e0 + 512 * i + lane * 16;
+                    if (e < K) {
+                        const float4* xp = reinterpret_cast<const float4*>(xs + e);
+                        acc0 = dot4_i8(buf.v[j][i].x, xp[0], acc0);
+                        acc1 = dot4_i8(buf.v[j][i].y, xp[1], acc1);
+                        acc0 = dot4_i8(buf.v[j][i].z, xp[2], acc0);
+                        acc1 = dot4_i8(buf.v[j][i].w, xp[3], acc1);
+                    }
+                }
+            }
+            // refill this slot with the item kDepth ahead
+            gemv_load<MODE, WT, R>(a, g, k + kDepth, buf.v[j]);
+            const float v = warp_sum((acc0.x + acc0.y) + (acc1.x + acc1.y));
+            if (lane == 0) part[c * g.rows_cap + lrow] = v;
         }
     }
     __syncthreads();
 
-    const int nch = (K + 255) >> 8;
-    const int hsel = (lane >> 2) & 1;   // bank-conflict-free order for the x loads
-    float best_v = -INFINITY;
-    int best_i = 0;
+    // tensor.cpp:675-676: rms = sqrt(ss/n + eps); inv = 1/rms
+    float inv = 1.0f;
+    if (a.norm_w) {
+        float t = 0.f;
+        for (int w = 0; w < kGemvWarps; ++w) t += red_ss[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+    }
 
-    for (int it = 0; it < my; ++it) {
-        const int slot = it % stages;
-        const uint32_t parity = (uint32_t)((it / stages) & 1);
-        if (!mbar_wait_bounded(&bar[slot], parity)) {
-            atomicOr(a.status, kStatusTimeout);
-            return;
+    // ---- epilogue: one thread per unit -----------------------------------------------
+    for (int lu = tid; lu < g.U1 - g.U0; lu += kGemvThreads) {
+        const int gu = g.U0 + lu;
+        float y[R];
+        int ms[R], rows[R];
+        bool valid[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float t = 0.f;
+            for (int c = 0; c < g.nc; ++c) t += part[c * g.rows_cap + lu * R + r];
+            valid[r] = group_row<MODE, R>(a, gu, r, ms[r], rows[r]);
+            const float sc = pre_scale[lu * R + r] * inv;
+            y[r] = (sc == 1.0f) ? t : t * sc;
         }
-        const unsigned char* stg = slots + slot * stage_bytes;
-        float acc[R];
-#pragma unroll
-        for (int i = 0; i < R; ++i) acc[i] = 0.f;
-        for (int c = warp; c < nch; c += kGemvWarps) {
-            const int k = c * 256 + lane * 8;
-            if (k < K) {
-                const float* xp = xs + k;
-                float4 p0 = *reinterpret_cast<const float4*>(xp + 4 * hsel);
-                float4 p1 = *reinterpret_cast<const float4*>(xp + 4 * (1 - hsel));
-                float4 xlo = hsel ? p1 : p0;
-                float4 xhi = hsel ? p0 : p1;
-#pragma unroll
-                for (int i = 0; i < R; ++i)
-                    acc[i] += dot8<WT>(stg + i * row_bytes + k * esz, xlo, xhi);
+        if (MODE == GM_GATEUP) {
+            // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
+            const float gr = fmaxf(y[0], 0.0f);
+            a.y[rows[0]] = __fmul_rn(__fmul_rn(gr, gr), y[1]);
+        } else if (MODE == GM_QKV) {
+            const int half = a.hd >> 1;
+            const int d = rows[0] % a.hd;   // < half
+            const int head = rows[0] / a.hd;
+            float y0 = y[0], y1 = y[1];
+            if (ms[0] < 2) {
+                // NeoX pair (d, d + hd/2), tensor.cpp:918-925
+                const float cs = pre_cos[d];
+                const float sn = pre_sin[d];
+                const float r0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+                const float r1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+                y0 = r0;
+                y1 = r1;
             }
-        }
-        float* pb = part + (it & 1) * kGemvWarps * R;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            float v = warp_sum(acc[i]);
-            if (lane == 0) pb[warp * R + i] = v;
-        }
-        __syncthreads();
-        if (tid == 0 && it + stages < my) issue(g0 + it + stages, slot);
-
-        // ---- epilogue ---------------------------------------------------------
-        const int g = g0 + it;
-        if (MODE == GM_QKV || MODE == GM_GATEUP) {
-            if (tid == 0) {
-                float y[R];
-                int ms[R], rows[R];
-#pragma unroll
-                for (int i = 0; i < R; ++i) {
-                    group_row<MODE, R>(a, g, i, ms[i], rows[i]);
-                    float t = 0.f;
-                    for (int w = 0; w < kGemvWarps; ++w) t += pb[w * R + i];
-                    const float sc = a.row_scale[ms[i]] ? a.row_scale[ms[i]][rows[i]] : a.tscale[ms[i]];
-                    y[i] = (WT == WT_F16 && !a.row_scale[ms[i]]) ? t : t * sc;
-                }
-                if (MODE == GM_GATEUP) {
-                    // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
-                    const float gr = fmaxf(y[0], 0.0f);
-                    a.y[rows[0]] = __fmul_rn(__fmul_rn(gr, gr), y[1]);
-                } else {
-                    const int half = a.hd >> 1;
-                    const int pos = a.st->pos;
-                    const int d = rows[0] % a.hd;            // < half
-                    const int head = rows[0] / a.hd;
-                    float y0 = y[0], y1 = y[1];
-                    if (ms[0] < 2) {
-                        // NeoX pair (d, d + hd/2), tensor.cpp:918-925
-                        const float c = a.rope_cos[(size_t)pos * half + d];
-                        const float s = a.rope_sin[(size_t)pos * half + d];
-                        const float r0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
-                        const float r1 = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
-                        y0 = r0;
-                        y1 = r1;
-                    }
-                    if (ms[0] == 0) {
-                        a.q_out[head * a.hd + d] = y0;
-                        a.q_out[head * a.hd + d + half] = y1;
-                    } else {
-                        float* dst = (ms[0] == 1 ? a.kcache : a.vcache) +
-                                     (size_t)pos * a.nkv * a.hd + head * a.hd + d;
-                        dst[0] = y0;
-                        dst[half] = y1;
-                    }
-                }
+            if (ms[0] == 0) {
+                a.q_out[head * a.hd + d] = y0;
+                a.q_out[head * a.hd + d + half] = y1;
+            } else {
+                float* dst = (ms[0] == 1 ? a.kcache : a.vcache) + (size_t)pos * a.nkv * a.hd +
+                             head * a.hd + d;
+                dst[0] = y0;
+                dst[half] = y1;
             }
-        } else if (tid < R) {
-            int m, row;
-            if (group_row<MODE, R>(a, g, tid, m, row)) {
-                float t = 0.f;
-                for (int w = 0; w < kGemvWarps; ++w) t += pb[w * R + tid];
-                float y;
-                if (WT == WT_F16 && !a.row_scale[0]) y = (a.tscale[0] == 1.0f) ? t : t * a.tscale[0];
-                else y = t * (a.row_scale[0] ? a.row_scale[0][row] : a.tscale[0]);
-                if (MODE == GM_PLAIN) a.y[row] = y;
-                else if (MODE == GM_RESID) a.y[row] = __fadd_rn(a.y[row], y);
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                if (!valid[r]) continue;
+                if (MODE == GM_PLAIN) a.y[rows[r]] = y[r];
+                else if (MODE == GM_RESID) a.y[rows[r]] = __fadd_rn(pre_res[lu * R + r], y[r]);
                 else {
-                    a.y[row] = y;
-                    if (y > best_v) { best_v = y; best_i = row; }
+                    a.y[rows[r]] = y[r];
+                    if (y[r] > best.v) { best.v = y[r]; best.i = rows[r]; }
                 }
             }
         }
     }
+}
 
-    if (MODE == GM_LMHEAD) {
-        __shared__ unsigned long long kbest[R];
-        __syncthreads();
-        if (tid < R) kbest[tid] = (best_v == -INFINITY) ? 0ull : argmax_pack(best_v, best_i);
-        __syncthreads();
-        if (tid == 0) {
-            unsigned long long k = 0;
-            for (int i = 0; i < R; ++i) k = kbest[i] > k ? kbest[i] : k;
-            if (k) atomicMax(&a.st->argmax_key, k);
+// LM-head completion: CTA-wide argmax, global max, and -- in the last CTA to
+// finish -- publication of the step's token and advance of the step state.
+__device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgmax& best) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ unsigned long long kbest[kGemvWarps];
+    unsigned long long key = (best.v == -INFINITY) ? 0ull : argmax_pack(best.v, best.i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+    }
+    if (lane == 0) kbest[warp] = key;
+    __syncthreads();
+    if (tid == 0) {
+        unsigned long long k = 0;
+        for (int w = 0; w < kGemvWarps; ++w) k = kbest[w] > k ? kbest[w] : k;
+        if (k) atomicMax(&a.st->argmax_key, k);
+        __threadfence();
+        const unsigned done = atomicAdd(&a.st->lm_done, 1u);
+        if (done == gridDim.x - 1) {
+            // Last CTA: publish this step's argmax and advance the step state.
             __threadfence();
-            const unsigned done = atomicAdd(&a.st->lm_done, 1u);
-            if (done == gridDim.x - 1) {
-                // Last CTA: publish this step's argmax and advance the step state.
-                __threadfence();
-                const unsigned long long fin = atomicAdd(&a.st->argmax_key, 0ull);
-                a.st->next_token = argmax_index(fin);
-                a.st->max_logit = argmax_value(fin);
-                a.st->token = argmax_index(fin);
-                a.st->pos = a.st->pos + 1;
-                a.st->argmax_key = 0ull;
-                a.st->lm_done = 0u;
-            }
+            const unsigned long long fin = atomicAdd(&a.st->argmax_key, 0ull);
+            a.st->next_token = argmax_index(fin);
+            a.st->max_logit = argmax_value(fin);
+            a.st->token = argmax_index(fin);
+            a.st->pos = a.st->pos + 1;
+            a.st->argmax_key = 0ull;
+            a.st->lm_done = 0u;
         }
     }
+}
+
+// Stand-alone launch of one GEMV phase (the per-op API and tests).
+template <int MODE, int WT, int R>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+stream_gemv_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    ChunkBuf buf;
+    gemv_prefetch<MODE, WT, R>(a, gridDim.x, blockIdx.x, threadIdx.x >> 5, buf);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = (MODE == GM_QKV) ? __ldcg(&a.st->pos) : 0;
+    const int token = (MODE == GM_QKV && a.gather_token) ? __ldcg(&a.st->token) : 0;
+    gemv_stage<MODE, WT, R>(a, smem, gridDim.x, pos);
+    GemvArgmax best{-INFINITY, 0};
+    gemv_run<MODE, WT, R>(a, smem, gridDim.x, pos, token, buf, best);
+    if (MODE == GM_LMHEAD) lmhead_finish(a, best);
 }
 
 }  // namespace tvb

@@ -9,8 +9,10 @@
 // so F32, F16 and INT8 outputs are bit-identical to the reference.
 //
 // B200 mapping: the rank-r delta is FP32 CUDA-core work with a fixed
-// summation order, issued as packed `mul/add.rn.f32x2` (one instruction per two
-// independently rounded lanes).  Each CTA owns ROWS output rows of one tensor;
+// summation order and IEEE-rounded, never-contracted multiplies and adds
+// (__fmul_rn/__fadd_rn).  Packed mul/add.rn.f32x2 would halve the issue count,
+// but ptxas contracts those pairs into fused multiply-adds, which changes the
+// low bit of the delta.  Each CTA owns ROWS output rows of one tensor;
 // its 8 warps stride across the 128-column I2_S blocks of those rows.  One
 // launch covers many tensors through a by-value descriptor table.
 #include "common.cuh"
@@ -101,9 +103,11 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
             }
 #pragma unroll
             for (int i = 0; i < ROWS; ++i) {
-                float2 bb = make_float2(bj[i], bj[i]);
-                acc[i][0] = add2_rn(acc[i][0], mul2_rn(a01, bb));
-                acc[i][1] = add2_rn(acc[i][1], mul2_rn(a23, bb));
+                // __fmul_rn/__fadd_rn are never contracted into an FMA.
+                acc[i][0].x = __fadd_rn(acc[i][0].x, __fmul_rn(a01.x, bj[i]));
+                acc[i][0].y = __fadd_rn(acc[i][0].y, __fmul_rn(a01.y, bj[i]));
+                acc[i][1].x = __fadd_rn(acc[i][1].x, __fmul_rn(a23.x, bj[i]));
+                acc[i][1].y = __fadd_rn(acc[i][1].y, __fmul_rn(a23.y, bj[i]));
             }
         }
         const float2 sf2 = make_float2(D.sf, D.sf);
@@ -113,12 +117,14 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
             if (row >= N) break;
             const int64_t blk = (int64_t)row * nchunks + c;
             uint32_t word = *reinterpret_cast<const uint32_t*>(D.i2s + blk * 32 + byte_off);
-            float2 d01 = mul2_rn(acc[i][0], sf2), d23 = mul2_rn(acc[i][1], sf2);
+            float2 d01 = make_float2(__fmul_rn(acc[i][0].x, sf2.x), __fmul_rn(acc[i][0].y, sf2.y));
+            float2 d23 = make_float2(__fmul_rn(acc[i][1].x, sf2.x), __fmul_rn(acc[i][1].y, sf2.y));
             float2 b01 = make_float2(code_value(word, 0, shift, D.scale),
                                      code_value(word, 1, shift, D.scale));
             float2 b23 = make_float2(code_value(word, 2, shift, D.scale),
                                      code_value(word, 3, shift, D.scale));
-            float2 v01 = add2_rn(b01, d01), v23 = add2_rn(b23, d23);
+            float2 v01 = make_float2(__fadd_rn(b01.x, d01.x), __fadd_rn(b01.y, d01.y));
+            float2 v23 = make_float2(__fadd_rn(b23.x, d23.x), __fadd_rn(b23.y, d23.y));
             const int64_t off = (int64_t)row * K + col;
             if (MODE == kOutF32) {
                 *reinterpret_cast<float4*>(static_cast<float*>(D.dst) + off) =

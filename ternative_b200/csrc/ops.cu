@@ -139,6 +139,25 @@ tvb_status tvb_kv_write(const float* k, const float* v, float* kc, float* vc, in
     return check_launch("kv_write_kernel");
 }
 
+tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* w, int N,
+                      void* stream) {
+    TVB_REQUIRE(y && x && w && w->w, "matmul: null pointer");
+    TVB_REQUIRE(M >= 0 && K > 0 && N > 0, "matmul: bad shape %dx%dx%d", M, K, N);
+    int wt;
+    if (w->dtype == TVB_F16) wt = 0;
+    else if (w->dtype == TVB_I8_ROW || w->dtype == TVB_I8_TENSOR) wt = 1;
+    else return set_error(TVB_ERR_UNSUPPORTED, "matmul: weight dtype %d", (int)w->dtype);
+    const float* rs = w->dtype == TVB_I8_ROW ? w->row_scales : nullptr;
+    const float ts = w->dtype == TVB_I8_TENSOR ? w->tensor_scale : 1.0f;
+    // One streaming GEMV per activation row.
+    for (int m = 0; m < M; ++m) {
+        tvb_status s = standalone_gemv(y + (size_t)m * N, x + (size_t)m * K, w->w, wt, rs, ts, K, N,
+                                       as_stream(stream));
+        if (s != TVB_OK) return s;
+    }
+    return TVB_OK;
+}
+
 tvb_status tvb_attention_decode(const float* q, const float* kc, const float* vc, int kv_len, float* out,
                                 int nh, int nkv, int hd, float scale, void* stream) {
     return standalone_attention(q, kc, vc, kv_len, out, nh, nkv, hd, scale, as_stream(stream));

@@ -113,10 +113,11 @@ def test_kv_write_and_attention(ctx_backend, restated, kv_len):
     dv[: kv_len - 1] = T(vc[:-1])
     # the last row goes through kv_write at pos = kv_len - 1
     from ternative_b200._lib import call
-    call("tvb_kv_write", T(kc[-1]).data_ptr(), T(vc[-1]).data_ptr(), dk.data_ptr(), dv.data_ptr(),
+    k_last, v_last, dq = T(kc[-1]), T(vc[-1]), T(q)   # keep the device copies alive
+    call("tvb_kv_write", k_last.data_ptr(), v_last.data_ptr(), dk.data_ptr(), dv.data_ptr(),
          kv_len - 1, nkv * hd, 0)
     out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
-    call("tvb_attention_decode", T(q).data_ptr(), dk.data_ptr(), dv.data_ptr(), kv_len,
+    call("tvb_attention_decode", dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), kv_len,
          out.data_ptr(), nh, nkv, hd, float(1 / np.sqrt(hd)), 0)
     close(host(out), restated.attention_decode(q, kc, vc, kv_len, nh, nkv, hd), rtol=1e-4)
 
