@@ -24,6 +24,7 @@ max over ranks.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import sys
@@ -51,7 +52,7 @@ def peaks():
 class ClockSampler:
     """Samples SM clock and clock-event reasons via NVML (read-only) while running."""
 
-    def __init__(self, cuda_index: int = 0, period: float = 0.2):
+    def __init__(self, cuda_index: int = 0, period: float = 0.02):
         self.period = period
         self.samples = []
         self.reasons = set()
@@ -110,6 +111,23 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+def profiled_traffic(kernel: str, layers: int):
+    """DRAM bytes (read + write) per launch of `kernel`, from the ncu summary
+    committed under profiles/ (`traffic_bytes_per_layer:` and
+    `traffic_bytes_fixed:` lines, scaled to `layers`).  None when absent."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}.md")
+    if not os.path.exists(path):
+        return None
+    vals = {}
+    for line in open(path):
+        for key in ("traffic_bytes_per_layer:", "traffic_bytes_fixed:"):
+            if line.strip().startswith(key):
+                vals[key] = float(line.split(":", 1)[1].strip().split()[0])
+    if len(vals) != 2:
+        return None
+    return vals["traffic_bytes_fixed:"] + layers * vals["traffic_bytes_per_layer:"]
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -199,6 +217,9 @@ def run_ours(args, world, rank, local):
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     cfg = SHAPES[args.config]
+    if args.layers:
+        # profiling only: the same shapes with fewer layers (smaller device footprint)
+        cfg = dataclasses.replace(cfg, num_layers=args.layers)
     synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0)
     be = CUDABackend()
     if args.only == "merge":
@@ -282,32 +303,44 @@ def run_ours(args, world, rank, local):
     e2e = {"value": world * args.steps / (e2e_ms / 1e3), "unit": "tok/s",
            "h2d_bytes_per_step": 8, "d2h_bytes_per_step": cfg.vocab_size * 4 + 4 * 76}
 
-    # ---- dominant kernel: streaming F16 GEMV, gate shape, rotating layers ---------
-    N, K = proj_shape(cfg, "w_gate")
-    x = torch.randn(K, device="cuda")
-    y = torch.empty(N, device="cuda")
-    ws = [m.weights[li]["w_gate"] for li in range(cfg.num_layers)]
-    for i in range(3):
-        be.gemv_d2d(y, x, ws[i], K, N)
-    be.sync_d()
-    reps = 3 * cfg.num_layers
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record(stream)
-    for i in range(reps):
-        be.gemv_d2d(y, x, ws[i % len(ws)], K, N)
-    g1.record(stream)
-    g1.synchronize()
-    gemv_us = g0.elapsed_time(g1) * 1e3 / reps
-    gemv_bytes = N * K * 2 + 4 * K + 4 * N
+    # ---- roofline of the dominant kernel: the decode-step kernel (one launch per
+    # token).  Algorithmic bytes per launch: every projection weight (F16), the
+    # tied lm_head, the KV rows read by attention and written for this token.
     hbm, peak_kind = peaks()
-    achieved = gemv_bytes / (gemv_us * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "kernel": "stream_gemv_kernel<PLAIN,F16> 6912x2560",
-                "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "peak_kind": peak_kind, "bytes_per_launch": gemv_bytes, "us_per_launch": gemv_us,
-                "traffic": None}
-    step_bytes = sum(2 * proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) \
+    pos_mid = args.prompt + args.warmup + args.steps // 2
+    Hk = cfg.num_kv_heads * cfg.head_dim
+    weight_bytes = sum(2 * proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) \
         * cfg.num_layers + cfg.vocab_size * cfg.hidden_size * 2
-    step_gbs = step_bytes / (ms_per_step * 1e-3) / 1e9
+    kv_bytes = cfg.num_layers * (2 * pos_mid * Hk * 4 + 2 * Hk * 4)
+    step_bytes = weight_bytes + kv_bytes
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+    traffic = profiled_traffic("decode_step_kernel", cfg.num_layers)
+    roofline = {"bound": "hbm", "kernel": "decode_step_kernel (whole decode step)",
+                "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "peak_kind": peak_kind, "bytes_per_launch": step_bytes,
+                "us_per_launch": ms_per_step * 1e3, "traffic": traffic}
+
+    # ---- the stand-alone streaming GEMV (gemv_d2d) on the GEMV-sweep shapes,
+    # rotating over every layer's copy so the weights come from HBM ------------
+    gemv = {}
+    for name in ("wk", "wq", "w_gate", "w_down"):
+        N, K = proj_shape(cfg, name)
+        x = torch.randn(K, device="cuda")
+        y = torch.empty(N, device="cuda")
+        ws = [m.weights[li][name] for li in range(cfg.num_layers)]
+        for i in range(3):
+            be.gemv_d2d(y, x, ws[i], K, N)
+        be.sync_d()
+        reps = 2 * cfg.num_layers
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(reps):
+            be.gemv_d2d(y, x, ws[i % len(ws)], K, N)
+        g1.record(stream)
+        g1.synchronize()
+        us = g0.elapsed_time(g1) * 1e3 / reps
+        gb = (N * K * 2 + 4 * K + 4 * N) / (us * 1e-6) / 1e9
+        gemv[f"{N}x{K}_f16"] = {"us": us, "GB/s": gb, "frac": gb / hbm}
 
     # ---- load-time merge: all 210 projections, F16 and per-row INT8 ---------------
     merge = {}
@@ -367,11 +400,9 @@ def run_ours(args, world, rank, local):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16-weights/f32-compute",
             "data": "synthetic", "config": config_block(args, cfg),
-            "roofline": roofline,
-            "step_roofline": {"bytes_per_step": step_bytes, "achieved_GBps": step_gbs,
-                              "frac": step_gbs / hbm, "peak": hbm, "peak_kind": peak_kind},
+            "roofline": roofline, "gemv_standalone": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": (5 * cfg.num_layers + 1) * args.steps,
+            "gpu_launches": args.steps,   # one decode_step_kernel launch per token
             "clocks": clk.report(), "merge": merge,
         }
         print(json.dumps(line), flush=True)
@@ -392,9 +423,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["decode", "gemv", "merge"], default=None,
                     help="profiling: run only W+K launches of one part, print nothing")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling with --only: use this many layers of the shape")
     args = ap.parse_args()
     if args.warmup < 3 and args.only is None:
         ap.error("--warmup must be >= 3")
+    if args.layers and args.only is None:
+        ap.error("--layers is for profiling runs (--only)")
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
