@@ -155,6 +155,21 @@ typedef struct {
 tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* w, int N,
                       void* stream);
 
+/* Allocation-free split-KV decode attention.  No counterpart in the
+ * reference: for callers that cannot allocate device memory when they call
+ * (a host that hands its device memory to its own pool at start-up, or a
+ * thread that must not risk the device synchronisation cudaMalloc/cudaFree
+ * can imply).  Same arguments and result as tvb_attention_decode; its split
+ * partials live in a static device array inside this library (64 heads x 8
+ * splits x head_dim 128, 264 KiB, held by every GPU that loads the library
+ * until the process exits).  n_heads > 64 is rejected with TVB_ERR_INVALID.
+ * The first call on a device looks up that array's device address (make it
+ * with the device current, before any stream capture).  Every call shares the
+ * array: calls that overlap on the GPU (other streams, other threads) race. */
+tvb_status tvb_attention_decode_noalloc(const float* q, const float* k_cache, const float* v_cache,
+                                        int kv_len, float* out, int n_heads, int n_kv_heads,
+                                        int head_dim, float scale, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Context: the state CUDABackend::Impl owns (ops_cuda.cu:309-591):         */
 /* stream, activation buffers, KV cache, pinned staging, workspace, plus    */

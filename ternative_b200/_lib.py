@@ -92,6 +92,7 @@ _SIGS = {
     "tvb_kv_write": [_P, _P, _P, _P, _I, _I, _P],
     "tvb_attention_decode": [_P, _P, _P, _I, _P, _I, _I, _I, _F, _P],
     "tvb_matmul": [_P, _P, _I, _I, C.POINTER(Weight), _I, _P],
+    "tvb_attention_decode_noalloc": [_P, _P, _P, _I, _P, _I, _I, _I, _F, _P],
     "tvb_context_create": [C.POINTER(ModelConfig), C.POINTER(C.c_void_p)],
     "tvb_context_destroy": [_P],
     "tvb_context_stream": [_P],

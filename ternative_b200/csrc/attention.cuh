@@ -28,7 +28,7 @@ struct AttnArgs {
 };
 
 // hd == 128: each lane owns 4 consecutive dimensions.
-__global__ void __launch_bounds__(kAttnThreads)
+static __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const __grid_constant__ AttnArgs a) {
     pdl_launch_dependents();
     pdl_wait();
