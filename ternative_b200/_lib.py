@@ -10,7 +10,8 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libtvb200.so")
+# TVB200_LIB selects another build of the library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("TVB200_LIB") or os.path.join(HERE, "libtvb200.so")
 
 # tvb_status
 TVB_OK = 0

@@ -128,19 +128,23 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
     bool ok = true;
     for (int p = 0; p < n_phases && ok; ++p) {
         const Phase& ph = desc[p & 1];
+        // The next phase's descriptor.  Its buffer held phase p - 1, which
+        // nothing reads any more; the GEMV prologue's __syncthreads (or the
+        // one below) publishes it.
+        const Phase& next = desc[(p + 1) & 1];
+        if (p + 1 < n_phases) load_phase(&desc[(p + 1) & 1], &phases[p + 1]);
         if (ph.kind == PK_GEMV) {
             GemvArgmax best{-INFINITY, 0};
             phase_gemv(ph, smem, G, pos, token, buf, best);
             if (ph.mode == GM_LMHEAD) lmhead_finish(ph.g, best);
-        } else if (b < ph.at.nkv * ph.at.nsplit) {
-            attn_item(ph.at, b, smem + 1024, pos);
+        } else {
+            __syncthreads();
+            if (b < ph.at.nkv * ph.at.nsplit) attn_item(ph.at, b, smem + 1024, pos);
         }
         if (p + 1 < n_phases) {
             grid_arrive(st);   // this phase's outputs are written (includes __syncthreads)
             // input-independent work for the next phase overlaps the barrier
-            load_phase(&desc[(p + 1) & 1], &phases[p + 1]);
-            __syncthreads();
-            phase_prepare(desc[(p + 1) & 1], smem, G, b, warp, pos, buf);
+            phase_prepare(next, smem, G, b, warp, pos, buf);
             ok = grid_wait(st, (unsigned)(p + 1) * (unsigned)G);
         }
     }
