@@ -30,6 +30,12 @@ tvb_status check_launch(const char* what);
         if (!(cond)) return ::tvb::set_error(TVB_ERR_INVALID, __VA_ARGS__);           \
     } while (0)
 
+#define TVB_TRY(x)                   \
+    do {                             \
+        tvb_status _s = (x);         \
+        if (_s != TVB_OK) return _s; \
+    } while (0)
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline int num_sms() {

@@ -10,6 +10,7 @@
 // (StepState), so the same graph serves every position and greedy decode can
 // chain steps without the host.
 #include "decode.cuh"
+#include "prefill.h"
 
 #include <algorithm>
 #include <cmath>
@@ -18,11 +19,6 @@
 #include <new>
 #include <vector>
 
-#define TVB_TRY(x)                   \
-    do {                             \
-        tvb_status _s = (x);         \
-        if (_s != TVB_OK) return _s; \
-    } while (0)
 
 namespace tvb {
 
@@ -158,6 +154,15 @@ struct tvb_context {
     cudaGraphExec_t g_step = nullptr;    // layers + lm_head
     cudaGraphExec_t g_layers = nullptr;  // layers only (prefill rows before the last)
     bool dirty = true;
+    // batched-prefill workspace (allocated by the first tvb_prefill): rows of
+    // the prompt chunk in flight, F16 hi/lo activation planes for the tensor
+    // cores, and the F16 widening of one projection group of an INT8 layer
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_h = nullptr;
+    uint16_t *pf_xh = nullptr, *pf_xl = nullptr;
+    int *pf_exp = nullptr, *pf_tok = nullptr;
+    uint16_t* pf_w16 = nullptr;
+    size_t pf_w16_elems = 0;
 };
 
 namespace {
@@ -358,6 +363,146 @@ tvb_status check_status(tvb_context* c) {
     return set_error(TVB_ERR_CUDA, "device status 0x%x", s);
 }
 
+// ---- batched prefill (Model::forward_prefill, model.cpp:1139-1234) -----------------
+
+tvb_status pf_workspace(tvb_context* c) {
+    if (c->pf_cap) return TVB_OK;
+    const int cap = std::min(c->cfg.max_prefill, c->cfg.max_seq_len);
+    const size_t kmax = (size_t)std::max(c->H, std::max(c->Hq, c->I));
+    struct { void** p; size_t b; } allocs[] = {
+        {(void**)&c->pf_x, (size_t)cap * c->H * 4},   {(void**)&c->pf_q, (size_t)cap * c->Hq * 4},
+        {(void**)&c->pf_attn, (size_t)cap * c->Hq * 4}, {(void**)&c->pf_h, (size_t)cap * c->I * 4},
+        {(void**)&c->pf_xh, cap * kmax * 2},          {(void**)&c->pf_xl, cap * kmax * 2},
+        {(void**)&c->pf_exp, (size_t)cap * 4},        {(void**)&c->pf_tok, (size_t)c->cfg.max_seq_len * 4},
+    };
+    for (auto& a : allocs) TVB_TRY(alloc_dev(a.p, a.b));
+    c->pf_cap = cap;
+    return TVB_OK;
+}
+
+// One projection operand; INT8 weights are widened to F16 into the scratch at
+// `off` (exact), their scales applied by the GEMM epilogue.
+tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size_t& off, PfMatrix& m) {
+    m.rows = rows;
+    m.row_scales = nullptr;
+    m.scale = 1.0f;
+    if (w.dtype == TVB_F16) {
+        m.w = static_cast<const uint16_t*>(w.w);
+        return TVB_OK;
+    }
+    TVB_REQUIRE(w.dtype == TVB_I8_ROW || w.dtype == TVB_I8_TENSOR, "prefill: weight dtype %d", (int)w.dtype);
+    const size_t n = (size_t)rows * K;
+    if (!c->pf_w16) {
+        // the largest projection group of a layer: gate + up, q + k + v, o or down
+        const size_t need = std::max({(size_t)2 * c->I * c->H, (size_t)(c->Hq + 2 * c->Hk) * c->H,
+                                      (size_t)c->H * c->Hq, (size_t)c->H * c->I});
+        TVB_TRY(alloc_dev((void**)&c->pf_w16, need * 2));
+        c->pf_w16_elems = need;
+    }
+    TVB_REQUIRE(off + n <= c->pf_w16_elems, "prefill: INT8 widening scratch too small");
+    TVB_TRY(pf_i8_to_f16(static_cast<const int8_t*>(w.w), n, c->pf_w16 + off, c->stream));
+    m.w = c->pf_w16 + off;
+    off += n;
+    if (w.dtype == TVB_I8_ROW) m.row_scales = w.row_scales;
+    else m.scale = w.tensor_scale;
+    return TVB_OK;
+}
+
+// The prompt in chunks of the workspace's rows: per layer RMSNorm -> q/k/v on
+// the tensor cores with RoPE and KV append fused -> causal attention over every
+// KV row so far -> sub-norm -> o_proj + residual -> ffn_norm -> gate/up with
+// relu^2 * up fused -> sub-norm -> down + residual; then output_norm + lm_head
+// + argmax of the last row, leaving the step state at (pos S, argmax).
+tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
+    TVB_TRY(pf_workspace(c));
+    const cudaStream_t st = c->stream;
+    const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
+    const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
+    for (int i = 0; i < S; ++i) c->h_io[i] = tokens[i];
+    TVB_CUDA(cudaMemcpyAsync(c->pf_tok, c->h_io, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+    int last_rows = 0;
+    for (int p0 = 0; p0 < S; p0 += c->pf_cap) {
+        const int n = std::min(c->pf_cap, S - p0);
+        last_rows = n;
+        TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), c->pf_tok + p0, n, H, c->pf_x, st));
+        for (int l = 0; l < c->L; ++l) {
+            const tvb_layer_weights& lw = c->layers[l];
+            float* kl = c->kcache + (size_t)l * c->cfg.max_seq_len * Hk;
+            float* vl = c->vcache + (size_t)l * c->cfg.max_seq_len * Hk;
+            size_t off = 0;
+            PfGemm g;
+            g.S = n;
+            g.xh = c->pf_xh;
+            g.xl = c->pf_xl;
+            g.row_exp = c->pf_exp;
+            g.status = &c->st->status;
+            // attn_norm -> q, k, v -> RoPE -> KV rows p0 ..
+            TVB_TRY(pf_norm_split(c->pf_x, lw.attn_norm, n, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            g.mode = PF_QKV;
+            g.K = H;
+            TVB_TRY(pf_operand(c, lw.wq, Hq, H, off, g.m[0]));
+            TVB_TRY(pf_operand(c, lw.wk, Hk, H, off, g.m[1]));
+            TVB_TRY(pf_operand(c, lw.wv, Hk, H, off, g.m[2]));
+            g.nh = c->cfg.num_heads;
+            g.nkv = c->cfg.num_kv_heads;
+            g.hd = hd;
+            g.pos0 = p0;
+            g.q_out = c->pf_q;
+            g.kcache = kl;
+            g.vcache = vl;
+            g.rope_cos = c->rope_cos;
+            g.rope_sin = c->rope_sin;
+            TVB_TRY(pf_gemm(g, st));
+            TVB_TRY(pf_attention(c->pf_q, kl, vl, n, p0, g.nh, g.nkv, hd, scale, c->pf_attn, st));
+            // attn_sub_norm -> o_proj -> residual
+            TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, n, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            off = 0;
+            g.mode = PF_RESID;
+            g.K = Hq;
+            TVB_TRY(pf_operand(c, lw.wo, H, Hq, off, g.m[0]));
+            g.y = c->pf_x;
+            g.ldy = H;
+            TVB_TRY(pf_gemm(g, st));
+            // ffn_norm -> gate/up -> relu^2 * up
+            TVB_TRY(pf_norm_split(c->pf_x, lw.ffn_norm, n, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            off = 0;
+            g.mode = PF_GATEUP;
+            g.K = H;
+            TVB_TRY(pf_operand(c, lw.w_gate, I, H, off, g.m[0]));
+            TVB_TRY(pf_operand(c, lw.w_up, I, H, off, g.m[1]));
+            g.y = c->pf_h;
+            g.ldy = I;
+            TVB_TRY(pf_gemm(g, st));
+            // ffn_sub_norm -> down -> residual
+            TVB_TRY(pf_norm_split(c->pf_h, lw.ffn_sub_norm, n, I, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            off = 0;
+            g.mode = PF_RESID;
+            g.K = I;
+            TVB_TRY(pf_operand(c, lw.w_down, H, I, off, g.m[0]));
+            g.y = c->pf_x;
+            g.ldy = H;
+            TVB_TRY(pf_gemm(g, st));
+        }
+    }
+    // output_norm + lm_head + argmax of the last row (the decode step's last
+    // phase as a stand-alone launch); it advances the step state to (S, argmax)
+    c->h_io[S] = S - 1;
+    c->h_io[S + 1] = tokens[S - 1];
+    TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io + S, 8, cudaMemcpyHostToDevice, st));
+    GemvArgs a = {};
+    a.w[0] = c->tok_embd;
+    a.tscale[0] = 1.0f;
+    a.N = c->V;
+    a.K = H;
+    a.x = c->pf_x + (size_t)(last_rows - 1) * H;
+    a.norm_w = c->output_norm;
+    a.eps = eps;
+    a.y = c->e_logits;
+    a.st = c->st;
+    a.status = &c->st->status;
+    return launch_gemv<GM_LMHEAD, WT_F16, 1>(a, st, false);
+}
+
 }  // namespace
 
 extern "C" {
@@ -456,7 +601,9 @@ tvb_status tvb_context_destroy(tvb_context* c) {
     if (c->g_layers) cudaGraphExecDestroy(c->g_layers);
     void* dev[] = {c->d_x, c->d_norm, c->d_q, c->d_k, c->d_v, c->d_gate, c->d_up, c->e_x, c->e_q,
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
-                   c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases};
+                   c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
+                   c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
+                   c->pf_w16};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
@@ -619,14 +766,9 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
     for (int i = 0; i < S; ++i)
         TVB_REQUIRE(tokens[i] >= 0 && tokens[i] < c->V, "prefill: token[%d]=%d outside vocab", i, tokens[i]);
     TVB_TRY(ensure_graphs(c));
-    // Row-at-a-time causal prefill: row s attends to KV rows [0, s], the same
-    // function as the batched forward_prefill (model.cpp:1084 kv_len = s + 1).
-    for (int s = 0; s < S; ++s) {
-        c->h_io[2 * s] = s;
-        c->h_io[2 * s + 1] = tokens[s];
-        TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io + 2 * s, 8, cudaMemcpyHostToDevice, c->stream));
-        TVB_CUDA(cudaGraphLaunch(s + 1 < S ? c->g_layers : c->g_step, c->stream));
-    }
+    // the pinned staging is about to be rewritten: let earlier copies from it finish
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_TRY(prefill_batched(c, tokens, S));
     TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
     if (last_logits)
         TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));

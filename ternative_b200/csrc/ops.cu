@@ -3,8 +3,13 @@
 // step does not use these; they keep the reference's call-by-call interface
 // available to a host that drives the layer loop itself.
 #include "common.cuh"
+#include "prefill.h"
 
 namespace tvb {
+
+// tvb_matmul takes the tensor-core GEMM from this many activation rows on
+// (below it, one streaming GEMV per row reads the weights fewer times).
+constexpr int kMatmulTensorRows = 8;
 
 tvb_status standalone_gemv(float* y, const float* x, const void* W, int wt, const float* row_scales,
                            float tscale, int K, int N, cudaStream_t st);
@@ -149,6 +154,42 @@ tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* 
     else return set_error(TVB_ERR_UNSUPPORTED, "matmul: weight dtype %d", (int)w->dtype);
     const float* rs = w->dtype == TVB_I8_ROW ? w->row_scales : nullptr;
     const float ts = w->dtype == TVB_I8_TENSOR ? w->tensor_scale : 1.0f;
+    const cudaStream_t st = as_stream(stream);
+    if (M >= kMatmulTensorRows && K % 64 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(w->w) & 15) == 0) {
+        // Batched rows: one tensor-core GEMM.  x is split into F16 hi/lo planes
+        // (with a power-of-two row scale) in stream-ordered scratch; INT8
+        // weights are widened to F16 there too.
+        const size_t plane = (size_t)M * K;
+        const size_t wide = wt ? (size_t)N * K : 0;
+        unsigned char* buf = nullptr;
+        const size_t bytes = (2 * plane + wide) * 2 + (size_t)M * 4 + 256;
+        TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&buf), bytes, st));
+        uint16_t* xh = reinterpret_cast<uint16_t*>(buf);
+        uint16_t* xl = xh + plane;
+        uint16_t* w16 = xl + plane;
+        int* ex = reinterpret_cast<int*>(w16 + wide);
+        tvb_status s = pf_norm_split(x, nullptr, M, K, 0.f, xh, xl, ex, st);
+        if (s == TVB_OK && wt) s = pf_i8_to_f16(static_cast<const int8_t*>(w->w), wide, w16, st);
+        if (s == TVB_OK) {
+            PfGemm g;
+            g.mode = PF_STORE;
+            g.S = M;
+            g.K = K;
+            g.xh = xh;
+            g.xl = xl;
+            g.row_exp = ex;
+            g.m[0].w = wt ? w16 : static_cast<const uint16_t*>(w->w);
+            g.m[0].rows = N;
+            g.m[0].row_scales = rs;
+            g.m[0].scale = ts;
+            g.y = y;
+            g.ldy = N;
+            s = pf_gemm(g, st);
+        }
+        cudaFreeAsync(buf, st);
+        return s;
+    }
     // One streaming GEMV per activation row.
     for (int m = 0; m < M; ++m) {
         tvb_status s = standalone_gemv(y + (size_t)m * N, x + (size_t)m * K, w->w, wt, rs, ts, K, N,

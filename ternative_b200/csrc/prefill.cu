@@ -1,0 +1,786 @@
+// Batched prefill kernels for sm_100a (see prefill.h).
+//
+// pf_gemm_kernel: one CTA computes a 128-token x 256-weight-row tile of
+// acc = X . W^T.  Warp roles: warp 0 lane 0 issues TMA loads into a 3-stage
+// shared-memory ring (128B-swizzled, K-major tiles: the activation planes hi/lo
+// [128 tokens][64 k] and the weight tile [256 rows][64 k], loaded as two
+// 128-row halves so one tile can pair rows of different matrices: gate with
+// up, q/k/v heads); warp 1 lane 0 issues tcgen05.mma (M=128, N=256, K=16,
+// F16 x F16 -> F32 in TMEM) and frees each stage with tcgen05.commit; warp 2
+// owns the TMEM allocation; warps 4-7 read the accumulator back with
+// tcgen05.ld (warp w sees TMEM lanes 32*(w%4) .. +31 = its 32 tokens) and run
+// the fused epilogue.  Every mbarrier wait is bounded: a stall of about a
+// second sets the status word and the CTA leaves through the normal exit path
+// (TMEM freed, outstanding TMA writes waited for).
+//
+// Activations reach the tensor cores as two F16 planes, x = (hi + lo) * 2^e
+// with a power-of-two row exponent e chosen so the row's largest magnitude
+// lies in [2^14, 2^15): hi carries 11 significant bits, lo the next 11, so
+// (hi + lo) reproduces the F32 activations to about 2^-22 of the row's largest
+// element and the products with exact F16 weights accumulate in F32, as the
+// reference's F32 x F16 GEMV/GEMM does (cuda/ops_cuda.cu:46-71, 269-294).
+#include "prefill.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "stream.cuh"
+
+namespace tvb {
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA primitives
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 2-D tiled TMA load global -> shared (no multicast), completion on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte
+// swizzling: rows of 128 B, 8-row groups 1024 B apart (stride byte offset),
+// leading byte offset unused for swizzled K-major layouts (encoded 1),
+// descriptor version 1 (bits 46-47), swizzle mode 2 = 128B (bits 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D F32 (bits 4-5 = 1), A and B F16 (0),
+// both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t pf_idesc(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma this thread issued has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive F32 columns of this thread's TMEM lane (warp-collective).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// GEMM kernel
+// ---------------------------------------------------------------------------
+constexpr int kPfBM = 128;                         // tokens per tile (MMA M, TMEM lanes)
+constexpr int kPfBN = 256;                         // weight rows per tile (MMA N, TMEM columns)
+constexpr int kPfBK = 64;                          // k per stage: 128 B of F16 = one swizzle row
+constexpr int kPfStages = 3;
+constexpr int kPfThreads = 256;
+constexpr int kPfPlane = kPfBM * kPfBK * 2;        // 16 KB activation plane per stage
+constexpr int kPfHalf = 128 * kPfBK * 2;           // 16 KB weight half-tile per stage
+constexpr int kPfStage = 2 * kPfPlane + 2 * kPfHalf;
+constexpr int kPfSmem = kPfStages * kPfStage + 1024 + 256;   // + alignment slack + barriers
+constexpr uint32_t kPfTmemCols = 256;
+
+struct PfMaps {
+    CUtensorMap xh, xl, w[3];
+};
+
+struct PfArgs {
+    int mode, S, K, nk, use_lo;
+    int rows[3];
+    const float* row_scales[3];
+    float scale[3];
+    const int* row_exp;   // per token: activations are (hi + lo) * 2^row_exp
+    float* y;
+    int ldy;
+    int nh, nkv, hd, pos0;
+    float* q_out;
+    float* kcache;
+    float* vcache;
+    const float* rope_cos;
+    const float* rope_sin;
+    unsigned* status;
+};
+
+// Which matrix and first row feed half `h` (128 rows) of column tile `tile`.
+__host__ __device__ inline bool pf_half(const PfArgs& a, int tile, int h, int& mi, int& row) {
+    if (a.mode == PF_GATEUP) {
+        mi = h;
+        row = tile * 128;
+        return row < a.rows[h];
+    }
+    if (a.mode == PF_QKV) {
+        int slot = tile * 2 + h;
+        if (slot < a.nh) { mi = 0; row = slot * 128; return true; }
+        slot -= a.nh;
+        if (slot < a.nkv) { mi = 1; row = slot * 128; return true; }
+        slot -= a.nkv;
+        mi = 2;
+        row = slot * 128;
+        return slot < a.nkv;
+    }
+    mi = 0;
+    row = tile * kPfBN + h * 128;
+    return row < a.rows[0];
+}
+
+__device__ __forceinline__ float pf_row_scale(const PfArgs& a, int mi, int n) {
+    return a.row_scales[mi] ? __ldg(a.row_scales[mi] + n) : a.scale[mi];
+}
+
+// Store 32 consecutive values (vector stores when aligned), optionally adding
+// to what is there; only the first `count` are written.
+__device__ __forceinline__ void pf_store32(float* dst, const float (&v)[32], int count, bool add) {
+    if (count >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (add) {
+                const float4 p = d4[j];
+                o = make_float4(__fadd_rn(p.x, o.x), __fadd_rn(p.y, o.y), __fadd_rn(p.z, o.z), __fadd_rn(p.w, o.w));
+            }
+            d4[j] = o;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < count) dst[j] = add ? __fadd_rn(dst[j], v[j]) : v[j];
+    }
+}
+
+__device__ __forceinline__ void pf_fail(const PfArgs& a, volatile int* abort_flag) {
+    *abort_flag = 1;
+    if (a.status) atomicOr(a.status, kStatusTimeout);
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfArgs a) {
+    extern __shared__ unsigned char pf_smem_raw[];
+    const uint32_t raw = smem_u32(pf_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;   // 128B-swizzled tiles want 1024-B alignment
+    unsigned char* smem = pf_smem_raw + (base - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPfStages * kPfStage);
+    uint64_t* empty = full + kPfStages;
+    uint64_t* done = empty + kPfStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued = const_cast<int*>(abort_flag) + 1;     // k-blocks requested by the producer
+    int* consumed = issued + 1;                         // k-blocks the MMA warp saw land
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x, s0 = blockIdx.y * kPfBM;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPfStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        *issued = 0;
+        *consumed = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kPfTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int mi[2], row[2];
+    bool hv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) hv[h] = pf_half(a, tile, h, mi[h], row[h]);
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: TMA ring ------------------------------------------------------
+        prefetch_tmap(&maps.xh);
+        if (a.use_lo) prefetch_tmap(&maps.xl);
+        const uint32_t bytes =
+            (uint32_t)(kPfPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
+        int kb = 0;
+        for (; kb < a.nk; ++kb) {
+            const int s = kb % kPfStages, r = kb / kPfStages;
+            if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
+                pf_fail(a, abort_flag);
+                break;
+            }
+            if (*abort_flag) break;
+            const uint32_t st = base + (uint32_t)(s * kPfStage);
+            mbar_expect_tx(&full[s], bytes);
+            tma_load_2d(st, &maps.xh, kb * kPfBK, s0, &full[s]);
+            if (a.use_lo) tma_load_2d(st + kPfPlane, &maps.xl, kb * kPfBK, s0, &full[s]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (hv[h]) tma_load_2d(st + 2 * kPfPlane + h * kPfHalf, &maps.w[mi[h]], kb * kPfBK, row[h], &full[s]);
+        }
+        *issued = kb;
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----------------------------------------------------------------
+        constexpr uint32_t idesc = pf_idesc(kPfBM, kPfBN);
+        int kb = 0;
+        for (; kb < a.nk; ++kb) {
+            const int s = kb % kPfStages, r = kb / kPfStages;
+            if (!mbar_wait_bounded(&full[s], (uint32_t)(r & 1))) {
+                pf_fail(a, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t st = base + (uint32_t)(s * kPfStage);
+#pragma unroll
+            for (int kk = 0; kk < kPfBK / 16; ++kk) {
+                const uint64_t bdesc = sw128_desc(st + 2 * kPfPlane + kk * 32);
+                tc_mma(tmem, sw128_desc(st + kk * 32), bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                if (a.use_lo) tc_mma(tmem, sw128_desc(st + kPfPlane + kk * 32), bdesc, idesc, 1u);
+            }
+            tc_commit(&empty[s]);   // stage s is free once these MMAs have read it
+        }
+        *consumed = kb;
+        tc_commit(done);            // accumulator complete (or the MMAs issued so far)
+    } else if (warp >= 4) {
+        // ---- epilogue ------------------------------------------------------------------
+        const int q = warp & 3;
+        const int s = s0 + 32 * q + lane;
+        const bool srow = s < a.S;
+        const bool ok = mbar_wait_bounded(done, 0u);
+        tc_fence_after();
+        if (!ok) pf_fail(a, abort_flag);
+        if (ok && !*abort_flag) {
+            const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+            const float e2 = (srow && a.row_exp) ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
+            uint32_t r0[32], r1[32];
+            float v0[32], v1[32];
+            if (a.mode == PF_GATEUP) {
+                // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
+                for (int c = 0; c < 4; ++c) {
+                    __syncwarp();
+                    tmem_ld32(trow + c * 32, r0);
+                    tmem_ld32(trow + 128 + c * 32, r1);
+                    tmem_wait_ld();
+                    const int n0 = row[0] + c * 32;
+                    if (srow && hv[0] && hv[1] && n0 < a.rows[0]) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = min(n0 + j, a.rows[0] - 1);
+                            const float g = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, 0, n));
+                            const float u = __fmul_rn(__uint_as_float(r1[j]) * e2, pf_row_scale(a, 1, n));
+                            const float gr = fmaxf(g, 0.0f);
+                            v0[j] = __fmul_rn(__fmul_rn(gr, gr), u);
+                        }
+                        pf_store32(a.y + (size_t)s * a.ldy + n0, v0, a.rows[0] - n0, false);
+                    }
+                }
+            } else if (a.mode == PF_QKV) {
+                const int half = a.hd >> 1;   // 64
+                for (int h = 0; h < 2; ++h) {
+                    const int head = row[h] / a.hd;
+                    for (int c = 0; c < 2; ++c) {
+                        __syncwarp();
+                        tmem_ld32(trow + h * 128 + c * 32, r0);
+                        tmem_ld32(trow + h * 128 + half + c * 32, r1);
+                        tmem_wait_ld();
+                        if (!(srow && hv[h])) continue;
+                        const int pos = a.pos0 + s;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int d = c * 32 + j;
+                            float y0 = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, mi[h], row[h] + d));
+                            float y1 = __fmul_rn(__uint_as_float(r1[j]) * e2,
+                                                 pf_row_scale(a, mi[h], row[h] + d + half));
+                            if (mi[h] < 2) {
+                                // NeoX pair (d, d + hd/2), tensor.cpp:918-925
+                                const float cs = __ldg(a.rope_cos + (size_t)pos * half + d);
+                                const float sn = __ldg(a.rope_sin + (size_t)pos * half + d);
+                                const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+                                const float t1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+                                y0 = t0;
+                                y1 = t1;
+                            }
+                            v0[j] = y0;
+                            v1[j] = y1;
+                        }
+                        float* dst;
+                        if (mi[h] == 0) dst = a.q_out + (size_t)s * a.nh * a.hd + head * a.hd;
+                        else
+                            dst = (mi[h] == 1 ? a.kcache : a.vcache) + (size_t)pos * a.nkv * a.hd + head * a.hd;
+                        pf_store32(dst + c * 32, v0, 32, false);
+                        pf_store32(dst + half + c * 32, v1, 32, false);
+                    }
+                }
+            } else {
+                const bool add = a.mode == PF_RESID;
+                for (int h = 0; h < 2; ++h) {
+                    for (int c = 0; c < 4; ++c) {
+                        __syncwarp();
+                        tmem_ld32(trow + h * 128 + c * 32, r0);
+                        tmem_wait_ld();
+                        const int n0 = row[h] + c * 32;
+                        if (!(srow && hv[h]) || n0 >= a.rows[0]) continue;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = min(n0 + j, a.rows[0] - 1);
+                            v0[j] = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, 0, n));
+                        }
+                        pf_store32(a.y + (size_t)s * a.ldy + n0, v0, a.rows[0] - n0, add);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort_flag) {
+        // leave no TMA write in flight into this CTA's shared memory
+        for (int kb = *consumed; kb < *issued; ++kb)
+            mbar_wait_bounded(&full[kb % kPfStages], (uint32_t)((kb / kPfStages) & 1));
+    }
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps and launch
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(tvb_status* st) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    *st = fn ? TVB_OK : set_error(TVB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+// F16 matrix [rows][K] (row pitch K), boxes of 128 rows x 64 k, 128B swizzle.
+static tvb_status encode_f16(CUtensorMap* m, const void* p, int rows, int K) {
+    tvb_status st;
+    auto fn = encode_fn(&st);
+    if (!fn) return st;
+    TVB_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, "prefill gemm: operand not 16-byte aligned");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kPfBK, 128u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(TVB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return TVB_OK;
+}
+
+static tvb_status pf_prepare() {
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        err = cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+    });
+    if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(pf_gemm_kernel)");
+    return TVB_OK;
+}
+
+tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
+    TVB_REQUIRE(g.S > 0 && g.K > 0 && g.xh, "prefill gemm: empty problem");
+    TVB_REQUIRE(g.K % kPfBK == 0, "prefill gemm: K=%d must be a multiple of %d", g.K, kPfBK);
+    TVB_TRY(pf_prepare());
+    PfMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    PfArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.mode = g.mode;
+    a.S = g.S;
+    a.K = g.K;
+    a.nk = g.K / kPfBK;
+    a.use_lo = g.xl != nullptr;
+    a.row_exp = g.row_exp;
+    a.y = g.y;
+    a.ldy = g.ldy;
+    a.nh = g.nh;
+    a.nkv = g.nkv;
+    a.hd = g.hd;
+    a.pos0 = g.pos0;
+    a.q_out = g.q_out;
+    a.kcache = g.kcache;
+    a.vcache = g.vcache;
+    a.rope_cos = g.rope_cos;
+    a.rope_sin = g.rope_sin;
+    a.status = g.status;
+    TVB_TRY(encode_f16(&maps.xh, g.xh, g.S, g.K));
+    if (g.xl) TVB_TRY(encode_f16(&maps.xl, g.xl, g.S, g.K));
+    const int nm = g.mode == PF_QKV ? 3 : g.mode == PF_GATEUP ? 2 : 1;
+    for (int i = 0; i < nm; ++i) {
+        TVB_REQUIRE(g.m[i].w && g.m[i].rows > 0, "prefill gemm: matrix %d missing", i);
+        TVB_TRY(encode_f16(&maps.w[i], g.m[i].w, g.m[i].rows, g.K));
+        a.rows[i] = g.m[i].rows;
+        a.row_scales[i] = g.m[i].row_scales;
+        a.scale[i] = g.m[i].scale;
+    }
+    int tiles = 0;
+    if (g.mode == PF_QKV) {
+        TVB_REQUIRE(g.hd == 128 && g.m[0].rows == g.nh * 128 && g.m[1].rows == g.nkv * 128 &&
+                        g.m[2].rows == g.nkv * 128 && g.q_out && g.kcache && g.vcache && g.rope_cos && g.rope_sin,
+                    "prefill gemm: inconsistent q/k/v geometry");
+        tiles = (g.nh + 2 * g.nkv + 1) / 2;
+    } else if (g.mode == PF_GATEUP) {
+        TVB_REQUIRE(g.m[0].rows == g.m[1].rows && g.m[0].rows % 32 == 0 && g.y && g.ldy >= g.m[0].rows,
+                    "prefill gemm: gate/up shapes");
+        tiles = (g.m[0].rows + 127) / 128;
+    } else {
+        TVB_REQUIRE(g.y && g.ldy >= g.m[0].rows, "prefill gemm: output");
+        tiles = (g.m[0].rows + kPfBN - 1) / kPfBN;
+    }
+    const dim3 grid((unsigned)tiles, (unsigned)((g.S + kPfBM - 1) / kPfBM));
+    pf_gemm_kernel<<<grid, kPfThreads, kPfSmem, stream>>>(maps, a);
+    return check_launch("pf_gemm_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm + hi/lo split, embedding gather, INT8 widening
+// ---------------------------------------------------------------------------
+constexpr int kNsThreads = 256;
+
+__global__ void __launch_bounds__(kNsThreads)
+pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
+                     __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp) {
+    const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const int K4 = K >> 2;
+    __shared__ float red[kNsThreads / 32];
+    __shared__ float s_inv, s_max;
+    float inv = 1.0f;
+    if (w) {
+        float ss = 0.f;
+        for (int k = tid; k < K4; k += kNsThreads) {
+            const float4 v = x4[k];
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (int i = 0; i < kNsThreads / 32; ++i) t += red[i];
+            // tensor.cpp:672-673: rms = sqrt(ss/n + eps); inv_rms = 1/rms
+            s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
+        }
+        __syncthreads();
+        inv = s_inv;
+    }
+    // the normalised row x * (inv_rms * w) (the vectorised path of tensor_rms_norm)
+    float mx = 0.f;
+    for (int k = tid; k < K4; k += kNsThreads) {
+        float4 v = x4[k];
+        if (w) {
+            const float4 g = w4[k];
+            v = make_float4(v.x * (inv * g.x), v.y * (inv * g.y), v.z * (inv * g.z), v.w * (inv * g.w));
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    mx = warp_max(mx);
+    __syncthreads();
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (int i = 0; i < kNsThreads / 32; ++i) t = fmaxf(t, red[i]);
+        s_max = t;
+    }
+    __syncthreads();
+    // power-of-two row scale: largest magnitude into [2^14, 2^15) (rows below
+    // 2^-86 stay scaled by 2^100, which keeps 2^-e finite)
+    const int e = (s_max > 0.f && isfinite(s_max)) ? max(ilogbf(s_max) - 14, -100) : 0;
+    if (tid == 0) row_exp[row] = e;
+    const float sc = ldexpf(1.0f, -e);
+    __half2* h2 = reinterpret_cast<__half2*>(xh + (size_t)row * K);
+    __half2* l2 = reinterpret_cast<__half2*>(xl + (size_t)row * K);
+    for (int k = tid; k < K4; k += kNsThreads) {
+        float4 v = x4[k];
+        if (w) {
+            const float4 g = w4[k];
+            v = make_float4(v.x * (inv * g.x), v.y * (inv * g.y), v.z * (inv * g.z), v.w * (inv * g.w));
+        }
+        const float f[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            hi[i] = __float2half_rn(f[i]);
+            lo[i] = __float2half_rn(f[i] - __half2float(hi[i]));
+        }
+        h2[2 * k] = __halves2half2(hi[0], hi[1]);
+        h2[2 * k + 1] = __halves2half2(hi[2], hi[3]);
+        l2[2 * k] = __halves2half2(lo[0], lo[1]);
+        l2[2 * k + 1] = __halves2half2(lo[2], lo[3]);
+    }
+}
+
+__global__ void pf_embed_kernel(const uint16_t* __restrict__ embd, const int* __restrict__ tokens, int H,
+                                float* __restrict__ x) {
+    const int s = blockIdx.x;
+    const uint16_t* e = embd + (size_t)__ldg(tokens + s) * H;
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+        x[(size_t)s * H + k] = __half2float(__ushort_as_half(__ldg(e + k)));
+}
+
+__global__ void pf_i8_kernel(const int8_t* __restrict__ q, size_t n, __half* __restrict__ out) {
+    const size_t n4 = n >> 2;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const char4 c = reinterpret_cast<const char4*>(q)[i];
+        reinterpret_cast<__half2*>(out)[2 * i] = __halves2half2(__int2half_rn(c.x), __int2half_rn(c.y));
+        reinterpret_cast<__half2*>(out)[2 * i + 1] = __halves2half2(__int2half_rn(c.z), __int2half_rn(c.w));
+    }
+}
+
+tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh, uint16_t* xl,
+                         int* row_exp, cudaStream_t st) {
+    TVB_REQUIRE(x && xh && xl && row_exp && S > 0 && K > 0 && K % 4 == 0, "norm_split: bad arguments");
+    pf_norm_split_kernel<<<S, kNsThreads, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
+                                                   reinterpret_cast<__half*>(xl), row_exp);
+    return check_launch("pf_norm_split_kernel");
+}
+
+tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st) {
+    TVB_REQUIRE(embd && tokens && x && S > 0 && H > 0, "embed: bad arguments");
+    pf_embed_kernel<<<S, 256, 0, st>>>(embd, tokens, H, x);
+    return check_launch("pf_embed_kernel");
+}
+
+tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st) {
+    TVB_REQUIRE(q && out && n % 4 == 0, "i8_to_f16: bad arguments");
+    const int blocks = (int)std::min<size_t>((n / 4 + 255) / 256, (size_t)num_sms() * 8);
+    pf_i8_kernel<<<std::max(blocks, 1), 256, 0, st>>>(q, n, reinterpret_cast<__half*>(out));
+    return check_launch("pf_i8_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Causal GQA attention (FP32 on the CUDA cores)
+// ---------------------------------------------------------------------------
+// A CTA takes one KV head and a block of query positions; its 64 rows are the
+// (position, query head) pairs that share that KV head.  Keys stream through
+// shared memory 64 at a time; each thread owns 4 rows x 4 keys of the score
+// tile (keys j, j+16, j+32, j+48: conflict-free rows of the padded K tile) and
+// 4 rows x 8 dims of the output, with online softmax (running max and sum per
+// row, kept by the 16 threads that share the rows).
+constexpr int kPaRows = 64, kPaKeys = 64, kPaThreads = 256;
+constexpr int kPaQs = 132;   // padded row stride (floats) of the Q and K tiles
+constexpr int kPaPs = 68;    // padded row stride of the probability tile
+constexpr int kPaSmem = (kPaRows * kPaQs + kPaKeys * kPaQs + kPaKeys * 128) * 4;
+
+__global__ void __launch_bounds__(kPaThreads, 2)
+pf_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int S,
+               int pos0, int nh, int nkv, float scale, float* __restrict__ out) {
+    extern __shared__ __align__(16) float pa_smem[];
+    float* Qs = pa_smem;                      // [64 rows][132]
+    float* Ks = Qs + kPaRows * kPaQs;         // [64 keys][132], reused for P [64 rows][68]
+    float* Vs = Ks + kPaKeys * kPaQs;         // [64 keys][128]
+    float* Ps = Ks;
+    constexpr int hd = 128;
+    const int group = nh / nkv, bq = kPaRows / group;
+    const int kvh = blockIdx.x;
+    const int qb = gridDim.y - 1 - blockIdx.y;   // longest blocks first
+    const int qlo = qb * bq;                     // first query row (0-based within the prompt)
+    const int tid = threadIdx.x, i = tid >> 4, j = tid & 15;
+    const int Hq = nh * hd, Hk = nkv * hd;
+
+    // Q tile: row r = (position qlo + r / group, head kvh * group + r % group)
+    for (int idx = tid; idx < kPaRows * (hd / 4); idx += kPaThreads) {
+        const int r = idx / (hd / 4), d4 = idx - r * (hd / 4);
+        const int sq = qlo + r / group;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sq < S) v = *reinterpret_cast<const float4*>(q + (size_t)sq * Hq + (kvh * group + r % group) * hd + d4 * 4);
+        *reinterpret_cast<float4*>(Qs + r * kPaQs + d4 * 4) = v;
+    }
+    float m[4], l[4], o[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        m[a] = -INFINITY;
+        l[a] = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[a][d] = 0.f;
+    }
+    int rpos[4];   // absolute position of each of this thread's rows (-1: none)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int sq = qlo + (4 * i + a) / group;
+        rpos[a] = sq < S ? pos0 + sq : -1;
+    }
+    const int last = pos0 + min(S, qlo + bq) - 1;   // largest position of this block
+    for (int t0 = 0; t0 <= last; t0 += kPaKeys) {
+        __syncthreads();   // previous tile's P and V reads are done
+        for (int idx = tid; idx < kPaKeys * (hd / 4); idx += kPaThreads) {
+            const int t = idx / (hd / 4), d4 = idx - t * (hd / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (t0 + t <= last) {
+                kv = *reinterpret_cast<const float4*>(kc + (size_t)(t0 + t) * Hk + kvh * hd + d4 * 4);
+                vv = *reinterpret_cast<const float4*>(vc + (size_t)(t0 + t) * Hk + kvh * hd + d4 * 4);
+            }
+            *reinterpret_cast<float4*>(Ks + t * kPaQs + d4 * 4) = kv;
+            *reinterpret_cast<float4*>(Vs + t * 128 + d4 * 4) = vv;
+        }
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) sc[a][b] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < hd; d += 4) {
+            float4 qa[4], kb4[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(Qs + (4 * i + a) * kPaQs + d);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) kb4[b] = *reinterpret_cast<const float4*>(Ks + (j + 16 * b) * kPaQs + d);
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    sc[a][b] = fmaf(qa[a].x, kb4[b].x, sc[a][b]);
+                    sc[a][b] = fmaf(qa[a].y, kb4[b].y, sc[a][b]);
+                    sc[a][b] = fmaf(qa[a].z, kb4[b].z, sc[a][b]);
+                    sc[a][b] = fmaf(qa[a].w, kb4[b].w, sc[a][b]);
+                }
+        }
+        // online softmax over this tile (16 threads share each row)
+        float alpha[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int t = t0 + j + 16 * b;
+                sc[a][b] = (t <= rpos[a]) ? sc[a][b] * scale : -INFINITY;
+                tmax = fmaxf(tmax, sc[a][b]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float mn = fmaxf(m[a], tmax);
+            alpha[a] = (mn == -INFINITY) ? 1.f : expf(m[a] - mn);
+            float psum = 0.f;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float p = (mn == -INFINITY) ? 0.f : expf(sc[a][b] - mn);
+                sc[a][b] = p;
+                psum += p;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+            l[a] = l[a] * alpha[a] + psum;
+            m[a] = mn;
+        }
+        __syncthreads();   // everyone is done reading K: reuse it for P
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) Ps[(4 * i + a) * kPaPs + j + 16 * b] = sc[a][b];
+        __syncthreads();
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[a][d] *= alpha[a];
+        const int tn = min(kPaKeys, last - t0 + 1);
+        for (int t = 0; t < tn; t += 4) {
+            float4 pa[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) pa[a] = *reinterpret_cast<const float4*>(Ps + (4 * i + a) * kPaPs + t);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float4 v0 = *reinterpret_cast<const float4*>(Vs + (t + u) * 128 + 4 * j);
+                const float4 v1 = *reinterpret_cast<const float4*>(Vs + (t + u) * 128 + 64 + 4 * j);
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    const float p = u == 0 ? pa[a].x : u == 1 ? pa[a].y : u == 2 ? pa[a].z : pa[a].w;
+                    o[a][0] = fmaf(p, v0.x, o[a][0]);
+                    o[a][1] = fmaf(p, v0.y, o[a][1]);
+                    o[a][2] = fmaf(p, v0.z, o[a][2]);
+                    o[a][3] = fmaf(p, v0.w, o[a][3]);
+                    o[a][4] = fmaf(p, v1.x, o[a][4]);
+                    o[a][5] = fmaf(p, v1.y, o[a][5]);
+                    o[a][6] = fmaf(p, v1.z, o[a][6]);
+                    o[a][7] = fmaf(p, v1.w, o[a][7]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        if (rpos[a] < 0) continue;
+        const int r = 4 * i + a;
+        const int sq = qlo + r / group, head = kvh * group + r % group;
+        const float inv = 1.0f / l[a];
+        float* dst = out + (size_t)sq * Hq + head * hd;
+        *reinterpret_cast<float4*>(dst + 4 * j) =
+            make_float4(o[a][0] * inv, o[a][1] * inv, o[a][2] * inv, o[a][3] * inv);
+        *reinterpret_cast<float4*>(dst + 64 + 4 * j) =
+            make_float4(o[a][4] * inv, o[a][5] * inv, o[a][6] * inv, o[a][7] * inv);
+    }
+}
+
+tvb_status pf_attention(const float* q, const float* kcache, const float* vcache, int S, int pos0, int nh, int nkv,
+                        int hd, float scale, float* out, cudaStream_t st) {
+    TVB_REQUIRE(q && kcache && vcache && out && S > 0 && pos0 >= 0, "prefill attention: bad arguments");
+    TVB_REQUIRE(hd == 128, "prefill attention: head_dim %d (only 128 is built)", hd);
+    TVB_REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0 && kPaRows % (nh / nkv) == 0,
+                "prefill attention: %d query heads per kv head must divide %d", nkv ? nh / nkv : 0, kPaRows);
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [] {
+        err = cudaFuncSetAttribute(pf_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPaSmem);
+    });
+    if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(pf_attn_kernel)");
+    const int bq = kPaRows / (nh / nkv);
+    const dim3 grid((unsigned)nkv, (unsigned)((S + bq - 1) / bq));
+    pf_attn_kernel<<<grid, kPaThreads, kPaSmem, st>>>(q, kcache, vcache, S, pos0, nh, nkv, scale, out);
+    return check_launch("pf_attn_kernel");
+}
+
+}  // namespace tvb

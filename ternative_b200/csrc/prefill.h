@@ -1,0 +1,73 @@
+// Batched prefill over S tokens (Model::forward_prefill, src/model.cpp:1139-1234)
+// on sm_100a: dense projections on the 5th-generation tensor cores (tcgen05.mma
+// with TMEM accumulators, operands staged by TMA), the RMSNorms that feed them,
+// and causal GQA attention.  Host-side launchers; kernels live in prefill.cu.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace tvb {
+
+// Epilogue of one projection GEMM.  Every mode computes
+//   acc[s][n] = sum_k x[s][k] * W[n][k]    (x given as F16 hi + lo planes, x = hi + lo)
+// and then, per output row n of W (scaled by the row's INT8 scale, if any):
+enum PfMode {
+    PF_STORE = 0,   // y[s][n] = acc                         (CUDABackend::matmul, M > 1)
+    PF_RESID = 1,   // y[s][n] += acc                        (o_proj / down + residual add)
+    PF_QKV = 2,     // q/k/v rows, NeoX RoPE on q and k at position pos0 + s, q -> q_out,
+                    // k/v -> the layer's KV cache rows           (model.cpp:1165-1177)
+    PF_GATEUP = 3,  // y[s][n] = relu(gate)^2 * up               (model.cpp:1203-1209)
+};
+
+// One operand matrix [rows][K] of F16 (INT8 weights are widened to F16 first;
+// their scales apply in the epilogue).
+struct PfMatrix {
+    const uint16_t* w = nullptr;
+    int rows = 0;
+    const float* row_scales = nullptr;   // per-row scale (INT8 per row), or nullptr
+    float scale = 1.0f;                  // per-tensor scale (INT8 per tensor), else 1
+};
+
+struct PfGemm {
+    int mode = PF_STORE;
+    int S = 0, K = 0;
+    const uint16_t* xh = nullptr;   // [S][K] F16, hi part of the activations
+    const uint16_t* xl = nullptr;   // [S][K] F16, lo part (x - hi), or nullptr for F16 x
+    const int* row_exp = nullptr;   // [S]: x = (hi + lo) * 2^row_exp[s] (pf_norm_split), or nullptr
+    PfMatrix m[3];                  // STORE/RESID: m[0]; GATEUP: gate, up; QKV: q, k, v
+    float* y = nullptr;             // STORE/RESID/GATEUP output [S][ldy]
+    int ldy = 0;
+    // PF_QKV
+    int nh = 0, nkv = 0, hd = 128, pos0 = 0;
+    float* q_out = nullptr;         // [S][nh * hd]
+    float* kcache = nullptr;        // this layer's rows [max_seq][nkv * hd]
+    float* vcache = nullptr;
+    const float* rope_cos = nullptr;   // [max_seq][hd / 2]
+    const float* rope_sin = nullptr;
+    unsigned* status = nullptr;     // device word; kStatusTimeout on a pipeline stall
+};
+
+tvb_status pf_gemm(const PfGemm& g, cudaStream_t st);
+
+// x[s] = f32(embd[tokens[s]])  (extract_embeddings_batched)
+tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st);
+
+// RMSNorm of each row of x [S][K] (tensor.cpp:636-708, x * (inv_rms * w)),
+// written as F16 hi + lo planes for the tensor cores with a power-of-two row
+// scale: v = (hi + lo) * 2^row_exp, |v / 2^row_exp| < 2^15.  w == nullptr: no
+// norm (the plain split, for CUDABackend::matmul).
+tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh,
+                         uint16_t* xl, int* row_exp, cudaStream_t st);
+
+// Causal GQA attention of S query rows at positions pos0 .. pos0 + S - 1 over
+// KV rows [0, pos0 + s] (compute_batched_attention, model.cpp:1071-1137).
+// q [S][nh * hd], caches [pos][nkv * hd], out [S][nh * hd].
+tvb_status pf_attention(const float* q, const float* kcache, const float* vcache, int S, int pos0,
+                        int nh, int nkv, int hd, float scale, float* out, cudaStream_t st);
+
+// INT8 -> F16 (exact: |q| <= 127).
+tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st);
+
+}  // namespace tvb
