@@ -49,6 +49,15 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 tensor throughput (TFLOP/s) a burst of kernels is compared with."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 class ClockSampler:
     """Samples SM clock and clock-event reasons via NVML (read-only) while running."""
 
@@ -320,6 +329,40 @@ def run_ours(args, world, rank, local):
                 "peak_kind": peak_kind, "bytes_per_launch": step_bytes,
                 "us_per_launch": ms_per_step * 1e3, "traffic": traffic}
 
+    # ---- batched prefill (tensor cores): prompt lengths 128 / 512 / 1024 ------------
+    # Algorithmic FLOPs per prompt: 2 x (projection weights) per token + causal
+    # attention 4 * S^2 * Hq / 2 per layer + the last row's lm_head.  The kernels
+    # issue twice the projection MMAs (F16 hi + lo activation planes).
+    tpeak, tpeak_kind = tensor_peak()
+    n_proj = sum(proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) * cfg.num_layers
+    Hq = cfg.num_heads * cfg.head_dim
+    prefill = {}
+    for S in (128, 512, 1024):
+        if S > min(cfg.max_prefill, cfg.max_seq_len):
+            continue
+        ptoks = rng.integers(0, cfg.vocab_size, S).astype(np.int32)
+        for _ in range(2):
+            be.clear_kv_d()
+            be.prefill(ptoks, want_logits=False)
+        best = None
+        for _ in range(3):
+            be.clear_kv_d()
+            be.sync_d()
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(stream)
+            be.prefill(ptoks, want_logits=False)
+            p1.record(stream)
+            p1.synchronize()
+            t = p0.elapsed_time(p1)
+            best = t if best is None else min(best, t)
+        flops = 2.0 * n_proj * S + cfg.num_layers * 4.0 * S * S * Hq / 2 + 2.0 * cfg.vocab_size * cfg.hidden_size
+        prefill[str(S)] = {"ms": best, "tok_s": S / (best * 1e-3), "TFLOP/s": flops / (best * 1e-3) / 1e12,
+                           "frac": flops / (best * 1e-3) / 1e12 / tpeak}
+    prefill["peak_TFLOP/s"] = tpeak
+    prefill["peak_kind"] = tpeak_kind
+    prefill["note"] = ("one tvb_prefill call (H2D tokens, all layers, last-row lm_head) timed with "
+                       "CUDA events, best of 3; KV cleared before each")
+
     # ---- the stand-alone streaming GEMV (gemv_d2d) on the GEMV-sweep shapes,
     # rotating over every layer's copy so the weights come from HBM ------------
     gemv = {}
@@ -403,7 +446,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline, "gemv_standalone": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps,   # one decode_step_kernel launch per token
-            "clocks": clk.report(), "merge": merge,
+            "clocks": clk.report(), "merge": merge, "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -94,6 +94,15 @@ typedef struct {
     float alpha;
     void* dst;
     float* row_scales;   /* TVB_I8_ROW only */
+    /* Column slice, for the tensor-parallel shard of a row-parallel projection
+     * (o_proj, down): merge columns [k0, k0 + K) of a tensor whose rows hold
+     * ld columns; i2s and A point at the WHOLE tensor's codes and LoRA A
+     * ([r][ld]).  Zero (the default) means k0 = 0, ld = K.  k0 and ld are
+     * multiples of 128.  A row slice needs no field: offset i2s by
+     * row0 * ld / 4 bytes and B by row0 * r floats.  TVB_I8_ROW scales of a
+     * column slice come from the slice's own absmax. */
+    int k0;
+    int ld;
 } tvb_merge_desc;
 
 /* All descriptors in one launch (descs is a HOST array of n entries; the
@@ -223,6 +232,37 @@ tvb_status tvb_kv_upload_layer(tvb_context* ctx, int layer, int n_positions, con
 tvb_status tvb_kv_download_slot(tvb_context* ctx, int layer, int pos, int n_floats, float* h_dst);
 /* sync_d (ops.h:123). */
 tvb_status tvb_context_sync(tvb_context* ctx);
+
+/* ------------------------------------------------------------------------ */
+/* Tensor parallelism: one process (and context) per GPU.  No counterpart in */
+/* the reference, whose GPU path is single-device.  Each rank's context is  */
+/* created with its shard's dimensions (num_heads, num_kv_heads and          */
+/* intermediate_size divided by the ranks; hidden_size and vocab_size whole) */
+/* and registered with its shard of every projection: q/k/v and gate/up are */
+/* split by rows, o_proj and down by columns (tvb_merge_desc k0/ld), the    */
+/* tied lm_head by vocabulary rows (tvb_set_output still takes the whole    */
+/* embedding table).  The decode step then exchanges partial rows with the  */
+/* other ranks over NVLink inside its single launch, after o_proj and after */
+/* down, and agrees on the argmax across vocabulary slices.                  */
+/*                                                                          */
+/* Setup: tvb_tp_init on every rank returns this rank's exchange buffer;    */
+/* export it with tvb_ipc_export, give the handles to every rank, import    */
+/* the others' with tvb_ipc_import and pass all buffers (own at [rank]) to  */
+/* tvb_tp_set_peers.  Every rank must then run the same sequence of decode  */
+/* and prefill calls; logits returned are this rank's vocabulary slice       */
+/* (vocab_size / world floats, rows [rank * vocab_size / world, ...)).      */
+/* After a device-side error every rank must be re-initialised.             */
+/* Close imported buffers (tvb_ipc_close) after destroying the context.     */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    unsigned char bytes[64];
+} tvb_ipc_handle;
+
+tvb_status tvb_tp_init(tvb_context* ctx, int rank, int world, void** exchange);
+tvb_status tvb_tp_set_peers(tvb_context* ctx, void* const* exchanges);
+tvb_status tvb_ipc_export(const void* dev_ptr, tvb_ipc_handle* out);
+tvb_status tvb_ipc_import(const tvb_ipc_handle* handle, void** dev_ptr);
+tvb_status tvb_ipc_close(void* dev_ptr);
 
 /* Weight table for the fused step. */
 typedef struct {

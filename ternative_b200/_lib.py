@@ -35,7 +35,7 @@ class TvbError(RuntimeError):
 class MergeDesc(C.Structure):
     _fields_ = [("i2s", C.c_void_p), ("scale", C.c_float), ("K", C.c_int), ("N", C.c_int),
                 ("A", C.c_void_p), ("B", C.c_void_p), ("r", C.c_int), ("alpha", C.c_float),
-                ("dst", C.c_void_p), ("row_scales", C.c_void_p)]
+                ("dst", C.c_void_p), ("row_scales", C.c_void_p), ("k0", C.c_int), ("ld", C.c_int)]
 
 
 class ModelConfig(C.Structure):
@@ -61,6 +61,10 @@ class LayerWeights(C.Structure):
                 ("attn_sub_norm", C.c_void_p), ("wo", Weight), ("ffn_norm", C.c_void_p),
                 ("w_gate", Weight), ("w_up", Weight), ("ffn_sub_norm", C.c_void_p),
                 ("w_down", Weight)]
+
+
+class IpcHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]
 
 
 _P = C.c_void_p
@@ -110,6 +114,11 @@ _SIGS = {
     "tvb_generate_greedy": [_P, _I, _I, _I, _P],
     "tvb_decode_enqueue": [_P, _I, _I, _I],
     "tvb_prefill": [_P, _P, _I, _P, _P],
+    "tvb_tp_init": [_P, _I, _I, C.POINTER(C.c_void_p)],
+    "tvb_tp_set_peers": [_P, C.POINTER(C.c_void_p)],
+    "tvb_ipc_export": [_P, C.POINTER(IpcHandle)],
+    "tvb_ipc_import": [C.POINTER(IpcHandle), C.POINTER(C.c_void_p)],
+    "tvb_ipc_close": [_P],
 }
 _RESTYPES = {
     "tvb_version": C.c_int,

@@ -22,7 +22,7 @@ from typing import Optional, Sequence
 import numpy as np
 
 from . import _lib
-from ._lib import (TVB_F16, TVB_F32, TVB_I8_ROW, TVB_I8_TENSOR, Buffers, LayerWeights,
+from ._lib import (TVB_F16, TVB_F32, TVB_I8_ROW, TVB_I8_TENSOR, Buffers, IpcHandle, LayerWeights,
                    MergeDesc, ModelConfig, Weight, call, load)
 
 
@@ -235,10 +235,45 @@ class CUDABackend:
     def set_output(self, tok_embd_f16, output_norm):
         call("tvb_set_output", self.ctx, _ptr(tok_embd_f16), _ptr(output_norm))
 
+    # ---- tensor parallelism (one process and context per GPU) -------------------
+    def tp_init(self, rank: int, world: int) -> int:
+        """Make this context rank `rank` of `world`; returns its exchange buffer."""
+        p = C.c_void_p()
+        call("tvb_tp_init", self.ctx, rank, world, C.byref(p))
+        self.tp_world = world
+        return p.value
+
+    def tp_set_peers(self, buffers: Sequence[int]) -> None:
+        arr = (C.c_void_p * len(buffers))(*buffers)
+        call("tvb_tp_set_peers", self.ctx, arr)
+
+    @staticmethod
+    def ipc_export(dev_ptr: int) -> bytes:
+        h = IpcHandle()
+        call("tvb_ipc_export", dev_ptr, C.byref(h))
+        return bytes(h.bytes)
+
+    @staticmethod
+    def ipc_import(handle: bytes) -> int:
+        h = IpcHandle()
+        C.memmove(h.bytes, handle, 64)
+        p = C.c_void_p()
+        call("tvb_ipc_import", C.byref(h), C.byref(p))
+        return p.value
+
+    @staticmethod
+    def ipc_close(dev_ptr: int) -> None:
+        call("tvb_ipc_close", dev_ptr)
+
+    def n_logits(self) -> int:
+        """Logits a step returns: the whole vocabulary, or this rank's slice."""
+        return self.cfg.vocab_size // getattr(self, "tp_world", 1)
+
     def decode_step(self, token: int, pos: int, want_logits: bool = True):
-        """Model::forward_gpu: returns (logits [V] float32 or None, argmax)."""
+        """Model::forward_gpu: returns (logits [V] float32 or None, argmax).
+        Under tensor parallelism the logits are this rank's vocabulary slice."""
         am = C.c_int()
-        logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        logits = np.empty(self.n_logits(), np.float32) if want_logits else None
         call("tvb_decode_step", self.ctx, token, pos, None if logits is None else logits.ctypes.data,
              C.byref(am))
         return logits, am.value
@@ -256,7 +291,7 @@ class CUDABackend:
         and returns (last-row logits or None, argmax)."""
         t = np.ascontiguousarray(tokens, np.int32)
         am = C.c_int()
-        logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        logits = np.empty(self.n_logits(), np.float32) if want_logits else None
         call("tvb_prefill", self.ctx, t.ctypes.data, t.size,
              None if logits is None else logits.ctypes.data, C.byref(am))
         return logits, am.value

@@ -161,6 +161,15 @@ struct tvb_context {
     float *pf_x = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_h = nullptr;
     uint16_t *pf_xh = nullptr, *pf_xl = nullptr;
     int *pf_exp = nullptr, *pf_tok = nullptr;
+    // tensor parallelism (tvb_tp_init / tvb_tp_set_peers): this rank's exchange
+    // buffer, every rank's (IPC-mapped) buffer, and a second residual vector
+    // (folds alternate between e_x and e_x2)
+    int tp_world = 1, tp_rank = 0;
+    float* tp_xchg = nullptr;
+    float* tp_peer[kMaxTp] = {};
+    bool tp_ready = false;
+    float* e_x2 = nullptr;
+    int n_tp_step = 0, n_tp_layers = 0;
     uint16_t* pf_w16 = nullptr;
     size_t pf_w16_elems = 0;
 };
@@ -177,6 +186,33 @@ tvb_status alloc_dev(void** p, size_t bytes) {
 std::vector<Phase> build_phases(tvb_context* c) {
     std::vector<Phase> ph;
     const float scale = 1.0f / std::sqrt((float)c->cfg.head_dim);
+    // Tensor parallelism: q/k/v and gate/up are this rank's rows, o_proj and
+    // down its columns; those two end with an exchange of partial rows and the
+    // phase after each folds them into the residual (alternating buffers).
+    const bool tp = c->tp_world > 1;
+    TpArgs tpb = {};
+    if (tp) {
+        tpb.world = c->tp_world;
+        tpb.rank = c->tp_rank;
+        tpb.ld = c->H + 4;
+        for (int r = 0; r < c->tp_world; ++r) tpb.peer[r] = c->tp_peer[r];
+        tpb.index = -1;
+        tpb.fold = -1;
+    }
+    float* xres[2] = {c->e_x, c->e_x2};
+    int cur = 0;            // residual buffer the next phase reads
+    int xi = 0;             // exchanges so far
+    int fold_norm = 0;      // full length of the sub-norm of the last exchange (0: none)
+    auto fold_into = [&](Phase& p) {
+        p.g.x = xres[cur];
+        if (tp && xi > 0) {
+            p.g.tp.fold = xi - 1;
+            p.g.tp.norm_n = fold_norm;
+            p.g.tp.x_out = xres[cur ^ 1];
+            p.g.x = xres[cur];
+            cur ^= 1;
+        }
+    };
     auto gemv = [&](int mode, int wt) {
         Phase p = {};
         p.kind = PK_GEMV;
@@ -185,6 +221,7 @@ std::vector<Phase> build_phases(tvb_context* c) {
         p.g.eps = c->cfg.rms_norm_eps;
         p.g.st = c->st;
         p.g.status = &c->st->status;
+        p.g.tp = tpb;
         return p;
     };
     for (int l = 0; l < c->L; ++l) {
@@ -199,9 +236,11 @@ std::vector<Phase> build_phases(tvb_context* c) {
             fill_weight(p.g, 1, lw.wk);
             fill_weight(p.g, 2, lw.wv);
             p.g.K = c->H;
-            p.g.x = c->e_x;
+            if (l == 0) cur = 0;
+            else fold_into(p);
+            if (l == 0) p.g.x = xres[0];
             p.g.embd = static_cast<const uint16_t*>(c->tok_embd);
-            p.g.x_out = c->e_x;
+            p.g.x_out = xres[0];
             p.g.gather_token = (l == 0);
             p.g.norm_w = lw.attn_norm;
             p.g.nh = c->cfg.num_heads;
@@ -242,7 +281,11 @@ std::vector<Phase> build_phases(tvb_context* c) {
             p.g.attn_nsplit = c->nsplit;
             p.g.hd = c->cfg.head_dim;
             p.g.norm_w = lw.attn_sub_norm;
-            p.g.y = c->e_x;
+            p.g.y = xres[cur];
+            if (tp) {
+                p.g.tp.index = xi++;
+                fold_norm = lw.attn_sub_norm ? c->Hq * c->tp_world : 0;
+            }
             ph.push_back(p);
         }
         {   // (g)-(h): ffn_norm, gate/up, relu^2 * up
@@ -251,7 +294,7 @@ std::vector<Phase> build_phases(tvb_context* c) {
             fill_weight(p.g, 1, lw.w_up);
             p.g.N = c->I;
             p.g.K = c->H;
-            p.g.x = c->e_x;
+            fold_into(p);
             p.g.norm_w = lw.ffn_norm;
             p.g.y = c->e_h;
             ph.push_back(p);
@@ -263,21 +306,32 @@ std::vector<Phase> build_phases(tvb_context* c) {
             p.g.K = c->I;
             p.g.x = c->e_h;
             p.g.norm_w = lw.ffn_sub_norm;
-            p.g.y = c->e_x;
+            p.g.y = xres[cur];
+            if (tp) {
+                p.g.tp.index = xi++;
+                fold_norm = lw.ffn_sub_norm ? c->I * c->tp_world : 0;
+            }
             ph.push_back(p);
         }
     }
+    c->n_tp_layers = xi;
     {   // final norm + tied lm_head + argmax
         Phase p = gemv(GM_LMHEAD, WT_F16);
-        p.g.w[0] = c->tok_embd;
+        const int vs = c->V / c->tp_world;   // this rank's vocabulary slice
+        p.g.w[0] = static_cast<const uint16_t*>(c->tok_embd) + (size_t)c->tp_rank * vs * c->H;
         p.g.tscale[0] = 1.0f;
-        p.g.N = c->V;
+        p.g.N = vs;
         p.g.K = c->H;
-        p.g.x = c->e_x;
+        fold_into(p);
         p.g.norm_w = c->output_norm;
         p.g.y = c->e_logits;
+        if (tp) {
+            p.g.tp.vocab0 = c->tp_rank * vs;
+            p.g.tp.index = xi++;   // argmax over the ranks' slices
+        }
         ph.push_back(p);
     }
+    c->n_tp_step = xi;
     return ph;
 }
 
@@ -288,7 +342,7 @@ int phase_units(const Phase& p) {
     return (p.g.N + R - 1) / R;
 }
 
-tvb_status capture(tvb_context* c, int n_phases, cudaGraphExec_t* out) {
+tvb_status capture(tvb_context* c, int n_phases, int n_tp, cudaGraphExec_t* out) {
     if (*out) {
         cudaGraphExecDestroy(*out);
         *out = nullptr;
@@ -304,8 +358,11 @@ tvb_status capture(tvb_context* c, int n_phases, cudaGraphExec_t* out) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t le = cudaLaunchKernelEx(&cfg, decode_step_kernel, (const Phase*)c->d_phases, n_phases,
-                                        c->st);
+    cudaError_t le = c->tp_world > 1
+                         ? cudaLaunchKernelEx(&cfg, decode_step_kernel<true>, (const Phase*)c->d_phases,
+                                              n_phases, c->st, n_tp)
+                         : cudaLaunchKernelEx(&cfg, decode_step_kernel<false>, (const Phase*)c->d_phases,
+                                              n_phases, c->st, n_tp);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (le != cudaSuccess) {
@@ -324,6 +381,8 @@ tvb_status ensure_graphs(tvb_context* c) {
     for (int l = 0; l < c->L; ++l)
         if (!c->layer_set[l]) return set_error(TVB_ERR_STATE, "layer %d weights not set", l);
     if (!c->tok_embd || !c->output_norm) return set_error(TVB_ERR_STATE, "output weights not set");
+    if (c->tp_world > 1 && !c->tp_ready)
+        return set_error(TVB_ERR_STATE, "tensor parallelism: peers not set (tvb_tp_set_peers)");
     std::vector<Phase> ph = build_phases(c);
     // shared memory: the largest per-phase layout, and the attention scratch
     const int G = num_sms();
@@ -337,9 +396,10 @@ tvb_status ensure_graphs(tvb_context* c) {
     }
     if (smem > g_max_dyn_smem)
         return set_error(TVB_ERR_UNSUPPORTED, "decode step needs %d B of shared memory", smem);
-    TVB_CUDA(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    auto kern = c->tp_world > 1 ? decode_step_kernel<true> : decode_step_kernel<false>;
+    TVB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int per_sm = 0;
-    TVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kGemvThreads, smem));
+    TVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem));
     if (per_sm < 1) return set_error(TVB_ERR_UNSUPPORTED, "decode step kernel cannot be resident");
     if (c->d_phases) cudaFree(c->d_phases);
     c->d_phases = nullptr;
@@ -347,8 +407,8 @@ tvb_status ensure_graphs(tvb_context* c) {
     TVB_CUDA(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     c->n_phases = (int)ph.size();
     c->step_smem = smem;
-    TVB_TRY(capture(c, c->n_phases, &c->g_step));
-    TVB_TRY(capture(c, c->n_phases - 1, &c->g_layers));
+    TVB_TRY(capture(c, c->n_phases, c->n_tp_step, &c->g_step));
+    TVB_TRY(capture(c, c->n_phases - 1, c->n_tp_layers, &c->g_layers));
     c->dirty = false;
     return TVB_OK;
 }
@@ -551,7 +611,8 @@ tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
         {(void**)&c->d_x, H * 4ull}, {(void**)&c->d_norm, std::max(H, I) * 4ull},
         {(void**)&c->d_q, Hq * 4ull}, {(void**)&c->d_k, Hk * 4ull}, {(void**)&c->d_v, Hk * 4ull},
         {(void**)&c->d_gate, I * 4ull}, {(void**)&c->d_up, I * 4ull},
-        {(void**)&c->e_x, H * 4ull}, {(void**)&c->e_q, Hq * 4ull}, {(void**)&c->e_attn, Hq * 4ull},
+        {(void**)&c->e_x, H * 4ull}, {(void**)&c->e_x2, H * 4ull}, {(void**)&c->e_q, Hq * 4ull},
+        {(void**)&c->e_attn, Hq * 4ull},
         {(void**)&c->e_h, I * 4ull}, {(void**)&c->e_logits, V * 4ull},
         {(void**)&c->attn_part, (size_t)m.num_heads * 32 * (m.head_dim + 4) * 4ull},
         {(void**)&c->kcache, kv * 4}, {(void**)&c->vcache, kv * 4},
@@ -603,7 +664,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
                    c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
-                   c->pf_w16};
+                   c->pf_w16, c->e_x2, c->tp_xchg};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
@@ -615,6 +676,62 @@ tvb_status tvb_context_destroy(tvb_context* c) {
 }
 
 void* tvb_context_stream(tvb_context* c) { return c ? (void*)c->stream : nullptr; }
+
+tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
+    TVB_REQUIRE(c && exchange, "tp_init: null argument");
+    TVB_REQUIRE(world >= 1 && world <= kMaxTp && rank >= 0 && rank < world,
+                "tp_init: rank %d of %d (at most %d ranks)", rank, world, kMaxTp);
+    TVB_REQUIRE(c->V % world == 0, "tp_init: vocabulary %d not divisible by %d ranks", c->V, world);
+    TVB_REQUIRE(!c->tp_xchg, "tp_init: already initialised");
+    const size_t floats = (size_t)kTpSlots + 2ull * world * (c->H + 4);
+    TVB_TRY(alloc_dev((void**)&c->tp_xchg, floats * 4));
+    TVB_CUDA(cudaMemset(c->tp_xchg, 0, floats * 4));
+    c->tp_world = world;
+    c->tp_rank = rank;
+    c->tp_ready = world == 1;
+    if (world == 1) c->tp_peer[0] = c->tp_xchg;
+    c->dirty = true;
+    *exchange = c->tp_xchg;
+    return TVB_OK;
+}
+
+tvb_status tvb_tp_set_peers(tvb_context* c, void* const* exchanges) {
+    TVB_REQUIRE(c && exchanges, "tp_set_peers: null argument");
+    TVB_REQUIRE(c->tp_xchg, "tp_set_peers: call tvb_tp_init first");
+    TVB_REQUIRE(exchanges[c->tp_rank] == c->tp_xchg, "tp_set_peers: entry %d is not this rank's buffer",
+                c->tp_rank);
+    for (int r = 0; r < c->tp_world; ++r) {
+        TVB_REQUIRE(exchanges[r] && (reinterpret_cast<uintptr_t>(exchanges[r]) & 15) == 0,
+                    "tp_set_peers: bad buffer for rank %d", r);
+        c->tp_peer[r] = static_cast<float*>(exchanges[r]);
+    }
+    c->tp_ready = true;
+    c->dirty = true;
+    return TVB_OK;
+}
+
+tvb_status tvb_ipc_export(const void* dev_ptr, tvb_ipc_handle* out) {
+    TVB_REQUIRE(dev_ptr && out, "ipc_export: null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(out->bytes), "IPC handle size");
+    cudaIpcMemHandle_t h;
+    TVB_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+    std::memcpy(out->bytes, &h, sizeof(h));
+    return TVB_OK;
+}
+
+tvb_status tvb_ipc_import(const tvb_ipc_handle* in, void** dev_ptr) {
+    TVB_REQUIRE(in && dev_ptr, "ipc_import: null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, in->bytes, sizeof(h));
+    TVB_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return TVB_OK;
+}
+
+tvb_status tvb_ipc_close(void* dev_ptr) {
+    TVB_REQUIRE(dev_ptr, "ipc_close: null argument");
+    TVB_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+    return TVB_OK;
+}
 
 tvb_status tvb_context_buffers(tvb_context* c, tvb_buffers* o) {
     TVB_REQUIRE(c && o, "context_buffers: null argument");
@@ -714,11 +831,12 @@ tvb_status tvb_decode_step(tvb_context* c, int token, int pos, float* logits_hos
     TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io, 8, cudaMemcpyHostToDevice, c->stream));
     TVB_CUDA(cudaGraphLaunch(c->g_step, c->stream));
     TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    const size_t nl = (size_t)(c->V / c->tp_world);   // this rank's logits
     if (logits_host)
-        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, nl * 4, cudaMemcpyDeviceToHost, c->stream));
     TVB_CUDA(cudaStreamSynchronize(c->stream));
     TVB_TRY(check_status(c));
-    if (logits_host) std::memcpy(logits_host, c->h_logit, (size_t)c->V * 4);
+    if (logits_host) std::memcpy(logits_host, c->h_logit, nl * 4);
     if (argmax_host) *argmax_host = c->h_st->next_token;
     return TVB_OK;
 }
@@ -768,13 +886,26 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
     TVB_TRY(ensure_graphs(c));
     // the pinned staging is about to be rewritten: let earlier copies from it finish
     TVB_CUDA(cudaStreamSynchronize(c->stream));
-    TVB_TRY(prefill_batched(c, tokens, S));
+    if (c->tp_world > 1) {
+        // tensor-parallel ranks: one decode-step launch per prompt row (the
+        // exchanges run inside it); row s attends to KV rows [0, s] as in
+        // forward_prefill (model.cpp:1084 kv_len = s + 1)
+        for (int s = 0; s < S; ++s) {
+            c->h_io[2 * s] = s;
+            c->h_io[2 * s + 1] = tokens[s];
+            TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io + 2 * s, 8, cudaMemcpyHostToDevice, c->stream));
+            TVB_CUDA(cudaGraphLaunch(s + 1 < S ? c->g_layers : c->g_step, c->stream));
+        }
+    } else {
+        TVB_TRY(prefill_batched(c, tokens, S));
+    }
     TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    const size_t nl = (size_t)(c->V / c->tp_world);   // this rank's logits
     if (last_logits)
-        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+        TVB_CUDA(cudaMemcpyAsync(c->h_logit, c->e_logits, nl * 4, cudaMemcpyDeviceToHost, c->stream));
     TVB_CUDA(cudaStreamSynchronize(c->stream));
     TVB_TRY(check_status(c));
-    if (last_logits) std::memcpy(last_logits, c->h_logit, (size_t)c->V * 4);
+    if (last_logits) std::memcpy(last_logits, c->h_logit, nl * 4);
     if (argmax_host) *argmax_host = c->h_st->next_token;
     return TVB_OK;
 }

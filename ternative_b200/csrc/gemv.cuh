@@ -52,7 +52,71 @@ struct StepState {
     unsigned bar_ctr;    // grid-barrier arrivals of the running decode-step launch
     unsigned exit_ctr;   // CTAs that left the running launch
     unsigned abort;      // set when a barrier wait gave up; every CTA then leaves
+    unsigned tp_epoch;   // tensor parallelism: cross-rank exchanges completed so far
 };
+
+// Tensor parallelism (one rank per GPU).  Every rank owns an exchange buffer
+// that its peers write over NVLink (peer pointers from CUDA IPC):
+//   [0, 64)     flags: flags[src] = epoch of the last exchange rank src signalled
+//   [64, 80)    argmax keys of the lm_head slices (64-bit, keys[src])
+//   [128, ...)  two slots (exchange epoch parity) of world x ld floats: slot[src]
+//               holds rank src's partial output rows and, at [H], its partial
+//               sum of squares of the sub-norm input
+constexpr int kMaxTp = 8;
+constexpr int kTpFlags = 0, kTpKeys = 64, kTpSlots = 128;
+
+// A zero-initialised TpArgs (world 0) means no tensor parallelism.
+struct TpArgs {
+    float* peer[kMaxTp];  // every rank's exchange buffer (this rank's at [rank])
+    int world, rank;
+    int ld;               // floats per rank in a slot (H + 4)
+    int index;            // >= 0: this phase ends with exchange `index` of the step
+    int fold;             // >= 0: input = residual + sum of exchange `fold`'s partials
+    int norm_n;           // fold: full length of the sub-norm whose partials arrive
+    float* x_out;         // fold: where the folded residual is stored (CTA-partitioned)
+    int vocab0;           // lm_head: first vocabulary row of this rank's slice
+};
+
+__device__ __forceinline__ float* tp_slot(float* buf, const TpArgs& t, unsigned epoch) {
+    return buf + kTpSlots + (size_t)(epoch & 1u) * t.world * t.ld;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Tell every rank that this rank's writes for exchange `epoch` are done (one
+// thread; the writes it covers were ordered before it at system scope).
+__device__ __forceinline__ void tp_signal(const TpArgs& t, unsigned epoch) {
+    __threadfence_system();
+    for (int r = 0; r < t.world; ++r)
+        st_release_sys(reinterpret_cast<unsigned*>(t.peer[r] + kTpFlags) + t.rank, epoch);
+}
+
+// Wait (one thread, bounded by about a second) until every rank has signalled
+// `epoch`; gives up early when this launch aborts.  On a timeout it raises the
+// abort latch and the timeout status bit.
+__device__ __forceinline__ bool tp_wait(const TpArgs& t, unsigned epoch, unsigned* abort_flag,
+                                        unsigned* status) {
+    const unsigned* f = reinterpret_cast<const unsigned*>(t.peer[t.rank] + kTpFlags);
+    const long long t0 = clock64();
+    for (int r = 0; r < t.world; ++r) {
+        while ((int)(ld_acquire_sys(f + r) - epoch) < 0) {
+            if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
+            if (clock64() - t0 > kSpinLimitCycles) {
+                atomicOr(abort_flag, 1u);
+                atomicOr(status, kStatusTimeout);
+                return false;
+            }
+        }
+    }
+    return true;
+}
 
 struct GemvArgs {
     const void* w[3];
@@ -77,6 +141,7 @@ struct GemvArgs {
     int gather_token;           // GM_QKV: 1 on layer 0
     const float* attn_part;     // GM_RESID after attention: input = merge of these partials
     int attn_nsplit;            // splits per head in attn_part ([nh][nsplit][hd + 4])
+    TpArgs tp;                  // world == 1: no tensor parallelism
 };
 
 __device__ __forceinline__ unsigned long long argmax_pack(float v, int idx) {
@@ -281,9 +346,11 @@ __device__ __forceinline__ void gemv_stage(const GemvArgs& a, unsigned char* sme
 // One GEMV phase whose constants are staged (gemv_stage), whose first kDepth
 // items are already requested in `buf`, and whose inputs are ready: residual
 // operands, activation prologue, chunk stream, epilogue.
-template <int MODE, int WT, int R>
+// TP: the tensor-parallel decode kernel's instantiation (folds and pushes of
+// partial rows); the single-GPU kernels compile those paths out.
+template <int MODE, int WT, int R, bool TP = false>
 __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem, int G, int pos, int token,
-                                         ChunkBuf& buf, GemvArgmax& best) {
+                                         ChunkBuf& buf, GemvArgmax& best, unsigned epoch0 = 0) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, b = blockIdx.x;
     const int K = a.K;
     const int esz = (WT == WT_F16) ? 2 : 1;
@@ -298,7 +365,10 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     float* pre_sin = pre_cos + kMaxRopeHalf;
 
     // ---- residual operands (written by earlier phases) ---------------------------
-    if (MODE == GM_RESID) {
+    // row-parallel shard (o_proj, down): partial rows to every rank.  The
+    // lm_head phase also carries an exchange index (its argmax), but no rows.
+    const bool push = TP && MODE == GM_RESID && a.tp.world > 1 && a.tp.index >= 0;
+    if (MODE == GM_RESID && !push) {
         for (int lr = tid; lr < g.nrows; lr += kGemvThreads) {
             int m, row;
             pre_res[lr] = group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row) ? __ldcg(a.y + row) : 0.f;
@@ -311,6 +381,20 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     // reduction off the critical path.  Activations are read through L2
     // (ld.global.cg): another CTA or kernel wrote them.
     __shared__ float red_ss[kGemvWarps];
+    // tensor parallelism: the input is the residual plus the partial outputs of
+    // every rank (summed in rank order, so every rank holds the same vector),
+    // scaled by the sub-norm factor from the ranks' partial sums of squares
+    const bool fold = TP && a.tp.world > 1 && a.tp.fold >= 0;
+    const float* tp_in = nullptr;
+    float tp_inv = 1.0f;
+    if (fold) {
+        tp_in = tp_slot(a.tp.peer[a.tp.rank], a.tp, epoch0 + (unsigned)a.tp.fold + 1u);
+        float ss_all = 0.f;
+        for (int r = 0; r < a.tp.world; ++r) ss_all += __ldcg(tp_in + (size_t)r * a.tp.ld + K);
+        // tensor.cpp:672-673 over the full sub-norm length (norm_n == 0: no sub-norm)
+        if (a.tp.norm_n > 0)
+            tp_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss_all, (float)a.tp.norm_n), a.eps)));
+    }
     {
         const uint16_t* esrc = nullptr;
         if (MODE == GM_QKV && a.gather_token) esrc = a.embd + (size_t)token * K;
@@ -363,6 +447,16 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
                 }
                 const float inv = 1.0f / Ls;
                 v = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+            } else if (fold) {
+                v = __ldcg(x4 + k4);
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < a.tp.world; ++r) {
+                    const float4 p = __ldcg(reinterpret_cast<const float4*>(tp_in + (size_t)r * a.tp.ld) + k4);
+                    acc = make_float4(acc.x + p.x, acc.y + p.y, acc.z + p.z, acc.w + p.w);
+                }
+                v = make_float4(__fadd_rn(v.x, acc.x * tp_inv), __fadd_rn(v.y, acc.y * tp_inv),
+                                __fadd_rn(v.z, acc.z * tp_inv), __fadd_rn(v.w, acc.w * tp_inv));
+                if (k4 % G == b) reinterpret_cast<float4*>(a.tp.x_out)[k4] = v;
             } else {
                 v = __ldcg(x4 + k4);
             }
@@ -420,11 +514,19 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     __syncthreads();
 
     // tensor.cpp:675-676: rms = sqrt(ss/n + eps); inv = 1/rms
-    float inv = 1.0f;
+    float inv = 1.0f, ss_local = 0.f;
+    size_t tp_off = 0;   // push: offset of this rank's partial rows in every rank's buffer
     if (a.norm_w) {
-        float t = 0.f;
-        for (int w = 0; w < kGemvWarps; ++w) t += red_ss[w];
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), a.eps)));
+        for (int w = 0; w < kGemvWarps; ++w) ss_local += red_ss[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss_local, (float)K), a.eps)));
+    }
+    if (push) {
+        // the sub-norm factor needs every rank's sum of squares: apply it when folding
+        inv = 1.0f;
+        const unsigned e = epoch0 + (unsigned)a.tp.index + 1u;
+        tp_off = (size_t)(tp_slot(a.tp.peer[0], a.tp, e) - a.tp.peer[0]) + (size_t)a.tp.rank * a.tp.ld;
+        if (b == 0 && tid == 0)
+            for (int r = 0; r < a.tp.world; ++r) a.tp.peer[r][tp_off + a.N] = ss_local;
     }
 
     // ---- epilogue: one thread per unit -----------------------------------------------
@@ -473,10 +575,15 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
             for (int r = 0; r < R; ++r) {
                 if (!valid[r]) continue;
                 if (MODE == GM_PLAIN) a.y[rows[r]] = y[r];
-                else if (MODE == GM_RESID) a.y[rows[r]] = __fadd_rn(pre_res[lu * R + r], y[r]);
-                else {
+                else if (MODE == GM_RESID) {
+                    if (push) {
+                        for (int q = 0; q < a.tp.world; ++q) a.tp.peer[q][tp_off + rows[r]] = y[r];
+                    } else {
+                        a.y[rows[r]] = __fadd_rn(pre_res[lu * R + r], y[r]);
+                    }
+                } else {
                     a.y[rows[r]] = y[r];
-                    if (y[r] > best.v) { best.v = y[r]; best.i = rows[r]; }
+                    if (y[r] > best.v) { best.v = y[r]; best.i = rows[r] + a.tp.vocab0; }
                 }
             }
         }
@@ -485,7 +592,8 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
 
 // LM-head completion: CTA-wide argmax, global max, and -- in the last CTA to
 // finish -- publication of the step's token and advance of the step state.
-__device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgmax& best) {
+template <bool TP = false>
+__device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgmax& best, unsigned epoch0 = 0) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ unsigned long long kbest[kGemvWarps];
     unsigned long long key = (best.v == -INFINITY) ? 0ull : argmax_pack(best.v, best.i);
@@ -505,7 +613,23 @@ __device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgma
         if (done == gridDim.x - 1) {
             // Last CTA: publish this step's argmax and advance the step state.
             __threadfence();
-            const unsigned long long fin = atomicAdd(&a.st->argmax_key, 0ull);
+            unsigned long long fin = atomicAdd(&a.st->argmax_key, 0ull);
+            if (TP && a.tp.world > 1) {
+                // vocabulary-parallel lm_head: the step's token is the largest
+                // key over the ranks' slices (every rank takes the same one)
+                const unsigned e = epoch0 + (unsigned)a.tp.index + 1u;
+                for (int r = 0; r < a.tp.world; ++r)
+                    reinterpret_cast<unsigned long long*>(a.tp.peer[r] + kTpKeys)[a.tp.rank] = fin;
+                tp_signal(a.tp, e);
+                if (tp_wait(a.tp, e, &a.st->abort, &a.st->status)) {
+                    const unsigned long long* keys =
+                        reinterpret_cast<const unsigned long long*>(a.tp.peer[a.tp.rank] + kTpKeys);
+                    for (int r = 0; r < a.tp.world; ++r) {
+                        const unsigned long long k = __ldcg(keys + r);
+                        fin = k > fin ? k : fin;
+                    }
+                }
+            }
             a.st->next_token = argmax_index(fin);
             a.st->max_logit = argmax_value(fin);
             a.st->token = argmax_index(fin);

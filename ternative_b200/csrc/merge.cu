@@ -38,6 +38,7 @@ struct MergeDescDev {
     float scale;
     float sf;       // alpha / r, rounded once as the reference does (model.cpp:226)
     int K, N, r;
+    int k0, ld;     // columns [k0, k0 + K) of source rows of ld columns
 };
 
 struct MergeBatch {
@@ -83,6 +84,7 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
     __syncthreads();
 
     const int nchunks = K >> 7;
+    const int src_blocks = D.ld >> 7, blk0 = D.k0 >> 7;   // I2_S blocks per source row, first block
     const int byte_off = (lane & 7) * 4;
     const int shift = 6 - 2 * (lane >> 3);
     for (int c = warp; c < nchunks; c += kMergeWarps) {
@@ -90,10 +92,10 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
         float2 acc[ROWS][2];
 #pragma unroll
         for (int i = 0; i < ROWS; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
-        const float* Ap = D.A + col;
+        const float* Ap = D.A + D.k0 + col;
 #pragma unroll 4
         for (int j = 0; j < r; ++j) {
-            float4 a = __ldg(reinterpret_cast<const float4*>(Ap + (int64_t)j * K));
+            float4 a = __ldg(reinterpret_cast<const float4*>(Ap + (int64_t)j * D.ld));
             float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
             float bj[ROWS];
 #pragma unroll
@@ -115,7 +117,7 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
         for (int i = 0; i < ROWS; ++i) {
             const int row = row0 + i;
             if (row >= N) break;
-            const int64_t blk = (int64_t)row * nchunks + c;
+            const int64_t blk = (int64_t)row * src_blocks + blk0 + c;
             uint32_t word = *reinterpret_cast<const uint32_t*>(D.i2s + blk * 32 + byte_off);
             float2 d01 = make_float2(__fmul_rn(acc[i][0].x, sf2.x), __fmul_rn(acc[i][0].y, sf2.y));
             float2 d23 = make_float2(__fmul_rn(acc[i][1].x, sf2.x), __fmul_rn(acc[i][1].y, sf2.y));
@@ -276,6 +278,9 @@ static tvb_status validate(const tvb_merge_desc& d, tvb_dtype out) {
     TVB_REQUIRE(aligned(d.dst, 16), "merge: dst must be 16-byte aligned");
     TVB_REQUIRE(!d.A || aligned(d.A, 16), "merge: A must be 16-byte aligned");
     TVB_REQUIRE(out != TVB_I8_ROW || d.row_scales, "merge: TVB_I8_ROW needs row_scales");
+    const int ld = d.ld ? d.ld : d.K;
+    TVB_REQUIRE(d.k0 >= 0 && d.k0 % 128 == 0 && ld % 128 == 0 && d.k0 + d.K <= ld,
+                "merge: column slice [%d, %d) of %d columns (multiples of 128)", d.k0, d.k0 + d.K, ld);
     return TVB_OK;
 }
 
@@ -316,6 +321,8 @@ static tvb_status merge_run(const tvb_merge_desc* descs, int n, tvb_dtype out, c
             d.sf = s.r ? s.alpha / (float)s.r : 0.0f;
             d.K = s.K;
             d.N = s.N;
+            d.k0 = s.k0;
+            d.ld = s.ld ? s.ld : s.K;
             b.cta_start[i] = ctas;
             ctas += (s.N + rows - 1) / rows;
         }

@@ -137,3 +137,45 @@ def test_merge_rejects_bad_shapes(backend):
     with pytest.raises(TvbError, match="aligned"):
         backend.apply_lora_i2s(src, 1.0, 128, 1, None, None, 0.0, TVB_F16, dst.data_ptr() + 2,
                                stream=0)
+
+
+def test_merge_tensor_parallel_slices(backend, restated):
+    """Shards of one tensor, merged separately (row slices for column-parallel
+    projections, column slices for row-parallel ones), are bit-identical to the
+    slices of the whole-tensor merge."""
+    import torch
+    K, N, r = 1024, 96, 16
+    i2s, s, A, B = make_case(restated, K, N, r, 777)
+    full = restated.merge(i2s, s, K, N, A, B, 2.0 * r)[1]          # [N][K] F16 bits
+    ti, tA, tB = dev(i2s, torch), dev(A, torch), dev(B, torch)
+    T = 4
+    descs, outs = [], []
+    for rank in range(T):
+        # column-parallel: rows [rank * N/T, ...)
+        n0, nn = rank * N // T, N // T
+        o = torch.empty(nn, K, dtype=torch.float16, device="cuda")
+        descs.append(MergeDesc(ti.data_ptr() + n0 * K // 4, s, K, nn, tA.data_ptr(),
+                               tB.data_ptr() + n0 * r * 4, r, 2.0 * r, o.data_ptr(), None, 0, 0))
+        outs.append(("rows", n0, nn, o))
+        # row-parallel: columns [rank * K/T, ...) of every row
+        k0, kk = rank * K // T, K // T
+        o = torch.empty(N, kk, dtype=torch.float16, device="cuda")
+        descs.append(MergeDesc(ti.data_ptr(), s, kk, N, tA.data_ptr(), tB.data_ptr(), r, 2.0 * r,
+                               o.data_ptr(), None, k0, K))
+        outs.append(("cols", k0, kk, o))
+    backend.merge_batch(descs, TVB_F16, stream=0)
+    torch.cuda.synchronize()
+    for kind, a0, n, o in outs:
+        got = o.cpu().numpy().view(np.uint16)
+        ref = full[a0:a0 + n] if kind == "rows" else full[:, a0:a0 + n]
+        assert np.array_equal(got, ref), (kind, a0)
+
+
+def test_merge_rejects_bad_slice(backend):
+    import torch
+    from ternative_b200 import TvbError
+    o = torch.empty(8, 128, dtype=torch.float16, device="cuda")
+    src = torch.zeros(8 * 256 // 4 + 4, dtype=torch.uint8, device="cuda")
+    d = MergeDesc(src.data_ptr(), 1.0, 128, 8, None, None, 0, 0.0, o.data_ptr(), None, 64, 256)
+    with pytest.raises(TvbError, match="column slice"):
+        backend.merge_batch([d], TVB_F16, stream=0)
