@@ -216,6 +216,80 @@ def config_block(args, cfg):
 
 
 # ---------------------------------------------------------------------------
+def run_tp_8b(args, world, rank):
+    """Batch-1 greedy decode of the 8B-shaped model (hidden 4096, 32 layers,
+    32/8 heads, FFN 14336, vocab 128256; I2_S + rank-32 LoRA alpha 64 merged to
+    F16), tensor-parallel over all ranks of this job: q/k/v and gate/up split by
+    rows, o_proj and down by columns, lm_head by vocabulary rows, partial rows
+    exchanged over NVLink inside the decode-step kernel.  A `tp_prompt`-token
+    random prompt is prefilled first; the timed region is `steps` chained decode
+    steps (CUDA events on the context stream, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from ternative_b200.model import SHAPES, SyntheticModel
+    from ternative_b200.tp import TPModel, shard_config
+
+    cfg = SHAPES["8b"]
+    cfg = dataclasses.replace(cfg, max_seq_len=max(cfg.max_seq_len, args.tp_prompt + args.warmup
+                                                   + args.steps + 8))
+
+    def all_gather(obj):
+        if world == 1:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
+    synth = SyntheticModel.generate(cfg, rank=32, alpha=64.0, seed=0)
+    m = TPModel(synth, world, rank, all_gather)
+    be = m.backend
+    stream = torch.cuda.ExternalStream(be.stream)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, args.tp_prompt).astype(np.int32)
+    be.clear_kv_d()
+    t0 = time.time()
+    _, tok = be.prefill(prompt, want_logits=False)
+    prefill_s = time.time() - t0
+    pos = len(prompt)
+    be.decode_enqueue(tok, pos, args.warmup)
+    be.sync_d()
+    pos += args.warmup
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    be.decode_enqueue(0, pos, args.steps)   # the device chains its own greedy tokens
+    e1.record(stream)
+    e1.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    local = shard_config(cfg, world)
+    n_w = sum(2 * a * b for a, b in [(local.num_heads * 128, 4096), (2 * local.num_kv_heads * 128, 4096),
+                                     (4096, local.num_heads * 128), (2 * local.intermediate_size, 4096),
+                                     (4096, local.intermediate_size)]) * cfg.num_layers
+    n_w += 2 * (cfg.vocab_size // world) * cfg.hidden_size
+    kv = cfg.num_layers * 2 * (pos + args.steps // 2) * local.num_kv_heads * 128 * 4
+    hbm, kind = peaks()
+    per_gpu = (n_w + kv) / (ms / args.steps * 1e-3) / 1e9
+    res = {"workload": f"8B-shaped batch-1 greedy decode, tensor-parallel over {world} GPU(s), "
+                       f"after a {args.tp_prompt}-token prompt",
+           "n_gpus": world, "tok_s": args.steps / (ms * 1e-3), "ms_per_token": ms / args.steps,
+           "per_gpu_bytes_per_token": n_w + kv, "per_gpu_GB/s": per_gpu, "frac_of_hbm": per_gpu / hbm,
+           "peak_kind": kind, "prefill_s": prefill_s,
+           "prefill_path": "batched tensor cores" if world == 1 else "row-by-row decode steps"}
+    if world > 1:
+        dist.barrier()
+    m.close()
+    del synth
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -225,6 +299,14 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if args.only_tp:
+        res = run_tp_8b(args, world, rank)
+        if rank == 0:
+            print(json.dumps({"tp_8b": res}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     cfg = SHAPES[args.config]
     if args.layers:
         # profiling only: the same shapes with fewer layers (smaller device footprint)
@@ -437,6 +519,12 @@ def run_ours(args, world, rank, local):
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                    "sample": f"unavailable: {e!r}"}
 
+    tp8 = None
+    if not args.no_tp:
+        try:
+            tp8 = run_tp_8b(args, world, rank)
+        except Exception as e:   # reported, not fatal to the headline line
+            tp8 = {"unavailable": repr(e)}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -446,7 +534,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline, "gemv_standalone": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps,   # one decode_step_kernel launch per token
-            "clocks": clk.report(), "merge": merge, "prefill": prefill,
+            "clocks": clk.report(), "merge": merge, "prefill": prefill, "tp_8b": tp8,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -468,6 +556,11 @@ def main():
                     help="profiling: run only W+K launches of one part, print nothing")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling with --only: use this many layers of the shape")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="skip the tensor-parallel 8B decode measurement")
+    ap.add_argument("--tp-prompt", type=int, default=512)
+    ap.add_argument("--only-tp", action="store_true",
+                    help="run only the tensor-parallel 8B decode measurement and print its JSON")
     args = ap.parse_args()
     if args.warmup < 3 and args.only is None:
         ap.error("--warmup must be >= 3")

@@ -38,14 +38,10 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 
 // Grid barrier, split so a CTA can do input-independent work between its
 // arrival and its wait.  Arrival: release-add on the counter (no round trip).
-// `sys`: the CTA also wrote peer memory, which must be ordered before the
-// arrival at system scope (a rank signals its peers after its barrier).
-__device__ __forceinline__ void grid_arrive(StepState* st, bool sys = false) {
+__device__ __forceinline__ void grid_arrive(StepState* st) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        if (sys) __threadfence_system();
+    if (threadIdx.x == 0)
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&st->bar_ctr) : "memory");
-    }
 }
 
 // Wait until `target` arrivals (barrier n of this launch: n * gridDim.x).
@@ -74,34 +70,13 @@ __device__ __forceinline__ bool grid_wait(StepState* st, unsigned target) {
     return s_ok != 0;
 }
 
-// Barrier that ends a row-parallel phase under tensor parallelism: CTA 0
-// waits for this rank's `target` arrivals and signals every rank that this
-// rank's partial rows are written; every CTA then waits until all ranks have
-// signalled `epoch`.  Both waits are bounded like grid_wait.
-__device__ __forceinline__ bool tp_grid_exchange(StepState* st, const TpArgs& t, unsigned target,
-                                                 unsigned epoch) {
+// End of a row-parallel phase under tensor parallelism: every CTA of every
+// rank counts its arrival on every rank (after its partial rows), then waits
+// until its own rank has counted all of them for exchange number n.
+__device__ __forceinline__ bool tp_exchange_wait(StepState* st, const TpArgs& t, unsigned n, int G) {
     __shared__ int s_tp_ok;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        if (blockIdx.x == 0) {
-            const long long t0 = clock64();
-            while (ld_acquire_gpu(&st->bar_ctr) < target) {
-                if (ld_acquire_gpu(&st->abort)) {
-                    ok = 0;
-                    break;
-                }
-                if (clock64() - t0 > kSpinLimitCycles) {
-                    atomicOr(&st->abort, 1u);
-                    atomicOr(&st->status, kStatusTimeout);
-                    ok = 0;
-                    break;
-                }
-            }
-            if (ok) tp_signal(t, epoch);
-        }
-        if (ok) ok = tp_wait(t, epoch, &st->abort, &st->status) ? 1 : 0;
-        s_tp_ok = ok;
-    }
+    if (threadIdx.x == 0)
+        s_tp_ok = tp_count_wait(t, n * (unsigned)t.world * (unsigned)G, &st->abort, &st->status) ? 1 : 0;
     __syncthreads();
     return s_tp_ok != 0;
 }
@@ -128,10 +103,10 @@ __device__ __forceinline__ void phase_prepare(const Phase& ph, unsigned char* sm
 
 template <bool TP>
 __device__ __forceinline__ void phase_gemv(const Phase& ph, unsigned char* smem, int G, int pos, int token,
-                                           ChunkBuf& buf, GemvArgmax& best, unsigned epoch0) {
+                                           ChunkBuf& buf, GemvArgmax& best, unsigned push0) {
 #define X(M, W, R)                                                                \
     if (ph.mode == M && ph.wt == W) {                                             \
-        gemv_run<M, W, R, TP>(ph.g, smem, G, pos, token, buf, best, epoch0);      \
+        gemv_run<M, W, R, TP>(ph.g, smem, G, pos, token, buf, best, push0);       \
         return;                                                                   \
     }
     TVB_GEMV_CASES(X)
@@ -149,11 +124,11 @@ __device__ __forceinline__ void load_phase(Phase* dst, const Phase* src) {
 // buffered), then the per-phase layouts (gemv_smem_layout / attention scratch).
 static_assert(2 * sizeof(Phase) <= 1024, "phase descriptors must fit the reserved area");
 
-// n_tp: cross-rank exchanges in the phase table (0 without tensor parallelism).
-// TP selects the tensor-parallel instantiation.
+// Tensor parallelism (TP instantiation): n_push row-parallel exchanges and
+// n_argmax (0 or 1) argmax exchanges in the phase table.
 template <bool TP>
 __global__ void __launch_bounds__(kGemvThreads, 1)
-decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st, int n_tp) {
+decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st, int n_push, int n_argmax) {
     extern __shared__ __align__(128) unsigned char smem[];
     Phase* desc = reinterpret_cast<Phase*>(smem);   // desc[p & 1]
     const int warp = threadIdx.x >> 5;
@@ -163,6 +138,7 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
     const int pos = __ldcg(&st->pos);
     const int token = __ldcg(&st->token);
     const unsigned epoch0 = __ldcg(&st->tp_epoch);
+    const unsigned push0 = __ldcg(&st->tp_pushes);
 
     ChunkBuf buf;
     load_phase(&desc[0], &phases[0]);
@@ -182,19 +158,21 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
         const TpArgs& tp = ph.g.tp;
         if (ph.kind == PK_GEMV) {
             GemvArgmax best{-INFINITY, 0};
-            phase_gemv<TP>(ph, smem, G, pos, token, buf, best, epoch0);
+            phase_gemv<TP>(ph, smem, G, pos, token, buf, best, push0);
             if (ph.mode == GM_LMHEAD) lmhead_finish<TP>(ph.g, best, epoch0);
         } else {
             __syncthreads();
             if (b < ph.at.nkv * ph.at.nsplit) attn_item(ph.at, b, smem + 1024, pos);
         }
-        if (p + 1 < n_phases) {
-            grid_arrive(st, exchange);   // this phase's outputs are written (includes __syncthreads)
+        // A row-parallel exchange is waited for even after the last phase: the
+        // next launch's first exchange reuses this one's slot parity.
+        if (p + 1 < n_phases || exchange) {
+            grid_arrive(st);   // this phase's outputs are written (includes __syncthreads)
+            if (exchange && threadIdx.x == 0) tp_count_arrive(tp);
             // input-independent work for the next phase overlaps the barrier
-            phase_prepare(next, smem, G, b, warp, pos, buf);
-            const unsigned target = (unsigned)(p + 1) * (unsigned)G;
-            ok = exchange ? tp_grid_exchange(st, tp, target, epoch0 + (unsigned)tp.index + 1u)
-                          : grid_wait(st, target);
+            if (p + 1 < n_phases) phase_prepare(next, smem, G, b, warp, pos, buf);
+            ok = exchange ? tp_exchange_wait(st, tp, push0 + (unsigned)tp.index + 1u, G)
+                          : grid_wait(st, (unsigned)(p + 1) * (unsigned)G);
         }
     }
     // last CTA out resets the barrier for the next launch
@@ -204,7 +182,8 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
         if (atomicAdd(&st->exit_ctr, 1u) == (unsigned)G - 1u) {
             st->bar_ctr = 0u;
             st->exit_ctr = 0u;
-            st->tp_epoch = epoch0 + (unsigned)n_tp;
+            st->tp_epoch = epoch0 + (unsigned)n_argmax;
+            st->tp_pushes = push0 + (unsigned)n_push;
             __threadfence();
         }
     }

@@ -169,7 +169,7 @@ struct tvb_context {
     float* tp_peer[kMaxTp] = {};
     bool tp_ready = false;
     float* e_x2 = nullptr;
-    int n_tp_step = 0, n_tp_layers = 0;
+    int n_push = 0;   // row-parallel exchanges per launch (both graphs)
     uint16_t* pf_w16 = nullptr;
     size_t pf_w16_elems = 0;
 };
@@ -314,7 +314,7 @@ std::vector<Phase> build_phases(tvb_context* c) {
             ph.push_back(p);
         }
     }
-    c->n_tp_layers = xi;
+    c->n_push = xi;
     {   // final norm + tied lm_head + argmax
         Phase p = gemv(GM_LMHEAD, WT_F16);
         const int vs = c->V / c->tp_world;   // this rank's vocabulary slice
@@ -327,11 +327,10 @@ std::vector<Phase> build_phases(tvb_context* c) {
         p.g.y = c->e_logits;
         if (tp) {
             p.g.tp.vocab0 = c->tp_rank * vs;
-            p.g.tp.index = xi++;   // argmax over the ranks' slices
+            p.g.tp.index = 0;   // the launch's argmax exchange over the ranks' slices
         }
         ph.push_back(p);
     }
-    c->n_tp_step = xi;
     return ph;
 }
 
@@ -342,7 +341,7 @@ int phase_units(const Phase& p) {
     return (p.g.N + R - 1) / R;
 }
 
-tvb_status capture(tvb_context* c, int n_phases, int n_tp, cudaGraphExec_t* out) {
+tvb_status capture(tvb_context* c, int n_phases, int n_argmax, cudaGraphExec_t* out) {
     if (*out) {
         cudaGraphExecDestroy(*out);
         *out = nullptr;
@@ -360,9 +359,9 @@ tvb_status capture(tvb_context* c, int n_phases, int n_tp, cudaGraphExec_t* out)
     cfg.numAttrs = 1;
     cudaError_t le = c->tp_world > 1
                          ? cudaLaunchKernelEx(&cfg, decode_step_kernel<true>, (const Phase*)c->d_phases,
-                                              n_phases, c->st, n_tp)
+                                              n_phases, c->st, c->n_push, n_argmax)
                          : cudaLaunchKernelEx(&cfg, decode_step_kernel<false>, (const Phase*)c->d_phases,
-                                              n_phases, c->st, n_tp);
+                                              n_phases, c->st, 0, 0);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (le != cudaSuccess) {
@@ -407,8 +406,8 @@ tvb_status ensure_graphs(tvb_context* c) {
     TVB_CUDA(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
     c->n_phases = (int)ph.size();
     c->step_smem = smem;
-    TVB_TRY(capture(c, c->n_phases, c->n_tp_step, &c->g_step));
-    TVB_TRY(capture(c, c->n_phases - 1, c->n_tp_layers, &c->g_layers));
+    TVB_TRY(capture(c, c->n_phases, 1, &c->g_step));
+    TVB_TRY(capture(c, c->n_phases - 1, 0, &c->g_layers));
     c->dirty = false;
     return TVB_OK;
 }

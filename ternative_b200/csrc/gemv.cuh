@@ -52,25 +52,30 @@ struct StepState {
     unsigned bar_ctr;    // grid-barrier arrivals of the running decode-step launch
     unsigned exit_ctr;   // CTAs that left the running launch
     unsigned abort;      // set when a barrier wait gave up; every CTA then leaves
-    unsigned tp_epoch;   // tensor parallelism: cross-rank exchanges completed so far
+    unsigned tp_epoch;   // tensor parallelism: argmax exchanges completed so far
+    unsigned tp_pushes;  // tensor parallelism: row-parallel exchanges completed so far
 };
 
 // Tensor parallelism (one rank per GPU).  Every rank owns an exchange buffer
 // that its peers write over NVLink (peer pointers from CUDA IPC):
-//   [0, 64)     flags: flags[src] = epoch of the last exchange rank src signalled
+//   [0, 8)      flags: flags[src] = number of the last argmax exchange rank src
+//               signalled
+//   [32]        arrivals: CTAs (of all ranks) that finished a row-parallel
+//               exchange; exchange n is complete at n * world * grid
 //   [64, 80)    argmax keys of the lm_head slices (64-bit, keys[src])
-//   [128, ...)  two slots (exchange epoch parity) of world x ld floats: slot[src]
-//               holds rank src's partial output rows and, at [H], its partial
-//               sum of squares of the sub-norm input
+//   [128, ...)  two slots (exchange number parity) of world x ld floats:
+//               slot[src] holds rank src's partial output rows and, at [H],
+//               its partial sum of squares of the sub-norm input
 constexpr int kMaxTp = 8;
-constexpr int kTpFlags = 0, kTpKeys = 64, kTpSlots = 128;
+constexpr int kTpFlags = 0, kTpCount = 32, kTpKeys = 64, kTpSlots = 128;
 
 // A zero-initialised TpArgs (world 0) means no tensor parallelism.
 struct TpArgs {
     float* peer[kMaxTp];  // every rank's exchange buffer (this rank's at [rank])
     int world, rank;
     int ld;               // floats per rank in a slot (H + 4)
-    int index;            // >= 0: this phase ends with exchange `index` of the step
+    int index;            // >= 0: row-parallel exchange `index` of the launch (o_proj, down),
+                          // or the lm_head's argmax exchange
     int fold;             // >= 0: input = residual + sum of exchange `fold`'s partials
     int norm_n;           // fold: full length of the sub-norm whose partials arrive
     float* x_out;         // fold: where the folded residual is stored (CTA-partitioned)
@@ -90,10 +95,39 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Tell every rank that this rank's writes for exchange `epoch` are done (one
-// thread; the writes it covers were ordered before it at system scope).
+// Row-parallel exchange, arrival (thread 0 after the CTA's __syncthreads): the
+// CTA's partial rows are ordered before the count at system scope (fence +
+// relaxed adds, a release pattern), and every rank's arrival count grows by 1.
+__device__ __forceinline__ void tp_count_arrive(const TpArgs& t) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < t.world; ++r)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(
+                         reinterpret_cast<unsigned*>(t.peer[r] + kTpCount))
+                     : "memory");
+}
+
+// Row-parallel exchange, wait (thread 0): until this rank's arrival count
+// reaches `target` (bounded like every wait; on a timeout the abort latch and
+// the timeout bit are raised).
+__device__ __forceinline__ bool tp_count_wait(const TpArgs& t, unsigned target, unsigned* abort_flag,
+                                              unsigned* status) {
+    const unsigned* cnt = reinterpret_cast<const unsigned*>(t.peer[t.rank] + kTpCount);
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys(cnt) - target) < 0) {
+        if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
+        if (clock64() - t0 > kSpinLimitCycles) {
+            atomicOr(abort_flag, 1u);
+            atomicOr(status, kStatusTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Tell every rank that this rank's writes for argmax exchange `epoch` are done
+// (one thread; the writes it covers were ordered before it at system scope).
 __device__ __forceinline__ void tp_signal(const TpArgs& t, unsigned epoch) {
-    __threadfence_system();
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int r = 0; r < t.world; ++r)
         st_release_sys(reinterpret_cast<unsigned*>(t.peer[r] + kTpFlags) + t.rank, epoch);
 }
@@ -348,9 +382,10 @@ __device__ __forceinline__ void gemv_stage(const GemvArgs& a, unsigned char* sme
 // operands, activation prologue, chunk stream, epilogue.
 // TP: the tensor-parallel decode kernel's instantiation (folds and pushes of
 // partial rows); the single-GPU kernels compile those paths out.
+// push0: row-parallel exchanges completed before this launch (slot parity).
 template <int MODE, int WT, int R, bool TP = false>
 __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem, int G, int pos, int token,
-                                         ChunkBuf& buf, GemvArgmax& best, unsigned epoch0 = 0) {
+                                         ChunkBuf& buf, GemvArgmax& best, unsigned push0 = 0) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, b = blockIdx.x;
     const int K = a.K;
     const int esz = (WT == WT_F16) ? 2 : 1;
@@ -388,7 +423,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     const float* tp_in = nullptr;
     float tp_inv = 1.0f;
     if (fold) {
-        tp_in = tp_slot(a.tp.peer[a.tp.rank], a.tp, epoch0 + (unsigned)a.tp.fold + 1u);
+        tp_in = tp_slot(a.tp.peer[a.tp.rank], a.tp, push0 + (unsigned)a.tp.fold + 1u);
         float ss_all = 0.f;
         for (int r = 0; r < a.tp.world; ++r) ss_all += __ldcg(tp_in + (size_t)r * a.tp.ld + K);
         // tensor.cpp:672-673 over the full sub-norm length (norm_n == 0: no sub-norm)
@@ -523,7 +558,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     if (push) {
         // the sub-norm factor needs every rank's sum of squares: apply it when folding
         inv = 1.0f;
-        const unsigned e = epoch0 + (unsigned)a.tp.index + 1u;
+        const unsigned e = push0 + (unsigned)a.tp.index + 1u;
         tp_off = (size_t)(tp_slot(a.tp.peer[0], a.tp, e) - a.tp.peer[0]) + (size_t)a.tp.rank * a.tp.ld;
         if (b == 0 && tid == 0)
             for (int r = 0; r < a.tp.world; ++r) a.tp.peer[r][tp_off + a.N] = ss_local;
