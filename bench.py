@@ -314,11 +314,13 @@ def run_ours(args, world, rank, local):
     synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0)
     be = CUDABackend()
     if args.only == "merge":
-        # profiling: one F16 merge launch over layer 0's 7 projections
+        # profiling: the F16 merge of layer 0's 7 projections, exact (CUDA-core)
+        # and tensor-core delta, W + K times each
         outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.float16, device="cuda")
                  for n in PROJ}]
         for _ in range(args.warmup + args.steps):
             be.merge_batch(synth.merge_descs(outs, layers=[0]), TVB_F16, stream=0)
+            be.merge_batch_tc(synth.merge_descs(outs, layers=[0]), TVB_F16, stream=0)
         torch.cuda.synchronize()
         return
     m = Model.load(synth, backend=be)
@@ -329,6 +331,14 @@ def run_ours(args, world, rank, local):
         y = torch.empty(N, device="cuda")
         for i in range(args.warmup + args.steps):
             be.gemv_d2d(y, x, m.weights[i % cfg.num_layers]["w_gate"], K, N)
+        be.sync_d()
+        return
+    if args.only == "prefill":
+        # profiling: W + K batched prefills of a --prefill-len random prompt
+        ptoks = np.random.default_rng(2).integers(0, cfg.vocab_size, args.prefill_len).astype(np.int32)
+        for _ in range(args.warmup + args.steps):
+            be.clear_kv_d()
+            be.prefill(ptoks, want_logits=False)
         be.sync_d()
         return
     if args.only == "decode":
@@ -501,6 +511,57 @@ def run_ours(args, world, rank, local):
     merge["r16_i8row"] = {"ms": ms_i8, "GB/s": (n_w / 4 + lora_b + n_w) / (ms_i8 * 1e6)}
     del outs, scs
 
+    # rank-64 LoRA (alpha 128) on the same I2_S codes: the merge microbench's
+    # configuration, exact (CUDA cores, bit-identical) and tensor-core (F16
+    # within 1 ulp) deltas to F16, exact per-row INT8
+    from ternative_b200._lib import MergeDesc
+    g64 = torch.Generator(device="cuda")
+    g64.manual_seed(64)
+    lora64, descs64 = [], []
+    outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.float16, device="cuda") for n in PROJ}
+            for _ in range(cfg.num_layers)]
+    for li in range(cfg.num_layers):
+        for name in PROJ:
+            N, K = proj_shape(cfg, name)
+            A = torch.randn(64, K, generator=g64, device="cuda") / np.sqrt(K)
+            B = torch.randn(N, 64, generator=g64, device="cuda") * 1e-3
+            lora64.append((A, B))
+            t = synth.layers[li][name]
+            descs64.append(MergeDesc(t.i2s.data_ptr(), t.scale, K, N, A.data_ptr(), B.data_ptr(), 64, 128.0,
+                                     outs[li][name].data_ptr(), None, 0, 0))
+    lora64_b = sum(4 * 64 * (proj_shape(cfg, n)[0] + proj_shape(cfg, n)[1]) for n in PROJ) * cfg.num_layers
+    for key, fn in (("r64_f16_exact", be.merge_batch), ("r64_f16_tc", be.merge_batch_tc)):
+        fn(descs64, TVB_F16)
+        be.sync_d()
+        m0.record(stream)
+        fn(descs64, TVB_F16)
+        m1.record(stream)
+        m1.synchronize()
+        ms = m0.elapsed_time(m1)
+        merge[key] = {"ms": ms, "GB/s": (n_w / 4 + lora64_b + 2 * n_w) / (ms * 1e6),
+                      "frac_of_hbm": (n_w / 4 + lora64_b + 2 * n_w) / (ms * 1e6) / hbm,
+                      "GFLOP/s": 2 * 64 * n_w / (ms * 1e6)}
+    del outs
+    outs = [{n: torch.empty(proj_shape(cfg, n), dtype=torch.int8, device="cuda") for n in PROJ}
+            for _ in range(cfg.num_layers)]
+    scs = [{n: torch.empty(proj_shape(cfg, n)[0], dtype=torch.float32, device="cuda") for n in PROJ}
+           for _ in range(cfg.num_layers)]
+    for d, (li, name) in zip(descs64, [(li, n) for li in range(cfg.num_layers) for n in PROJ]):
+        d.dst = outs[li][name].data_ptr()
+        d.row_scales = scs[li][name].data_ptr()
+    be.merge_batch(descs64, TVB_I8_ROW)
+    be.sync_d()
+    m0.record(stream)
+    be.merge_batch(descs64, TVB_I8_ROW)
+    m1.record(stream)
+    m1.synchronize()
+    ms = m0.elapsed_time(m1)
+    merge["r64_i8row_exact"] = {"ms": ms, "GB/s": (n_w / 4 + lora64_b + n_w) / (ms * 1e6)}
+    merge["note"] = ("all 210 projections of the 2B shape in one call; GB/s = (I2_S codes + LoRA A,B + "
+                     "output) / time; exact = CUDA-core delta bit-identical to apply_lora, tc = "
+                     "tcgen05 delta (F16 within 1 ulp)")
+    del outs, scs, lora64, descs64
+
     # ---- CPU baseline: the reference's own decode on this host --------------------
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -552,13 +613,15 @@ def main():
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["decode", "gemv", "merge"], default=None,
+    ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill"], default=None,
                     help="profiling: run only W+K launches of one part, print nothing")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling with --only: use this many layers of the shape")
     ap.add_argument("--no-tp", action="store_true",
                     help="skip the tensor-parallel 8B decode measurement")
     ap.add_argument("--tp-prompt", type=int, default=512)
+    ap.add_argument("--prefill-len", type=int, default=1024,
+                    help="profiling with --only prefill: prompt length")
     ap.add_argument("--only-tp", action="store_true",
                     help="run only the tensor-parallel 8B decode measurement and print its JSON")
     args = ap.parse_args()

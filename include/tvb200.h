@@ -110,6 +110,15 @@ typedef struct {
  * sharded-by-tensor load-time merge: give each rank its own subset. */
 tvb_status tvb_merge_batch(const tvb_merge_desc* descs, int n, tvb_dtype out, void* stream);
 
+/* The same merge with the rank-r delta as a tensor-core contraction
+ * (tcgen05.mma on F16 hi + lo splits of A and B, F32 accumulation): TVB_F16
+ * output within one unit in the last place of tvb_merge_batch's (which is
+ * bit-identical to apply_lora), for ranks up to 64.  Other outputs (F32,
+ * TVB_I8_ROW, whose codes must be bit-exact) and larger ranks take the
+ * tvb_merge_batch path.  Uses a stream-ordered workspace of about
+ * 260 B x (N + K) per tensor for the duration of the call. */
+tvb_status tvb_merge_batch_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, void* stream);
+
 /* tensor.cpp:1006-1050: I2_S codes -> F32 (n % 128 == 0). */
 tvb_status tvb_i2s_unpack(const uint8_t* i2s, int64_t n, float scale, float* out, void* stream);
 

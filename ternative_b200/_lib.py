@@ -84,6 +84,7 @@ _SIGS = {
     "tvb_release": [_P],
     "tvb_merge_i2s_lora": [_P, _F, _I, _I, _P, _P, _I, _F, _I, _P, _P, _P],
     "tvb_merge_batch": [C.POINTER(MergeDesc), _I, _I, _P],
+    "tvb_merge_batch_tc": [C.POINTER(MergeDesc), _I, _I, _P],
     "tvb_i2s_unpack": [_P, _I64, _F, _P, _P],
     "tvb_quantize_int8": [_P, _I, _I, _I, _P, _P, _P],
     "tvb_gemv_f16": [_P, _P, _P, _I, _I, _P],

@@ -217,6 +217,11 @@ class CUDABackend:
         arr = (MergeDesc * len(descs))(*descs)
         call("tvb_merge_batch", arr, len(descs), out_dtype, self.stream if stream is None else stream)
 
+    def merge_batch_tc(self, descs: Sequence[MergeDesc], out_dtype: int, stream=None):
+        """merge_batch with the LoRA delta on the tensor cores (F16 within 1 ulp)."""
+        arr = (MergeDesc * len(descs))(*descs)
+        call("tvb_merge_batch_tc", arr, len(descs), out_dtype, self.stream if stream is None else stream)
+
     def i2s_unpack(self, i2s, n, scale, out, stream=None):
         call("tvb_i2s_unpack", _ptr(i2s), n, scale, _ptr(out), self.stream if stream is None else stream)
 

@@ -75,6 +75,15 @@ __host__ __device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
     return (uint16_t)(sign | ((uint32_t)ne << 10) | (m >> 13));
 }
 
+// The same truncation with the hardware round-toward-zero conversion where the
+// two agree: finite |f| < 65536 (RTZ keeps the top 10 mantissa bits, subnormals
+// included, like the bit routine).  Larger magnitudes (the reference gives
+// infinity where RTZ saturates at 65504) and NaN take the bit routine.
+__device__ __forceinline__ uint16_t f32_to_f16_trunc_fast(float f) {
+    if (fabsf(f) < 65536.0f) return __half_as_ushort(__float2half_rz(f));
+    return f32_to_f16_trunc(f);
+}
+
 // Round half away from zero (std::round) for |x| < 2^23, built from truncation.
 __device__ __forceinline__ float round_half_away(float x) {
     float t = truncf(x);

@@ -359,12 +359,19 @@ __device__ __forceinline__ void gemv_stage(const GemvArgs& a, unsigned char* sme
         for (int k4 = tid; k4 < (a.K >> 2); k4 += kGemvThreads) nw4[k4] = __ldg(w4 + k4);
     }
     float* pre_scale = reinterpret_cast<float*>(smem + L.pre_off);
+    float* pre_res = pre_scale + g.rows_cap;
     for (int lr = tid; lr < g.nrows; lr += kGemvThreads) {
         int m, row;
         float sc = 1.0f;
-        if (group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row))
-            sc = a.row_scale[m] ? __ldg(a.row_scale[m] + row) : a.tscale[m];
+        const bool v = group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row);
+        if (v) sc = a.row_scale[m] ? __ldg(a.row_scale[m] + row) : a.tscale[m];
         pre_scale[lr] = sc;
+        // The residual a RESID phase adds to was last written two phases
+        // earlier (o_proj: the previous layer's down or the layer-0 gather;
+        // down: o_proj), with a grid barrier in between, so it can be staged
+        // before the wait for this phase's inputs.  (Under tensor parallelism
+        // the residual is folded by the next phase instead.)
+        if (MODE == GM_RESID && !(a.tp.world > 1 && a.tp.index >= 0)) pre_res[lr] = v ? __ldcg(a.y + row) : 0.f;
     }
     if (MODE == GM_QKV) {
         float* pre_cos = pre_scale + 2 * g.rows_cap;
@@ -403,12 +410,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
     // row-parallel shard (o_proj, down): partial rows to every rank.  The
     // lm_head phase also carries an exchange index (its argmax), but no rows.
     const bool push = TP && MODE == GM_RESID && a.tp.world > 1 && a.tp.index >= 0;
-    if (MODE == GM_RESID && !push) {
-        for (int lr = tid; lr < g.nrows; lr += kGemvThreads) {
-            int m, row;
-            pre_res[lr] = group_row<MODE, R>(a, g.U0 + lr / R, lr % R, m, row) ? __ldcg(a.y + row) : 0.f;
-        }
-    }
+    // (RESID: the residual operands were staged by gemv_stage)
 
     // ---- prologue: activation vector into shared memory ------------------------
     // One vectorised pass stores x*w and accumulates sum(x^2); 1/rms is applied

@@ -132,8 +132,8 @@ merge_kernel(const __grid_constant__ MergeBatch batch) {
                 *reinterpret_cast<float4*>(static_cast<float*>(D.dst) + off) =
                     make_float4(v01.x, v01.y, v23.x, v23.y);
             } else {
-                uint32_t h0 = f32_to_f16_trunc(v01.x) | ((uint32_t)f32_to_f16_trunc(v01.y) << 16);
-                uint32_t h1 = f32_to_f16_trunc(v23.x) | ((uint32_t)f32_to_f16_trunc(v23.y) << 16);
+                uint32_t h0 = f32_to_f16_trunc_fast(v01.x) | ((uint32_t)f32_to_f16_trunc_fast(v01.y) << 16);
+                uint32_t h1 = f32_to_f16_trunc_fast(v23.x) | ((uint32_t)f32_to_f16_trunc_fast(v23.y) << 16);
                 if (MODE == kOutF16) {
                     *reinterpret_cast<uint2*>(static_cast<uint16_t*>(D.dst) + off) = make_uint2(h0, h1);
                 } else {
@@ -336,6 +336,10 @@ static tvb_status merge_run(const tvb_merge_desc* descs, int n, tvb_dtype out, c
         if (st_ != TVB_OK) return st_;
     }
     return TVB_OK;
+}
+
+tvb_status merge_exact(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st) {
+    return merge_run(descs, n, out, st);
 }
 
 }  // namespace tvb

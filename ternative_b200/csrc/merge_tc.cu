@@ -1,0 +1,410 @@
+// Load-time merge with the LoRA delta on the tensor cores (tvb_merge_batch_tc).
+//
+//   merged[n][k] = scale * map(code[n][k]) + (sum_j B[n][j] * A[j][k]) * (alpha / r)
+//
+// as in apply_lora (src/model.cpp:180-258), F16 output by truncation
+// (tensor.cpp:33-57).  The rank-r contraction runs as tcgen05.mma
+// (kind::f16, F32 accumulation in TMEM): B and A^T are split once per tensor
+// into F16 hi + lo planes with power-of-two exponents per row of B and per
+// column of A (largest magnitude of each in [2^14, 2^15)), and three MMAs per
+// 16-wide k-step (hi.hi + hi.lo + lo.hi) give the delta to ~2^-21 of its
+// largest term.  The F16 results are within one unit in the last place of the
+// reference's sequential F32 sum (usually identical); tvb_merge_batch keeps the
+// bit-exact CUDA-core path for F32, INT8 and ranks above 64.
+//
+// One CTA per 128-row stripe of a tensor: the stripe's B rows (hi, lo) stay in
+// shared memory, the A^T column tiles (256 columns, hi, lo) stream through a
+// double buffer, the MMAs of tile t run while the epilogue of tile t - 1
+// (I2_S unpack, scale, F16 cast, 128-bit stores) reads the other half of a
+// 512-column TMEM accumulator.
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+#include <algorithm>
+
+namespace tvb {
+
+constexpr int kMtRows = 128;                  // W rows per stripe (MMA M)
+constexpr int kMtCols = 256;                  // W columns per tile (MMA N)
+constexpr int kMtRank = 64;                   // padded rank: one 128-byte swizzle row of F16
+constexpr int kMtThreads = 512;
+constexpr int kMtMaxDescs = 192;
+constexpr int kMtAop = kMtRows * 128;         // bytes per plane of the stripe's B rows
+constexpr int kMtBop = kMtCols * 128;         // bytes per plane of an A^T tile
+// the column exponents rotate over 3 tiles: tile t + 1 is staged while the
+// epilogue of tile t - 1 still reads its own
+constexpr int kMtSmem = 2 * kMtAop + 4 * kMtBop + 3 * kMtCols * 4 + kMtRows * 4 + 64 + 1024;
+
+struct MtDesc {
+    const uint8_t* i2s;      // whole tensor's codes (row pitch ld / 4 bytes)
+    const uint16_t* bh;      // [N][64] F16 hi of B * 2^-eb[n]
+    const uint16_t* bl;
+    const int* eb;           // [N]
+    const uint16_t* ath;     // [K][64] F16 hi of A^T * 2^-ea[k]
+    const uint16_t* atl;
+    const int* ea;           // [K]
+    uint16_t* dst;           // [N][K] F16
+    const float* A;          // LoRA A [r][ld] (whole tensor's columns)
+    const float* B;          // LoRA B [N][r]
+    float scale;             // I2_S per-tensor scale
+    float sf;                // alpha / r
+    int K, N, r, k0, ld;
+};
+
+struct MtBatch {
+    MtDesc d[kMtMaxDescs];
+    int cta_start[kMtMaxDescs + 1];   // merge CTAs (128-row stripes)
+    int row_start[kMtMaxDescs + 1];   // prep warps (rows of B)
+    int col_start[kMtMaxDescs + 1];   // prep threads (columns of A)
+    int n;
+};
+
+// Descriptor owning global unit `u` of a start table.
+__device__ __forceinline__ int mt_owner(const int* start, int n, int u) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ int mt_find(const MtBatch& b, int cta) {
+    int lo = 0, hi = b.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (b.cta_start[mid] <= cta) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Power-of-two exponent putting |m| in [2^14, 2^15) (0 for zero rows).
+__device__ __forceinline__ int mt_exp(float m) {
+    return (m > 0.f && isfinite(m)) ? max(ilogbf(m) - 14, -100) : 0;
+}
+
+__device__ __forceinline__ void mt_split(float v, float sc, __half& hi, __half& lo) {
+    const float f = v * sc;
+    hi = __float2half_rn(f);
+    lo = __float2half_rn(f - __half2float(hi));
+}
+
+// B rows -> hi/lo planes: one warp per row (rank <= 64: lanes own j, j + 32).
+__global__ void mt_prep_b(const __grid_constant__ MtBatch b) {
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int lo = mt_owner(b.row_start, b.n, gw);
+    const MtDesc& d = b.d[lo];
+    const int n = gw - b.row_start[lo];
+    if (n < 0 || n >= d.N) return;
+    const float* B = d.B;
+    const float v0 = (lane < d.r) ? B[(size_t)n * d.r + lane] : 0.f;
+    const float v1 = (lane + 32 < d.r) ? B[(size_t)n * d.r + lane + 32] : 0.f;
+    const int e = mt_exp(warp_max(fmaxf(fabsf(v0), fabsf(v1))));
+    const float sc = ldexpf(1.0f, -e);
+    __half h0, l0, h1, l1;
+    mt_split(v0, sc, h0, l0);
+    mt_split(v1, sc, h1, l1);
+    __half* bh = reinterpret_cast<__half*>(const_cast<uint16_t*>(d.bh)) + (size_t)n * kMtRank;
+    __half* bl = reinterpret_cast<__half*>(const_cast<uint16_t*>(d.bl)) + (size_t)n * kMtRank;
+    bh[lane] = h0;
+    bh[lane + 32] = h1;
+    bl[lane] = l0;
+    bl[lane + 32] = l1;
+    if (lane == 0) const_cast<int*>(d.eb)[n] = e;
+}
+
+// Columns [k0, k0 + K) of A [r][ld] -> A^T hi/lo planes: one thread per column.
+__global__ void mt_prep_a(const __grid_constant__ MtBatch b) {
+    const int gc = blockIdx.x * blockDim.x + threadIdx.x;
+    const int lo = mt_owner(b.col_start, b.n, gc);
+    const MtDesc& d = b.d[lo];
+    const int k = gc - b.col_start[lo];
+    if (k < 0 || k >= d.K) return;
+    const float* A = d.A;
+    float m = 0.f;
+    for (int j = 0; j < d.r; ++j) m = fmaxf(m, fabsf(A[(size_t)j * d.ld + d.k0 + k]));
+    const int e = mt_exp(m);
+    const float sc = ldexpf(1.0f, -e);
+    uint4* th = reinterpret_cast<uint4*>(const_cast<uint16_t*>(d.ath) + (size_t)k * kMtRank);
+    uint4* tl = reinterpret_cast<uint4*>(const_cast<uint16_t*>(d.atl) + (size_t)k * kMtRank);
+    for (int c = 0; c < kMtRank / 8; ++c) {
+        __half h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int j = c * 8 + i;
+            mt_split(j < d.r ? A[(size_t)j * d.ld + d.k0 + k] : 0.f, sc, h[i], l[i]);
+        }
+        th[c] = *reinterpret_cast<const uint4*>(h);
+        tl[c] = *reinterpret_cast<const uint4*>(l);
+    }
+    const_cast<int*>(d.ea)[k] = e;
+}
+
+__device__ __forceinline__ void mt_fail(unsigned* status) {
+    if (status) atomicOr(status, kStatusTimeout);
+}
+
+__global__ void __launch_bounds__(kMtThreads, 1)
+merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
+    extern __shared__ unsigned char mt_smem_raw[];
+    const uint32_t raw = smem_u32(mt_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = mt_smem_raw + (base - raw);
+    const uint32_t a_hi = base, a_lo = base + kMtAop;
+    const uint32_t b_op = base + 2 * kMtAop;                    // [buf][plane] tiles of kMtBop
+    int* ea_s = reinterpret_cast<int*>(smem + 2 * kMtAop + 4 * kMtBop);   // [3][256], tile % 3
+    int* eb_s = ea_s + 3 * kMtCols;                                       // [128]
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(eb_s + kMtRows);        // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int di = mt_find(b, blockIdx.x);
+    const MtDesc& d = b.d[di];
+    const int row0 = (blockIdx.x - b.cta_start[di]) * kMtRows;
+
+    // the stripe's B rows (hi, lo) and their exponents
+    for (int idx = tid; idx < kMtRows * 8; idx += kMtThreads) {
+        const int r = idx >> 3, c = idx & 7;
+        uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h;
+        if (row0 + r < d.N) {
+            h = *reinterpret_cast<const uint4*>(d.bh + (size_t)(row0 + r) * kMtRank + c * 8);
+            l = *reinterpret_cast<const uint4*>(d.bl + (size_t)(row0 + r) * kMtRank + c * 8);
+        }
+        *reinterpret_cast<uint4*>(smem + sw128_offset(r, c)) = h;
+        *reinterpret_cast<uint4*>(smem + kMtAop + sw128_offset(r, c)) = l;
+    }
+    for (int r = tid; r < kMtRows; r += kMtThreads) eb_s[r] = row0 + r < d.N ? d.eb[row0 + r] : 0;
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, 512);
+    fence_proxy_async_smem_cta();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int ntiles = (d.K + kMtCols - 1) / kMtCols;
+    const int q = warp & 3, cq = warp >> 2;          // TMEM lane quarter, column quarter (64)
+    const int rloc = 32 * q + lane, n = row0 + rloc;
+    const int src_blocks = d.ld >> 7, blk0 = d.k0 >> 7;
+    // A^T tile t (256 columns, hi and lo) into buffer `buf`: asynchronous
+    // 16-byte copies into the swizzled layout, zero-filled past K
+    auto load_tile = [&](int t, int buf) {
+        const uint32_t dst = b_op + (uint32_t)(2 * buf) * kMtBop;
+        for (int idx = tid; idx < kMtCols * 8; idx += kMtThreads) {
+            const int r = idx >> 3, c = idx & 7, col = t * kMtCols + r;
+            const bool in = col < d.K;
+            const size_t off = in ? (size_t)col * kMtRank + c * 8 : 0;
+            const uint32_t nb = in ? 16u : 0u;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + sw128_offset(r, c)),
+                         "l"(d.ath + off), "r"(nb)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + kMtBop + sw128_offset(r, c)),
+                         "l"(d.atl + off), "r"(nb)
+                         : "memory");
+        }
+        for (int r = tid; r < kMtCols; r += kMtThreads) {
+            const int col = t * kMtCols + r;
+            ea_s[(t % 3) * kMtCols + r] = col < d.K ? d.ea[col] : 0;
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    bool ok = true;
+    load_tile(0, 0);
+    for (int t = 0; t <= ntiles; ++t) {
+        // MMA(t - 1) done: its A^T buffer is free for tile t + 1, its accumulator ready
+        if (t > 0 && ok && !mbar_wait_bounded(&mbar[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1))) {
+            ok = false;
+            mt_fail(status);
+        }
+        if (t + 1 < ntiles) load_tile(t + 1, (t + 1) & 1);
+        if (t < ntiles) {
+            const int buf = t & 1;
+            if (t + 1 < ntiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
+            else asm volatile("cp.async.wait_group 0;" ::: "memory");
+            fence_proxy_async_smem_cta();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0 && ok) {
+                constexpr uint32_t idesc = umma_idesc_f16(kMtRows, kMtCols);
+                const uint32_t dcol = tmem + (uint32_t)(buf * kMtCols);
+                const uint32_t bh_s = b_op + (uint32_t)(2 * buf) * kMtBop, bl_s = bh_s + kMtBop;
+#pragma unroll
+                for (int kk = 0; kk < kMtRank / 16; ++kk) {
+                    const uint64_t ah = sw128_desc(a_hi + kk * 32), al = sw128_desc(a_lo + kk * 32);
+                    const uint64_t bh = sw128_desc(bh_s + kk * 32), bl = sw128_desc(bl_s + kk * 32);
+                    tc_mma(dcol, ah, bh, idesc, kk ? 1u : 0u);
+                    tc_mma(dcol, ah, bl, idesc, 1u);
+                    tc_mma(dcol, al, bh, idesc, 1u);
+                }
+                tc_commit(&mbar[buf]);
+            }
+        }
+        if (t > 0) {
+            const int u = t - 1, ubuf = u & 1;
+            const int colh = u * kMtCols + cq * 64;      // first of this thread's 64 columns
+            // their I2_S codes: half of one 128-column block (32 bytes, 4 column slots)
+            uint4 w[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+            const bool rowok = ok && n < d.N && colh < d.K;
+            const uint8_t* blk = d.i2s + ((size_t)n * src_blocks + blk0 + (colh >> 7)) * 32;
+            if (rowok) {
+                w[0] = *reinterpret_cast<const uint4*>(blk);
+                w[1] = *reinterpret_cast<const uint4*>(blk + 16);
+            }
+            const uint32_t words[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+            const int eb = eb_s[rloc];
+            for (int c = 0; c < 2; ++c) {
+                __syncwarp();
+                uint32_t acc[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ubuf * kMtCols + cq * 64 + c * 32), acc);
+                tmem_wait_ld();
+                if (!rowok) continue;
+                // column 32 * slot + j of the block: byte j, bits shift + 1 .. shift
+                const int shift = 6 - 2 * (((colh & 127) >> 5) + c);
+                uint32_t packed[16];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const uint32_t code = (words[j >> 2] >> (8 * (j & 3) + shift)) & 3u;
+                    const float m = (code == 0u) ? -1.0f : (code == 2u ? 1.0f : 0.0f);
+                    const float bv = __fmul_rn(d.scale, m);
+                    const int e = eb + ea_s[(u % 3) * kMtCols + cq * 64 + c * 32 + j];
+                    // exact power of two (the exponents keep it in the normal range)
+                    const float p2 = (e >= -126 && e <= 127) ? __int_as_float((e + 127) << 23) : ldexpf(1.0f, e);
+                    const float delta = __uint_as_float(acc[j]) * p2;
+                    const uint32_t h = f32_to_f16_trunc_fast(__fadd_rn(bv, __fmul_rn(delta, d.sf)));
+                    if (j & 1) packed[j >> 1] |= h << 16;
+                    else packed[j >> 1] = h;
+                }
+                uint4* out = reinterpret_cast<uint4*>(d.dst + (size_t)n * d.K + colh + c * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    out[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
+            tc_fence_before();
+        }
+        __syncthreads();
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+static tvb_status mt_prepare() {
+    static cudaError_t err = cudaErrorNotReady;
+    if (err == cudaErrorNotReady) {
+        err = cudaFuncSetAttribute(merge_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem);
+        // keep the stream-ordered pool's memory between calls (the workspace is
+        // a few hundred MB for a whole model and would otherwise be unmapped
+        // and mapped again at every synchronisation)
+        int dev = 0;
+        cudaMemPool_t pool;
+        if (err == cudaSuccess && cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+            uint64_t keep = ~0ull;
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        }
+    }
+    if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(merge_tc_kernel)");
+    return TVB_OK;
+}
+
+tvb_status merge_exact(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st);
+
+tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st) {
+    if (n <= 0) return TVB_OK;
+    TVB_REQUIRE(descs, "merge_tc: descs is NULL");
+    bool exact = out != TVB_F16;
+    for (int i = 0; i < n && !exact; ++i) exact = descs[i].r > kMtRank;
+    if (exact) return merge_exact(descs, n, out, st);   // F32 / INT8 / rank > 64: bit-exact path
+    for (int i = 0; i < n; ++i) {
+        const tvb_merge_desc& s = descs[i];
+        const int ld = s.ld ? s.ld : s.K;
+        TVB_REQUIRE(s.i2s && s.dst && s.K > 0 && s.N > 0 && s.K % 128 == 0, "merge_tc: descriptor %d", i);
+        TVB_REQUIRE(s.r >= 0 && (s.r == 0 || (s.A && s.B)), "merge_tc: rank %d needs A and B", s.r);
+        TVB_REQUIRE(s.k0 >= 0 && s.k0 % 128 == 0 && ld % 128 == 0 && s.k0 + s.K <= ld,
+                    "merge_tc: column slice [%d, %d) of %d columns", s.k0, s.k0 + s.K, ld);
+        TVB_REQUIRE((reinterpret_cast<uintptr_t>(s.dst) & 15) == 0 && (reinterpret_cast<uintptr_t>(s.i2s) & 15) == 0,
+                    "merge_tc: dst and i2s must be 16-byte aligned");
+    }
+    TVB_TRY(mt_prepare());
+    static thread_local MtBatch b;
+    for (int base = 0; base < n; base += kMtMaxDescs) {
+        const int cnt = std::min(kMtMaxDescs, n - base);
+        // workspace: prepared planes and exponents of every tensor of this launch
+        size_t rows = 0, cols = 0;
+        for (int i = 0; i < cnt; ++i) {
+            rows += (size_t)descs[base + i].N;
+            cols += (size_t)descs[base + i].K;
+        }
+        const size_t bytes = 2 * (rows + cols) * kMtRank * 2 + (rows + cols) * 4 + 256;
+        unsigned char* ws = nullptr;
+        TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st));
+        uint16_t* bh = reinterpret_cast<uint16_t*>(ws);
+        uint16_t* bl = bh + rows * kMtRank;
+        uint16_t* ah = bl + rows * kMtRank;
+        uint16_t* al = ah + cols * kMtRank;
+        int* eb = reinterpret_cast<int*>(al + cols * kMtRank);
+        int* ea = eb + rows;
+        size_t ro = 0, co = 0;
+        int ctas = 0, rwarps = 0, cthreads = 0;
+        for (int i = 0; i < cnt; ++i) {
+            const tvb_merge_desc& s = descs[base + i];
+            MtDesc& d = b.d[i];
+            d.i2s = s.i2s;
+            d.bh = bh + ro * kMtRank;
+            d.bl = bl + ro * kMtRank;
+            d.eb = eb + ro;
+            d.ath = ah + co * kMtRank;
+            d.atl = al + co * kMtRank;
+            d.ea = ea + co;
+            d.dst = static_cast<uint16_t*>(s.dst);
+            d.A = s.r ? s.A : nullptr;
+            d.B = s.r ? s.B : nullptr;
+            d.scale = s.scale;
+            d.sf = s.r ? s.alpha / (float)s.r : 0.0f;
+            d.K = s.K;
+            d.N = s.N;
+            d.r = s.r;
+            d.k0 = s.k0;
+            d.ld = s.ld ? s.ld : s.K;
+            b.cta_start[i] = ctas;
+            b.row_start[i] = rwarps;
+            b.col_start[i] = cthreads;
+            ctas += (s.N + kMtRows - 1) / kMtRows;
+            rwarps += s.N;
+            cthreads += s.K;
+            ro += (size_t)s.N;
+            co += (size_t)s.K;
+        }
+        b.cta_start[cnt] = ctas;
+        b.row_start[cnt] = rwarps;
+        b.col_start[cnt] = cthreads;
+        b.n = cnt;
+        mt_prep_b<<<(rwarps + 7) / 8, 256, 0, st>>>(b);
+        tvb_status s = check_launch("mt_prep_b");
+        if (s == TVB_OK) {
+            mt_prep_a<<<(cthreads + 255) / 256, 256, 0, st>>>(b);
+            s = check_launch("mt_prep_a");
+        }
+        if (s == TVB_OK) {
+            merge_tc_kernel<<<ctas, kMtThreads, kMtSmem, st>>>(b, nullptr);
+            s = check_launch("merge_tc_kernel");
+        }
+        cudaFreeAsync(ws, st);
+        if (s != TVB_OK) return s;
+    }
+    return TVB_OK;
+}
+
+}  // namespace tvb
+
+extern "C" tvb_status tvb_merge_batch_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, void* stream) {
+    return tvb::merge_tc(descs, n, out, tvb::as_stream(stream));
+}

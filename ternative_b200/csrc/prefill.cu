@@ -28,81 +28,9 @@
 #include <mutex>
 
 #include "stream.cuh"
+#include "tcgen05.cuh"
 
 namespace tvb {
-
-// ---------------------------------------------------------------------------
-// tcgen05 / TMA primitives
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// 2-D tiled TMA load global -> this CTA's shared memory, completion on `bar`.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte
-// swizzling: rows of 128 B, 8-row groups 1024 B apart (stride byte offset),
-// leading byte offset unused for swizzled K-major layouts (encoded 1),
-// descriptor version 1 (bits 46-47), swizzle mode 2 = 128B (bits 61-63).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1u << 16;
-    d |= (uint64_t)(1024u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
-}
-
-// Instruction descriptor, kind::f16: D F32 (bits 4-5 = 1), A and B F16 (0),
-// both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-constexpr uint32_t pf_idesc(int M, int N) {
-    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// Arrive on `bar` once every tcgen05.mma this thread issued has completed.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-
-// 32 consecutive F32 columns of this thread's TMEM lane (warp-collective).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // GEMM kernel
@@ -207,6 +135,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, s0 = blockIdx.y * kPfBM;
+    const int nkb = a.nk;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kPfStages; ++i) {
@@ -241,9 +170,9 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         if (a.use_lo) prefetch_tmap(&maps.xl);
         const uint32_t bytes =
             (uint32_t)(kPfPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
-        int kb = 0;
-        for (; kb < a.nk; ++kb) {
-            const int s = kb % kPfStages, r = kb / kPfStages;
+        int i = 0;
+        for (; i < nkb; ++i) {
+            const int s = i % kPfStages, r = i / kPfStages, kx = i * kPfBK;
             if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
                 pf_fail(a, abort_flag);
                 break;
@@ -251,18 +180,18 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
             if (*abort_flag) break;
             const uint32_t st = base + (uint32_t)(s * kPfStage);
             mbar_expect_tx(&full[s], bytes);
-            tma_load_2d(st, &maps.xh, kb * kPfBK, s0, &full[s]);
-            if (a.use_lo) tma_load_2d(st + kPfPlane, &maps.xl, kb * kPfBK, s0, &full[s]);
+            tma_load_2d(st, &maps.xh, kx, s0, &full[s]);
+            if (a.use_lo) tma_load_2d(st + kPfPlane, &maps.xl, kx, s0, &full[s]);
 #pragma unroll
             for (int h = 0; h < 2; ++h)
-                if (hv[h]) tma_load_2d(st + 2 * kPfPlane + h * kPfHalf, &maps.w[mi[h]], kb * kPfBK, row[h], &full[s]);
+                if (hv[h]) tma_load_2d(st + 2 * kPfPlane + h * kPfHalf, &maps.w[mi[h]], kx, row[h], &full[s]);
         }
-        *issued = kb;
+        *issued = i;
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------
-        constexpr uint32_t idesc = pf_idesc(kPfBM, kPfBN);
+        constexpr uint32_t idesc = umma_idesc_f16(kPfBM, kPfBN);
         int kb = 0;
-        for (; kb < a.nk; ++kb) {
+        for (; kb < nkb; ++kb) {
             const int s = kb % kPfStages, r = kb / kPfStages;
             if (!mbar_wait_bounded(&full[s], (uint32_t)(r & 1))) {
                 pf_fail(a, abort_flag);
@@ -288,8 +217,13 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         const bool ok = mbar_wait_bounded(done, 0u);
         tc_fence_after();
         if (!ok) pf_fail(a, abort_flag);
+        const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+        // accumulator columns [col, col + 32) of this thread's token row
+        auto fetch = [&](int col, uint32_t (&r)[32]) {
+            tmem_ld32(trow + col, r);
+            tmem_wait_ld();
+        };
         if (ok && !*abort_flag) {
-            const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
             const float e2 = (srow && a.row_exp) ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
             uint32_t r0[32], r1[32];
             float v0[32], v1[32];
@@ -297,9 +231,8 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                 // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
                 for (int c = 0; c < 4; ++c) {
                     __syncwarp();
-                    tmem_ld32(trow + c * 32, r0);
-                    tmem_ld32(trow + 128 + c * 32, r1);
-                    tmem_wait_ld();
+                    fetch(c * 32, r0);
+                    fetch(128 + c * 32, r1);
                     const int n0 = row[0] + c * 32;
                     if (srow && hv[0] && hv[1] && n0 < a.rows[0]) {
 #pragma unroll
@@ -319,9 +252,8 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                     const int head = row[h] / a.hd;
                     for (int c = 0; c < 2; ++c) {
                         __syncwarp();
-                        tmem_ld32(trow + h * 128 + c * 32, r0);
-                        tmem_ld32(trow + h * 128 + half + c * 32, r1);
-                        tmem_wait_ld();
+                        fetch(h * 128 + c * 32, r0);
+                        fetch(h * 128 + half + c * 32, r1);
                         if (!(srow && hv[h])) continue;
                         const int pos = a.pos0 + s;
 #pragma unroll
@@ -355,8 +287,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                 for (int h = 0; h < 2; ++h) {
                     for (int c = 0; c < 4; ++c) {
                         __syncwarp();
-                        tmem_ld32(trow + h * 128 + c * 32, r0);
-                        tmem_wait_ld();
+                        fetch(h * 128 + c * 32, r0);
                         const int n0 = row[h] + c * 32;
                         if (!(srow && hv[h]) || n0 >= a.rows[0]) continue;
 #pragma unroll

@@ -49,6 +49,7 @@ struct PfGemm {
     unsigned* status = nullptr;     // device word; kStatusTimeout on a pipeline stall
 };
 
+
 tvb_status pf_gemm(const PfGemm& g, cudaStream_t st);
 
 // x[s] = f32(embd[tokens[s]])  (extract_embeddings_batched)
