@@ -85,6 +85,11 @@ __device__ __forceinline__ int mt_exp(float m) {
     return (m > 0.f && isfinite(m)) ? max(ilogbf(m) - 14, -100) : 0;
 }
 
+// 2^e as a float (e within the normal range is built from its bits).
+__device__ __forceinline__ float mt_pow2(int e) {
+    return (e >= -126 && e <= 127) ? __int_as_float((e + 127) << 23) : ldexpf(1.0f, e);
+}
+
 __device__ __forceinline__ void mt_split(float v, float sc, __half& hi, __half& lo) {
     const float f = v * sc;
     hi = __float2half_rn(f);
@@ -154,8 +159,8 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
     unsigned char* smem = mt_smem_raw + (base - raw);
     const uint32_t a_hi = base, a_lo = base + kMtAop;
     const uint32_t b_op = base + 2 * kMtAop;                    // [buf][plane] tiles of kMtBop
-    int* ea_s = reinterpret_cast<int*>(smem + 2 * kMtAop + 4 * kMtBop);   // [3][256], tile % 3
-    int* eb_s = ea_s + 3 * kMtCols;                                       // [128]
+    float* fa_s = reinterpret_cast<float*>(smem + 2 * kMtAop + 4 * kMtBop);   // [3][256] 2^ea, tile % 3
+    int* eb_s = reinterpret_cast<int*>(fa_s + 3 * kMtCols);                   // [128]
     uint64_t* mbar = reinterpret_cast<uint64_t*>(eb_s + kMtRows);        // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 2);
 
@@ -210,11 +215,23 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
         }
         for (int r = tid; r < kMtCols; r += kMtThreads) {
             const int col = t * kMtCols + r;
-            ea_s[(t % 3) * kMtCols + r] = col < d.K ? d.ea[col] : 0;
+            fa_s[(t % 3) * kMtCols + r] = col < d.K ? mt_pow2(d.ea[col]) : 0.f;
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    // I2_S codes of this thread's 64 columns of tile u (32 bytes), one tile ahead
+    uint4 wn[2];
+    auto load_codes = [&](int u) {
+        const int colh = u * kMtCols + cq * 64;
+        wn[0] = wn[1] = make_uint4(0u, 0u, 0u, 0u);
+        if (u < ntiles && n < d.N && colh < d.K) {
+            const uint8_t* blk = d.i2s + ((size_t)n * src_blocks + blk0 + (colh >> 7)) * 32;
+            wn[0] = __ldcs(reinterpret_cast<const uint4*>(blk));
+            wn[1] = __ldcs(reinterpret_cast<const uint4*>(blk + 16));
+        }
+    };
     bool ok = true;
+    load_codes(0);
     load_tile(0, 0);
     for (int t = 0; t <= ntiles; ++t) {
         // MMA(t - 1) done: its A^T buffer is free for tile t + 1, its accumulator ready
@@ -249,16 +266,17 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
         if (t > 0) {
             const int u = t - 1, ubuf = u & 1;
             const int colh = u * kMtCols + cq * 64;      // first of this thread's 64 columns
-            // their I2_S codes: half of one 128-column block (32 bytes, 4 column slots)
-            uint4 w[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
             const bool rowok = ok && n < d.N && colh < d.K;
-            const uint8_t* blk = d.i2s + ((size_t)n * src_blocks + blk0 + (colh >> 7)) * 32;
-            if (rowok) {
-                w[0] = *reinterpret_cast<const uint4*>(blk);
-                w[1] = *reinterpret_cast<const uint4*>(blk + 16);
-            }
-            const uint32_t words[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
-            const int eb = eb_s[rloc];
+            // their I2_S codes (half of one 128-column block, 32 bytes) were
+            // requested during the previous tile; request the next tile's now
+            const uint32_t words[8] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w};
+            load_codes(u + 1);
+            // per row: alpha / r times 2^eb (both exact powers-of-two scalings of
+            // the delta, applied as (acc * 2^ea) * (sf * 2^eb): one rounding, as
+            // the reference's delta * sf)
+            const float g = d.sf * mt_pow2(eb_s[rloc]);
+            const float4* fa4 = reinterpret_cast<const float4*>(fa_s + (u % 3) * kMtCols + cq * 64);
+            const float sp = d.scale, sn = -d.scale;
             for (int c = 0; c < 2; ++c) {
                 __syncwarp();
                 uint32_t acc[32];
@@ -269,17 +287,29 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
                 const int shift = 6 - 2 * (((colh & 127) >> 5) + c);
                 uint32_t packed[16];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const uint32_t code = (words[j >> 2] >> (8 * (j & 3) + shift)) & 3u;
-                    const float m = (code == 0u) ? -1.0f : (code == 2u ? 1.0f : 0.0f);
-                    const float bv = __fmul_rn(d.scale, m);
-                    const int e = eb + ea_s[(u % 3) * kMtCols + cq * 64 + c * 32 + j];
-                    // exact power of two (the exponents keep it in the normal range)
-                    const float p2 = (e >= -126 && e <= 127) ? __int_as_float((e + 127) << 23) : ldexpf(1.0f, e);
-                    const float delta = __uint_as_float(acc[j]) * p2;
-                    const uint32_t h = f32_to_f16_trunc_fast(__fadd_rn(bv, __fmul_rn(delta, d.sf)));
-                    if (j & 1) packed[j >> 1] |= h << 16;
-                    else packed[j >> 1] = h;
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 fa = fa4[c * 8 + j4];
+                    const float fav[4] = {fa.x, fa.y, fa.z, fa.w};
+                    float mv[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 4 * j4 + i;
+                        const uint32_t code = (words[j >> 2] >> (8 * (j & 3) + shift)) & 3u;
+                        // map2bit {-1, 0, +1, 0} times the scale (tensor.cpp:1020)
+                        const float bv = (code & 1u) ? 0.0f : (code ? sp : sn);
+                        mv[i] = __fadd_rn(bv, __fmul_rn(__fmul_rn(__uint_as_float(acc[j]), fav[i]), g));
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; i += 2) {
+                        uint32_t h2;
+                        if (fabsf(mv[i]) < 65536.0f && fabsf(mv[i + 1]) < 65536.0f) {
+                            // round toward zero = the reference's truncation in this range
+                            asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(mv[i + 1]), "f"(mv[i]));
+                        } else {
+                            h2 = (uint32_t)f32_to_f16_trunc(mv[i]) | ((uint32_t)f32_to_f16_trunc(mv[i + 1]) << 16);
+                        }
+                        packed[2 * j4 + (i >> 1)] = h2;
+                    }
                 }
                 uint4* out = reinterpret_cast<uint4*>(d.dst + (size_t)n * d.K + colh + c * 32);
 #pragma unroll
