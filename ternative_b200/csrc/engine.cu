@@ -161,6 +161,7 @@ struct tvb_context {
     float *pf_x = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_h = nullptr;
     uint16_t *pf_xh = nullptr, *pf_xl = nullptr;
     int *pf_exp = nullptr, *pf_tok = nullptr;
+    void* pf_planes = nullptr;   // F16 hi/lo q, K, V^T planes of the tensor-core attention
     // tensor parallelism (tvb_tp_init / tvb_tp_set_peers): this rank's exchange
     // buffer, every rank's (IPC-mapped) buffer, and a second residual vector
     // (folds alternate between e_x and e_x2)
@@ -435,6 +436,9 @@ tvb_status pf_workspace(tvb_context* c) {
         {(void**)&c->pf_exp, (size_t)cap * 4},        {(void**)&c->pf_tok, (size_t)c->cfg.max_seq_len * 4},
     };
     for (auto& a : allocs) TVB_TRY(alloc_dev(a.p, a.b));
+    if (pf_attention_tc_supported(c->cfg.num_heads, c->cfg.num_kv_heads, c->cfg.head_dim))
+        TVB_TRY(alloc_dev(&c->pf_planes, pf_attn_planes_bytes(cap, c->cfg.max_seq_len, c->cfg.num_heads,
+                                                              c->cfg.num_kv_heads)));
     c->pf_cap = cap;
     return TVB_OK;
 }
@@ -512,7 +516,11 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
             g.rope_cos = c->rope_cos;
             g.rope_sin = c->rope_sin;
             TVB_TRY(pf_gemm(g, st));
-            TVB_TRY(pf_attention(c->pf_q, kl, vl, n, p0, g.nh, g.nkv, hd, scale, c->pf_attn, st));
+            if (c->pf_planes)
+                TVB_TRY(pf_attention_tc(c->pf_q, kl, vl, n, p0, g.nh, g.nkv, hd, scale, c->pf_attn, c->pf_planes,
+                                        c->pf_cap, c->cfg.max_seq_len, &c->st->status, st));
+            else
+                TVB_TRY(pf_attention(c->pf_q, kl, vl, n, p0, g.nh, g.nkv, hd, scale, c->pf_attn, st));
             // attn_sub_norm -> o_proj -> residual
             TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, n, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
             off = 0;
@@ -663,7 +671,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
                    c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
-                   c->pf_w16, c->e_x2, c->tp_xchg};
+                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};

@@ -333,6 +333,27 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(tvb_status* st) {
     return fn;
 }
 
+tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint64_t* dims, const uint64_t* strides,
+                            const uint32_t* box) {
+    tvb_status st;
+    auto fn = encode_fn(&st);
+    if (!fn) return st;
+    TVB_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, "tensor map: base not 16-byte aligned");
+    cuuint64_t d[5], sb[4];
+    cuuint32_t b[5], e[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        e[i] = 1u;
+        if (i + 1 < rank) sb[i] = strides[i];
+    }
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(p), d, sb, b, e,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(TVB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return TVB_OK;
+}
+
 // F16 matrix [rows][K] (row pitch K), boxes of 128 rows x 64 k, 128B swizzle.
 static tvb_status encode_f16(CUtensorMap* m, const void* p, int rows, int K) {
     tvb_status st;

@@ -68,6 +68,20 @@ tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps
 tvb_status pf_attention(const float* q, const float* kcache, const float* vcache, int S, int pos0,
                         int nh, int nkv, int hd, float scale, float* out, cudaStream_t st);
 
+// The same attention on the tensor cores (prefill_attn.cu): q, K and V^T are
+// split into F16 hi/lo planes in `planes` (pf_attn_planes_bytes for up to
+// max_rows query rows and max_keys KV rows), then a two-pass tcgen05 kernel.
+// |q|, |k|, |v| must stay below the F16 range (65504).
+bool pf_attention_tc_supported(int nh, int nkv, int hd);
+size_t pf_attn_planes_bytes(int max_rows, int max_keys, int nh, int nkv);
+tvb_status pf_attention_tc(const float* q, const float* kcache, const float* vcache, int S, int pos0, int nh,
+                           int nkv, int hd, float scale, float* out, void* planes, int max_rows, int max_keys,
+                           unsigned* status, cudaStream_t st);
+
+// Tiled TMA descriptor of an F16 tensor (128-byte swizzle, zero fill outside).
+tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint64_t* dims, const uint64_t* strides,
+                            const uint32_t* box);
+
 // INT8 -> F16 (exact: |q| <= 127).
 tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st);
 
