@@ -37,7 +37,7 @@ constexpr int kAtOffK = kAtOffQ + 4 * kAtQAtom;          // Kh[2], Kl[2]
 constexpr int kAtOffV = kAtOffK + 4 * kAtKAtom;          // Vth, Vtl
 constexpr int kAtOffP = kAtOffV + 2 * kAtVt;             // Ph, Pl
 constexpr int kAtOffBar = kAtOffP + 2 * kAtP;
-constexpr int kAtSmem = kAtOffBar + 128 + 1024;
+constexpr int kAtSmem = kAtOffBar + 64 + 4 * 128 * 4 + 1024;   // + barriers + row exchange
 
 struct AtMaps {
     CUtensorMap qh, ql, kh, kl, vth, vtl;
@@ -133,11 +133,18 @@ pf_attn_tc_kernel(const __grid_constant__ AtMaps mp, const __grid_constant__ AtA
         tc_commit(sbar);
     };
 
-    // this thread's row (threads 0-127 = TMEM lanes): position, or -1 past the prompt
-    const int r = tid;
+    // Softmax: every thread takes 32 of a row's 64 keys (TMEM lane quarter
+    // warp % 4, column half warp / 4); the two halves of a row combine their
+    // max and sum through shared memory in a fixed order.  Scores are kept in
+    // the log2 domain (scale * log2(e) folded in), exponentials are exp2f.
+    const int r = 32 * (warp & 3) + (tid & 31);
+    const int half = warp >> 2;
     const int rq = qlo + r / a.group;
-    const int rpos = (tid < kAtRows && rq < a.S) ? a.pos0 + rq : -1;
-    const uint32_t s_row = s_t + ((uint32_t)(32 * (warp & 3)) << 16);
+    const int rpos = rq < a.S ? a.pos0 + rq : -1;
+    const uint32_t s_part = s_t + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * half);
+    float* red = reinterpret_cast<float*>(smem + kAtOffBar + 64);   // [2 halves][128 rows]
+    float* red2 = red + 2 * kAtRows;
+    const float sc2 = a.scale * 1.4426950408889634f;   // log2(e)
     float m = -INFINITY, l = 0.f;
     uint32_t kpar = 0, spar = 0, vpar = 0, opar = 0;
 
@@ -157,29 +164,30 @@ pf_attn_tc_kernel(const __grid_constant__ AtMaps mp, const __grid_constant__ AtA
         spar ^= 1u;
         tc_fence_after();
         if (tid == 0) load_k(kt + 1 < ntiles ? kt + 1 : 0);   // the K buffer is free; pass 2 starts at tile 0
-        if (warp < 4) {
-            uint32_t sv[2][32];
-            tmem_ld32(s_row, sv[0]);
-            tmem_ld32(s_row + 32, sv[1]);
-            tmem_wait_ld();
-            float tmax = -INFINITY;
+        uint32_t sv[32];
+        tmem_ld32(s_part, sv);
+        tmem_wait_ld();
+        const int key0 = kt * kAtKeys + 32 * half;
+        float tmax = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const float s = kt * kAtKeys + j <= rpos ? __uint_as_float(sv[j >> 5][j & 31]) * a.scale : -INFINITY;
-                tmax = fmaxf(tmax, s);
-            }
-            if (tmax > -INFINITY) {
-                const float mn = fmaxf(m, tmax);
-                float sum = 0.f;
-#pragma unroll
-                for (int j = 0; j < 64; ++j)
-                    if (kt * kAtKeys + j <= rpos) sum += expf(__uint_as_float(sv[j >> 5][j & 31]) * a.scale - mn);
-                l = (m > -INFINITY ? l * expf(m - mn) : 0.f) + sum;
-                m = mn;
-            }
-        }
+        for (int j = 0; j < 32; ++j)
+            if (key0 + j <= rpos) tmax = fmaxf(tmax, __uint_as_float(sv[j]) * sc2);
+        red[half * kAtRows + r] = tmax;
         tc_fence_before();
         __syncthreads();
+        const float mn = fmaxf(m, fmaxf(red[r], red[kAtRows + r]));
+        float sum = 0.f;
+        if (mn > -INFINITY) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (key0 + j <= rpos) sum += exp2f(__uint_as_float(sv[j]) * sc2 - mn);
+        }
+        red2[half * kAtRows + r] = sum;
+        __syncthreads();
+        if (mn > -INFINITY) {
+            l = (m > -INFINITY ? l * exp2f(m - mn) : 0.f) + (red2[r] + red2[kAtRows + r]);
+            m = mn;
+        }
     }
 
     // ---- pass 2: normalised probabilities, O = P.V -----------------------------------
@@ -199,26 +207,24 @@ pf_attn_tc_kernel(const __grid_constant__ AtMaps mp, const __grid_constant__ AtA
         spar ^= 1u;
         tc_fence_after();
         if (tid == 0 && kt + 1 < ntiles) load_k(kt + 1);
-        if (warp < 4) {
-            uint32_t sv[2][32];
-            tmem_ld32(s_row, sv[0]);
-            tmem_ld32(s_row + 32, sv[1]);
+        {
+            uint32_t sv[32];
+            tmem_ld32(s_part, sv);
             tmem_wait_ld();
+            const int key0 = kt * kAtKeys + 32 * half;
             unsigned char* ph = smem + kAtOffP;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 __half hi[8], lo[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int j = c * 8 + i;
-                    const float p = kt * kAtKeys + j <= rpos
-                                        ? expf(__uint_as_float(sv[j >> 5][j & 31]) * a.scale - m) * inv_l
-                                        : 0.f;
+                    const float p = key0 + j <= rpos ? exp2f(__uint_as_float(sv[j]) * sc2 - m) * inv_l : 0.f;
                     hi[i] = __float2half_rn(p);
                     lo[i] = __float2half_rn(p - __half2float(hi[i]));
                 }
-                *reinterpret_cast<uint4*>(ph + sw128_offset(r, c)) = *reinterpret_cast<const uint4*>(hi);
-                *reinterpret_cast<uint4*>(ph + kAtP + sw128_offset(r, c)) = *reinterpret_cast<const uint4*>(lo);
+                *reinterpret_cast<uint4*>(ph + sw128_offset(r, 4 * half + c)) = *reinterpret_cast<const uint4*>(hi);
+                *reinterpret_cast<uint4*>(ph + kAtP + sw128_offset(r, 4 * half + c)) = *reinterpret_cast<const uint4*>(lo);
             }
             fence_proxy_async_smem_cta();
         }
@@ -248,12 +254,13 @@ pf_attn_tc_kernel(const __grid_constant__ AtMaps mp, const __grid_constant__ AtA
         if (tid == 0 && kt + 1 < ntiles) load_v(kt + 1);
     }
 
-    // ---- output rows -----------------------------------------------------------------
-    if (warp < 4 && !*abort_flag) {
-        const uint32_t o_row = o_t + ((uint32_t)(32 * (warp & 3)) << 16);
-        float* dst = rpos >= 0 ? a.out + (size_t)rq * a.nh * kAtHd + (size_t)(kvh * a.group + r % a.group) * kAtHd
+    // ---- output rows: each thread stores 64 of its row's 128 dims ----------------
+    if (!*abort_flag) {
+        const uint32_t o_row = o_t + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(64 * half);
+        float* dst = rpos >= 0 ? a.out + (size_t)rq * a.nh * kAtHd + (size_t)(kvh * a.group + r % a.group) * kAtHd +
+                                     64 * half
                                : nullptr;
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
             __syncwarp();
             uint32_t ov[32];
             tmem_ld32(o_row + c * 32, ov);
