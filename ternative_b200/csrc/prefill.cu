@@ -36,15 +36,15 @@ namespace tvb {
 // GEMM kernel
 // ---------------------------------------------------------------------------
 constexpr int kPfBM = 128;                         // tokens per tile (MMA M, TMEM lanes)
-constexpr int kPfBN = 256;                         // weight rows per tile (MMA N, TMEM columns)
 constexpr int kPfBK = 64;                          // k per stage: 128 B of F16 = one swizzle row
 constexpr int kPfStages = 3;
 constexpr int kPfThreads = 256;
 constexpr int kPfPlane = kPfBM * kPfBK * 2;        // 16 KB activation plane per stage
 constexpr int kPfHalf = 128 * kPfBK * 2;           // 16 KB weight half-tile per stage
-constexpr int kPfStage = 2 * kPfPlane + 2 * kPfHalf;
-constexpr int kPfSmem = kPfStages * kPfStage + 1024 + 256;   // + alignment slack + barriers
-constexpr uint32_t kPfTmemCols = 256;
+// NH = 128-row weight halves per tile (2: 256 rows, the default; 1: 128 rows
+// for projections with too few 256-row tiles to cover the SMs)
+__host__ __device__ constexpr int pf_stage_bytes(int nh) { return 2 * kPfPlane + nh * kPfHalf; }
+__host__ __device__ constexpr int pf_smem_bytes(int nh) { return kPfStages * pf_stage_bytes(nh) + 1024 + 256; }
 
 struct PfMaps {
     CUtensorMap xh, xl, w[3];
@@ -67,15 +67,16 @@ struct PfArgs {
     unsigned* status;
 };
 
-// Which matrix and first row feed half `h` (128 rows) of column tile `tile`.
-__host__ __device__ inline bool pf_half(const PfArgs& a, int tile, int h, int& mi, int& row) {
+// Which matrix and first row feed half `h` (128 rows) of column tile `tile`
+// (NH halves per tile).
+__host__ __device__ inline bool pf_half(const PfArgs& a, int nh, int tile, int h, int& mi, int& row) {
     if (a.mode == PF_GATEUP) {
         mi = h;
         row = tile * 128;
         return row < a.rows[h];
     }
     if (a.mode == PF_QKV) {
-        int slot = tile * 2 + h;
+        int slot = tile * nh + h;
         if (slot < a.nh) { mi = 0; row = slot * 128; return true; }
         slot -= a.nh;
         if (slot < a.nkv) { mi = 1; row = slot * 128; return true; }
@@ -85,7 +86,7 @@ __host__ __device__ inline bool pf_half(const PfArgs& a, int tile, int h, int& m
         return slot < a.nkv;
     }
     mi = 0;
-    row = tile * kPfBN + h * 128;
+    row = tile * 128 * nh + h * 128;
     return row < a.rows[0];
 }
 
@@ -119,8 +120,11 @@ __device__ __forceinline__ void pf_fail(const PfArgs& a, volatile int* abort_fla
     if (a.status) atomicOr(a.status, kStatusTimeout);
 }
 
+template <int NH>
 __global__ void __launch_bounds__(kPfThreads, 1)
 pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfArgs a) {
+    constexpr int kPfStage = pf_stage_bytes(NH);
+    constexpr uint32_t kPfTmemCols = 128 * NH;
     extern __shared__ unsigned char pf_smem_raw[];
     const uint32_t raw = smem_u32(pf_smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;   // 128B-swizzled tiles want 1024-B alignment
@@ -162,7 +166,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
     int mi[2], row[2];
     bool hv[2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) hv[h] = pf_half(a, tile, h, mi[h], row[h]);
+    for (int h = 0; h < 2; ++h) hv[h] = h < NH && pf_half(a, NH, tile, h, mi[h], row[h]);
 
     if (warp == 0 && lane == 0) {
         // ---- producer: TMA ring ------------------------------------------------------
@@ -189,7 +193,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         *issued = i;
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----------------------------------------------------------------
-        constexpr uint32_t idesc = umma_idesc_f16(kPfBM, kPfBN);
+        constexpr uint32_t idesc = umma_idesc_f16(kPfBM, 128 * NH);
         int kb = 0;
         for (; kb < nkb; ++kb) {
             const int s = kb % kPfStages, r = kb / kPfStages;
@@ -248,7 +252,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                 }
             } else if (a.mode == PF_QKV) {
                 const int half = a.hd >> 1;   // 64
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < NH; ++h) {
                     const int head = row[h] / a.hd;
                     for (int c = 0; c < 2; ++c) {
                         __syncwarp();
@@ -284,7 +288,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                 }
             } else {
                 const bool add = a.mode == PF_RESID;
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < NH; ++h) {
                     for (int c = 0; c < 4; ++c) {
                         __syncwarp();
                         fetch(h * 128 + c * 32, r0);
@@ -375,7 +379,10 @@ static tvb_status pf_prepare() {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
     std::call_once(once, [] {
-        err = cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+        err = cudaFuncSetAttribute(pf_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem_bytes(2));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       pf_smem_bytes(1));
     });
     if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(pf_gemm_kernel)");
     return TVB_OK;
@@ -417,22 +424,38 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
         a.row_scales[i] = g.m[i].row_scales;
         a.scale[i] = g.m[i].scale;
     }
-    int tiles = 0;
+    // 128-row halves of weight rows: q/k/v heads (one half each) or plain rows
+    int halves = 0;
     if (g.mode == PF_QKV) {
         TVB_REQUIRE(g.hd == 128 && g.m[0].rows == g.nh * 128 && g.m[1].rows == g.nkv * 128 &&
                         g.m[2].rows == g.nkv * 128 && g.q_out && g.kcache && g.vcache && g.rope_cos && g.rope_sin,
                     "prefill gemm: inconsistent q/k/v geometry");
-        tiles = (g.nh + 2 * g.nkv + 1) / 2;
+        halves = g.nh + 2 * g.nkv;
     } else if (g.mode == PF_GATEUP) {
         TVB_REQUIRE(g.m[0].rows == g.m[1].rows && g.m[0].rows % 32 == 0 && g.y && g.ldy >= g.m[0].rows,
                     "prefill gemm: gate/up shapes");
-        tiles = (g.m[0].rows + 127) / 128;
     } else {
         TVB_REQUIRE(g.y && g.ldy >= g.m[0].rows, "prefill gemm: output");
-        tiles = (g.m[0].rows + kPfBN - 1) / kPfBN;
+        halves = (g.m[0].rows + 127) / 128;
     }
-    const dim3 grid((unsigned)tiles, (unsigned)((g.S + kPfBM - 1) / kPfBM));
-    pf_gemm_kernel<<<grid, kPfThreads, kPfSmem, stream>>>(maps, a);
+    const int mtiles = (g.S + kPfBM - 1) / kPfBM;
+    // 256-row tiles, or 128-row tiles when those keep more of the SMs busy over
+    // the grid's waves (gate/up tiles always pair a gate half with an up half)
+    int nh = 2, tiles;
+    if (g.mode == PF_GATEUP) {
+        tiles = (g.m[0].rows + 127) / 128;
+    } else {
+        tiles = (halves + 1) / 2;
+        const int sms = num_sms();
+        auto busy = [&](int ctas) { return (double)ctas / (double)(((ctas + sms - 1) / sms) * sms); };
+        if (busy(halves * mtiles) > busy(tiles * mtiles) + 1e-9) {
+            nh = 1;
+            tiles = halves;
+        }
+    }
+    const dim3 grid((unsigned)tiles, (unsigned)mtiles);
+    if (nh == 2) pf_gemm_kernel<2><<<grid, kPfThreads, pf_smem_bytes(2), stream>>>(maps, a);
+    else pf_gemm_kernel<1><<<grid, kPfThreads, pf_smem_bytes(1), stream>>>(maps, a);
     return check_launch("pf_gemm_kernel");
 }
 
