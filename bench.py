@@ -476,6 +476,44 @@ def run_ours(args, world, rank, local):
         us = g0.elapsed_time(g1) * 1e3 / reps
         gb = (N * K * 2 + 4 * K + 4 * N) / (us * 1e-6) / 1e9
         gemv[f"{N}x{K}_f16"] = {"us": us, "GB/s": gb, "frac": gb / hbm}
+        # the same shape with per-row INT8 weights (per-row absmax of the F16 copies)
+        q8 = []
+        for w in ws:
+            q = torch.empty(N, K, dtype=torch.int8, device="cuda")
+            sc = torch.empty(N, dtype=torch.float32, device="cuda")
+            be.quantize_int8(w, N, K, True, q, sc)
+            q8.append((q, sc))
+        be.sync_d()
+        for i in range(3):
+            be.gemv_d2d_int8_rows(y, x, q8[i][0], q8[i][1], K, N)
+        be.sync_d()
+        g0.record(stream)
+        for i in range(reps):
+            q, sc = q8[i % len(q8)]
+            be.gemv_d2d_int8_rows(y, x, q, sc, K, N)
+        g1.record(stream)
+        g1.synchronize()
+        us = g0.elapsed_time(g1) * 1e3 / reps
+        gb = (N * K + 4 * N + 4 * K + 4 * N) / (us * 1e-6) / 1e9
+        gemv[f"{N}x{K}_i8row"] = {"us": us, "GB/s": gb, "frac": gb / hbm}
+        del q8
+    # the tied lm_head (128256 x 2560, 657 MB: beyond L2 on its own)
+    N, K = cfg.vocab_size, cfg.hidden_size
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    for _ in range(3):
+        be.gemv_d2d(y, x, m.tok_embd, K, N)
+    be.sync_d()
+    g0.record(stream)
+    for _ in range(10):
+        be.gemv_d2d(y, x, m.tok_embd, K, N)
+    g1.record(stream)
+    g1.synchronize()
+    us = g0.elapsed_time(g1) * 1e3 / 10
+    gb = (N * K * 2 + 4 * K + 4 * N) / (us * 1e-6) / 1e9
+    gemv[f"{N}x{K}_f16"] = {"us": us, "GB/s": gb, "frac": gb / hbm}
+    gemv["note"] = ("one tvb_gemv_* launch per call (includes the launch), rotating over the 30 layers' "
+                    "copies (lm_head: one 657 MB copy); bytes = weights + scales + x + y")
 
     # ---- load-time merge: all 210 projections, F16 and per-row INT8 ---------------
     merge = {}
@@ -562,6 +600,46 @@ def run_ours(args, world, rank, local):
                      "tcgen05 delta (F16 within 1 ulp)")
     del outs, scs, lora64, descs64
 
+    # ---- mixed offload (layers 0-13 F16, 14-29 per-row INT8): prefill of a
+    # 1024-token prompt, then 256 greedy decode steps from position 1024 ------
+    mixed = None
+    if args.mixed:
+        be2 = CUDABackend()
+        m2 = Model.load(synth, int8_layers=range(14, cfg.num_layers), backend=be2)
+        stream2 = torch.cuda.ExternalStream(be2.stream)
+        ptoks = rng.integers(0, cfg.vocab_size, 1024).astype(np.int32)
+        for _ in range(2):
+            be2.clear_kv_d()
+            _, t2 = be2.prefill(ptoks, want_logits=False)
+        be2.clear_kv_d()
+        be2.sync_d()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream2)
+        _, t2 = be2.prefill(ptoks, want_logits=False)
+        q1.record(stream2)
+        q1.synchronize()
+        pms = q0.elapsed_time(q1)
+        be2.decode_enqueue(t2, 1024, 4)
+        be2.sync_d()
+        q0.record(stream2)
+        be2.decode_enqueue(0, 1028, 256)
+        q1.record(stream2)
+        q1.synchronize()
+        dms = q0.elapsed_time(q1) / 256
+        Hk = cfg.num_kv_heads * cfg.head_dim
+        layer_f16 = sum(2 * proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ)
+        layer_i8 = sum(proj_shape(cfg, n)[0] * (proj_shape(cfg, n)[1] + 4) for n in PROJ)
+        dbytes = 14 * layer_f16 + (cfg.num_layers - 14) * layer_i8 + cfg.vocab_size * cfg.hidden_size * 2 \
+            + cfg.num_layers * 2 * (1028 + 128) * Hk * 4
+        mixed = {"workload": "2B shape, layers 0-13 F16 and 14-29 per-row INT8: 1024-token prefill, then "
+                             "256 greedy decode steps from position 1028",
+                 "prefill_ms": pms, "prefill_tok_s": 1024 / (pms * 1e-3),
+                 "decode_ms_per_token": dms, "decode_tok_s": 1e3 / dms,
+                 "decode_bytes_per_token": dbytes, "decode_GB/s": dbytes / (dms * 1e-3) / 1e9,
+                 "decode_frac_of_hbm": dbytes / (dms * 1e-3) / 1e9 / hbm}
+        be2.close()
+        del m2
+
     # ---- CPU baseline: the reference's own decode on this host --------------------
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -595,7 +673,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline, "gemv_standalone": gemv,
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps,   # one decode_step_kernel launch per token
-            "clocks": clk.report(), "merge": merge, "prefill": prefill, "tp_8b": tp8,
+            "clocks": clk.report(), "merge": merge, "prefill": prefill, "mixed_offload": mixed, "tp_8b": tp8,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -620,6 +698,8 @@ def main():
     ap.add_argument("--no-tp", action="store_true",
                     help="skip the tensor-parallel 8B decode measurement")
     ap.add_argument("--tp-prompt", type=int, default=512)
+    ap.add_argument("--no-mixed", dest="mixed", action="store_false",
+                    help="skip the mixed F16/INT8 prefill + decode measurement")
     ap.add_argument("--prefill-len", type=int, default=1024,
                     help="profiling with --only prefill: prompt length")
     ap.add_argument("--only-tp", action="store_true",

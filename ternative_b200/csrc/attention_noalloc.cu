@@ -91,8 +91,9 @@ static float* scratch_for_current_device(tvb_status* st) {
             *st = cuda_error(e, "cudaGetSymbolAddress(attention scratch)");
             return nullptr;
         }
+        // the largest attention item: 4 query heads per KV head
         e = cudaFuncSetAttribute(attn_split_noalloc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kGemvWarps * (kNoAllocHeadDim + 4) * (int)sizeof(float));
+                                 attn_item_smem(4, kNoAllocHeadDim));
         if (e != cudaSuccess) {
             *st = cuda_error(e, "cudaFuncSetAttribute");
             return nullptr;
@@ -143,7 +144,7 @@ extern "C" tvb_status tvb_attention_decode_noalloc(const float* q, const float* 
     a.kv_len = kv_len;
     const cudaStream_t st = as_stream(stream);
     attn_split_noalloc_kernel<<<n_kv_heads * nsplit, kGemvThreads,
-                                kGemvWarps * (head_dim + 4) * sizeof(float), st>>>(a);
+                                attn_item_smem(group, head_dim), st>>>(a);
     TVB_CUDA(cudaGetLastError());
     attn_merge_noalloc_kernel<<<n_heads, 32, 0, st>>>(scratch, nsplit, head_dim, out);
     return check_launch("attn_merge_noalloc_kernel");

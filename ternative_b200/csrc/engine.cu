@@ -386,7 +386,7 @@ tvb_status ensure_graphs(tvb_context* c) {
     std::vector<Phase> ph = build_phases(c);
     // shared memory: the largest per-phase layout, and the attention scratch
     const int G = num_sms();
-    int smem = 1024 + kGemvWarps * (c->cfg.head_dim + 4) * 4;
+    int smem = 1024 + attn_item_smem(c->cfg.num_heads / c->cfg.num_kv_heads, c->cfg.head_dim);
     for (const Phase& p : ph) {
         if (p.kind != PK_GEMV) continue;
         const int R = (p.mode == GM_QKV || p.mode == GM_GATEUP) ? 2 : 1;

@@ -241,11 +241,31 @@ __device__ __forceinline__ float2 dot8_h(uint4 u, const float4& xlo, const float
     acc = ffma2(make_float2(w[6], w[7]), make_float2(xhi.z, xhi.w), acc);
     return acc;
 }
+// (v.x, v.y, v.z, v.w) rotated left by r words.
+__device__ __forceinline__ uint4 rot_words(const uint4& v, int r) {
+    const uint4 t = (r & 1) ? make_uint4(v.y, v.z, v.w, v.x) : v;
+    return (r & 2) ? make_uint4(t.z, t.w, t.x, t.y) : t;
+}
+
+// acc += 4 int8 weights . 4 activations.  Each biased byte (b + 128) is
+// placed by one byte permute into the low mantissa of 2^23 (the float
+// 2^23 + 128 + b); one packed add per pair removes 2^23 + 128 exactly.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
 __device__ __forceinline__ float2 dot4_i8(uint32_t u, const float4& x, float2 acc) {
-    float w[4];
-    i8x4_to_f4(u, w);
-    acc = ffma2(make_float2(w[0], w[1]), make_float2(x.x, x.y), acc);
-    acc = ffma2(make_float2(w[2], w[3]), make_float2(x.z, x.w), acc);
+    const uint32_t b = u ^ 0x80808080u;
+    constexpr uint32_t kMagic = 0x4B000000u;   // bytes 4-7 of the permute: 00 00 00 4B
+    const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+    const float2 one = make_float2(1.0f, 1.0f);
+    const float2 w01 = ffma2(make_float2(__uint_as_float(prmt(b, kMagic, 0x7540u)), __uint_as_float(prmt(b, kMagic, 0x7541u))),
+                             one, bias);
+    const float2 w23 = ffma2(make_float2(__uint_as_float(prmt(b, kMagic, 0x7542u)), __uint_as_float(prmt(b, kMagic, 0x7543u))),
+                             one, bias);
+    acc = ffma2(w01, make_float2(x.x, x.y), acc);
+    acc = ffma2(w23, make_float2(x.z, x.w), acc);
     return acc;
 }
 
@@ -511,6 +531,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
 
     // ---- main loop: kDepth chunks in flight per warp ---------------------------------
     const int hsel = (lane >> 2) & 1;   // bank-conflict-free order for the F16 x loads
+    const int qrot = (lane >> 1) & 3;   // and for the INT8 ones
     for (int k0 = 0; k0 < g.mine; k0 += kDepth) {
 #pragma unroll
         for (int j = 0; j < kDepth; ++j) {
@@ -534,11 +555,14 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
                 } else {
                     const int e = e0 + 512 * i + lane * 16;
                     if (e < K) {
+                        // the lane's 16 activations as 4 float4, read in a rotated
+                        // order (quad (q + lane / 2) % 4): conflict-free shared memory
                         const float4* xp = reinterpret_cast<const float4*>(xs + e);
-                        acc0 = dot4_i8(buf.v[j][i].x, xp[0], acc0);
-                        acc1 = dot4_i8(buf.v[j][i].y, xp[1], acc1);
-                        acc0 = dot4_i8(buf.v[j][i].z, xp[2], acc0);
-                        acc1 = dot4_i8(buf.v[j][i].w, xp[3], acc1);
+                        const uint4 w = rot_words(buf.v[j][i], qrot);
+                        acc0 = dot4_i8(w.x, xp[qrot], acc0);
+                        acc1 = dot4_i8(w.y, xp[(qrot + 1) & 3], acc1);
+                        acc0 = dot4_i8(w.z, xp[(qrot + 2) & 3], acc0);
+                        acc1 = dot4_i8(w.w, xp[(qrot + 3) & 3], acc1);
                     }
                 }
             }
