@@ -11,6 +11,7 @@
 // chain steps without the host.
 #include "decode.cuh"
 #include "prefill.h"
+#include "tp_prefill.h"
 
 #include <algorithm>
 #include <cmath>
@@ -48,7 +49,7 @@ static cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size
 // opt-in per-block limit minus a margin for the kernels' static shared memory.
 static int g_max_dyn_smem = 0;
 
-template <int MODE, int WT, int R>
+template <int MODE, int WT, int R, bool TP = false>
 static tvb_status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
     const int units = gemv_units<MODE>(a, R);
     if (units <= 0) return TVB_OK;
@@ -56,7 +57,7 @@ static tvb_status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
     const GemvSmem L = gemv_smem_layout(a.K, WT == WT_F16 ? 2 : 1, gemv_rows_cap(units, grid, R));
     if (L.total > g_max_dyn_smem)
         return set_error(TVB_ERR_UNSUPPORTED, "gemv: K=%d too large for shared-memory staging", a.K);
-    auto kern = stream_gemv_kernel<MODE, WT, R>;
+    auto kern = stream_gemv_kernel<MODE, WT, R, TP>;
     TVB_CUDA(launch_ex(kern, dim3(grid), dim3(kGemvThreads), (size_t)L.total, st, pdl, a));
     return TVB_OK;
 }
@@ -83,6 +84,8 @@ tvb_status prepare_kernels() {
         allow_smem<GM_RESID, WT_F16, 1>(), allow_smem<GM_RESID, WT_I8, 1>(),
         allow_smem<GM_GATEUP, WT_F16, 2>(), allow_smem<GM_GATEUP, WT_I8, 2>(),
         allow_smem<GM_LMHEAD, WT_F16, 1>(),
+        cudaFuncSetAttribute(stream_gemv_kernel<GM_LMHEAD, WT_F16, 1, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, g_max_dyn_smem),
     };
     for (cudaError_t x : r)
         if (x != cudaSuccess) e = x;
@@ -171,6 +174,8 @@ struct tvb_context {
     bool tp_ready = false;
     float* e_x2 = nullptr;
     int n_push = 0;   // row-parallel exchanges per launch (both graphs)
+    size_t tp_pf_off = 0;   // float offset of the prefill region in every rank's exchange buffer
+    float* pf_inv = nullptr;   // per-row 1/rms of a tensor-parallel sub-norm
     uint16_t* pf_w16 = nullptr;
     size_t pf_w16_elems = 0;
 };
@@ -434,6 +439,7 @@ tvb_status pf_workspace(tvb_context* c) {
         {(void**)&c->pf_attn, (size_t)cap * c->Hq * 4}, {(void**)&c->pf_h, (size_t)cap * c->I * 4},
         {(void**)&c->pf_xh, cap * kmax * 2},          {(void**)&c->pf_xl, cap * kmax * 2},
         {(void**)&c->pf_exp, (size_t)cap * 4},        {(void**)&c->pf_tok, (size_t)c->cfg.max_seq_len * 4},
+        {(void**)&c->pf_inv, (size_t)cap * 4},
     };
     for (auto& a : allocs) TVB_TRY(alloc_dev(a.p, a.b));
     if (pf_attention_tc_supported(c->cfg.num_heads, c->cfg.num_kv_heads, c->cfg.head_dim))
@@ -441,6 +447,13 @@ tvb_status pf_workspace(tvb_context* c) {
                                                               c->cfg.num_kv_heads)));
     c->pf_cap = cap;
     return TVB_OK;
+}
+
+// The batched prefill tiles K by 64 (every projection's input width), gate/up
+// rows by 32 and the attention's 64-row blocks by whole query-head groups.
+bool pf_batched_supported(const tvb_context* c) {
+    const int group = c->cfg.num_heads / c->cfg.num_kv_heads;
+    return c->H % 64 == 0 && c->Hq % 64 == 0 && c->I % 64 == 0 && 64 % group == 0;
 }
 
 // One projection operand; INT8 weights are widened to F16 into the scratch at
@@ -476,11 +489,41 @@ tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size
 // KV row so far -> sub-norm -> o_proj + residual -> ffn_norm -> gate/up with
 // relu^2 * up fused -> sub-norm -> down + residual; then output_norm + lm_head
 // + argmax of the last row, leaving the step state at (pos S, argmax).
+//
+// Tensor parallelism: q/k/v, attention and gate/up run on this rank's heads and
+// rows; o_proj and down multiply this rank's columns into its exchange region
+// (the sub-norm before them deferred to the reduction), and after a flag sync
+// every rank adds all ranks' partial rows, in rank order, to its copy of the
+// residual.  The lm_head takes this rank's vocabulary slice and the ranks agree
+// on the argmax through the decode step's key exchange.
 tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
     TVB_TRY(pf_workspace(c));
     const cudaStream_t st = c->stream;
     const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
     const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
+    const bool tp = c->tp_world > 1;
+    TpArgs tpa = {};
+    size_t reg_off[2] = {0, 0};
+    float* reg[2] = {nullptr, nullptr};
+    if (tp) {
+        tpa.world = c->tp_world;
+        tpa.rank = c->tp_rank;
+        tpa.ld = H + 4;
+        for (int r = 0; r < c->tp_world; ++r) tpa.peer[r] = c->tp_peer[r];
+        tpa.index = -1;
+        tpa.fold = -1;
+        const size_t region = tp_prefill_region_floats(c->pf_cap, H);
+        for (int j = 0; j < 2; ++j) {
+            reg_off[j] = c->tp_pf_off + j * region;
+            reg[j] = c->tp_xchg + reg_off[j];
+        }
+    }
+    // a row-parallel projection: its partial rows into exchange region j, a
+    // sync, and the residual += inv_rms * the ranks' partial rows
+    auto exchange = [&](int j, int n, const void* sub_norm, int k_local) -> tvb_status {
+        TVB_TRY(tp_sync(tpa, c->st, st));
+        return tp_reduce_rows(tpa, reg_off[j], n, H, sub_norm ? k_local * c->tp_world : 0, eps, c->pf_x, st);
+    };
     for (int i = 0; i < S; ++i) c->h_io[i] = tokens[i];
     TVB_CUDA(cudaMemcpyAsync(c->pf_tok, c->h_io, (size_t)S * 4, cudaMemcpyHostToDevice, st));
     int last_rows = 0;
@@ -522,14 +565,16 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
             else
                 TVB_TRY(pf_attention(c->pf_q, kl, vl, n, p0, g.nh, g.nkv, hd, scale, c->pf_attn, st));
             // attn_sub_norm -> o_proj -> residual
-            TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, n, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, n, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
+                                  tp ? reg[0] + (size_t)n * H : nullptr));
             off = 0;
-            g.mode = PF_RESID;
+            g.mode = tp ? PF_STORE : PF_RESID;
             g.K = Hq;
             TVB_TRY(pf_operand(c, lw.wo, H, Hq, off, g.m[0]));
-            g.y = c->pf_x;
+            g.y = tp ? reg[0] : c->pf_x;
             g.ldy = H;
             TVB_TRY(pf_gemm(g, st));
+            if (tp) TVB_TRY(exchange(0, n, lw.attn_sub_norm, Hq));
             // ffn_norm -> gate/up -> relu^2 * up
             TVB_TRY(pf_norm_split(c->pf_x, lw.ffn_norm, n, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
             off = 0;
@@ -541,14 +586,16 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
             g.ldy = I;
             TVB_TRY(pf_gemm(g, st));
             // ffn_sub_norm -> down -> residual
-            TVB_TRY(pf_norm_split(c->pf_h, lw.ffn_sub_norm, n, I, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+            TVB_TRY(pf_norm_split(c->pf_h, lw.ffn_sub_norm, n, I, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
+                                  tp ? reg[1] + (size_t)n * H : nullptr));
             off = 0;
-            g.mode = PF_RESID;
+            g.mode = tp ? PF_STORE : PF_RESID;
             g.K = I;
             TVB_TRY(pf_operand(c, lw.w_down, H, I, off, g.m[0]));
-            g.y = c->pf_x;
+            g.y = tp ? reg[1] : c->pf_x;
             g.ldy = H;
             TVB_TRY(pf_gemm(g, st));
+            if (tp) TVB_TRY(exchange(1, n, lw.ffn_sub_norm, I));
         }
     }
     // output_norm + lm_head + argmax of the last row (the decode step's last
@@ -557,9 +604,10 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
     c->h_io[S + 1] = tokens[S - 1];
     TVB_CUDA(cudaMemcpyAsync(c->st, c->h_io + S, 8, cudaMemcpyHostToDevice, st));
     GemvArgs a = {};
-    a.w[0] = c->tok_embd;
+    const int vs = c->V / c->tp_world;   // this rank's vocabulary slice
+    a.w[0] = static_cast<const uint16_t*>(c->tok_embd) + (size_t)c->tp_rank * vs * H;
     a.tscale[0] = 1.0f;
-    a.N = c->V;
+    a.N = vs;
     a.K = H;
     a.x = c->pf_x + (size_t)(last_rows - 1) * H;
     a.norm_w = c->output_norm;
@@ -567,7 +615,11 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
     a.y = c->e_logits;
     a.st = c->st;
     a.status = &c->st->status;
-    return launch_gemv<GM_LMHEAD, WT_F16, 1>(a, st, false);
+    if (!tp) return launch_gemv<GM_LMHEAD, WT_F16, 1>(a, st, false);
+    a.tp = tpa;
+    a.tp.vocab0 = c->tp_rank * vs;
+    a.tp.index = 0;   // the argmax exchange over the ranks' slices
+    return launch_gemv<GM_LMHEAD, WT_F16, 1, true>(a, st, false);
 }
 
 }  // namespace
@@ -671,7 +723,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
                    c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
-                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes};
+                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes, c->pf_inv};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
@@ -690,7 +742,12 @@ tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
                 "tp_init: rank %d of %d (at most %d ranks)", rank, world, kMaxTp);
     TVB_REQUIRE(c->V % world == 0, "tp_init: vocabulary %d not divisible by %d ranks", c->V, world);
     TVB_REQUIRE(!c->tp_xchg, "tp_init: already initialised");
-    const size_t floats = (size_t)kTpSlots + 2ull * world * (c->H + 4);
+    // decode exchange area, then the batched-prefill region (partial rows and
+    // row sums of squares of up to max_prefill rows)
+    const size_t decode_floats = (size_t)kTpSlots + 2ull * world * (c->H + 4);
+    c->tp_pf_off = (decode_floats + 63) / 64 * 64;
+    const int pf_rows = std::min(c->cfg.max_prefill, c->cfg.max_seq_len);
+    const size_t floats = c->tp_pf_off + 2 * tp_prefill_region_floats(pf_rows, c->H);
     TVB_TRY(alloc_dev((void**)&c->tp_xchg, floats * 4));
     TVB_CUDA(cudaMemset(c->tp_xchg, 0, floats * 4));
     c->tp_world = world;
@@ -893,9 +950,9 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
     TVB_TRY(ensure_graphs(c));
     // the pinned staging is about to be rewritten: let earlier copies from it finish
     TVB_CUDA(cudaStreamSynchronize(c->stream));
-    if (c->tp_world > 1) {
-        // tensor-parallel ranks: one decode-step launch per prompt row (the
-        // exchanges run inside it); row s attends to KV rows [0, s] as in
+    if (!pf_batched_supported(c)) {
+        // shapes the tensor-core kernels do not tile: one decode-step launch
+        // per prompt row; row s attends to KV rows [0, s] as in
         // forward_prefill (model.cpp:1084 kv_len = s + 1)
         for (int s = 0; s < S; ++s) {
             c->h_io[2 * s] = s;

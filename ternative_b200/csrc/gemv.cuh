@@ -689,6 +689,7 @@ __device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgma
                         const unsigned long long k = __ldcg(keys + r);
                         fin = k > fin ? k : fin;
                     }
+                    a.st->tp_epoch = e;   // (the decode step's exit writes the same value)
                 }
             }
             a.st->next_token = argmax_index(fin);
@@ -702,7 +703,7 @@ __device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgma
 }
 
 // Stand-alone launch of one GEMV phase (the per-op API and tests).
-template <int MODE, int WT, int R>
+template <int MODE, int WT, int R, bool TP = false>
 __global__ void __launch_bounds__(kGemvThreads, 1)
 stream_gemv_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -714,8 +715,8 @@ stream_gemv_kernel(const __grid_constant__ GemvArgs a) {
     const int token = (MODE == GM_QKV && a.gather_token) ? __ldcg(&a.st->token) : 0;
     gemv_stage<MODE, WT, R>(a, smem, gridDim.x, pos);
     GemvArgmax best{-INFINITY, 0};
-    gemv_run<MODE, WT, R>(a, smem, gridDim.x, pos, token, buf, best);
-    if (MODE == GM_LMHEAD) lmhead_finish(a, best);
+    gemv_run<MODE, WT, R, TP>(a, smem, gridDim.x, pos, token, buf, best);
+    if (MODE == GM_LMHEAD) lmhead_finish<TP>(a, best, TP ? __ldcg(&a.st->tp_epoch) : 0u);
 }
 
 }  // namespace tvb

@@ -466,7 +466,8 @@ constexpr int kNsThreads = 256;
 
 __global__ void __launch_bounds__(kNsThreads)
 pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
-                     __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp) {
+                     __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp,
+                     float* __restrict__ ss_out) {
     const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
     const float4* w4 = reinterpret_cast<const float4*>(w);
@@ -486,8 +487,16 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
         if (tid == 0) {
             float t = 0.f;
             for (int i = 0; i < kNsThreads / 32; ++i) t += red[i];
-            // tensor.cpp:672-673: rms = sqrt(ss/n + eps); inv_rms = 1/rms
-            s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
+            // tensor.cpp:672-673: rms = sqrt(ss/n + eps); inv_rms = 1/rms.  A
+            // sub-norm whose row spans the tensor-parallel ranks is deferred:
+            // the row's sum of squares goes out and the consumer scales by the
+            // factor of the ranks' summed squares.
+            if (ss_out) {
+                ss_out[row] = t;
+                s_inv = 1.0f;
+            } else {
+                s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), eps)));
+            }
         }
         __syncthreads();
         inv = s_inv;
@@ -557,10 +566,10 @@ __global__ void pf_i8_kernel(const int8_t* __restrict__ q, size_t n, __half* __r
 }
 
 tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh, uint16_t* xl,
-                         int* row_exp, cudaStream_t st) {
+                         int* row_exp, cudaStream_t st, float* ss_out) {
     TVB_REQUIRE(x && xh && xl && row_exp && S > 0 && K > 0 && K % 4 == 0, "norm_split: bad arguments");
     pf_norm_split_kernel<<<S, kNsThreads, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
-                                                   reinterpret_cast<__half*>(xl), row_exp);
+                                                   reinterpret_cast<__half*>(xl), row_exp, ss_out);
     return check_launch("pf_norm_split_kernel");
 }
 

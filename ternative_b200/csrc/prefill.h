@@ -59,8 +59,11 @@ tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float
 // written as F16 hi + lo planes for the tensor cores with a power-of-two row
 // scale: v = (hi + lo) * 2^row_exp, |v / 2^row_exp| < 2^15.  w == nullptr: no
 // norm (the plain split, for CUDABackend::matmul).
+// ss_out (optional, with w): defer the normalisation -- the rows are scaled by
+// w only and each row's sum of squares is written to ss_out[s] (a sub-norm
+// whose rows span the tensor-parallel ranks).
 tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh,
-                         uint16_t* xl, int* row_exp, cudaStream_t st);
+                         uint16_t* xl, int* row_exp, cudaStream_t st, float* ss_out = nullptr);
 
 // Causal GQA attention of S query rows at positions pos0 .. pos0 + S - 1 over
 // KV rows [0, pos0 + s] (compute_batched_attention, model.cpp:1071-1137).

@@ -1,0 +1,85 @@
+// Tensor-parallel batched prefill: the exchanges between the tensor-core
+// kernels of prefill.cu when each rank holds a shard of every layer
+// (q/k/v and gate/up by rows, o_proj and down by columns).
+//
+// Every rank's exchange buffer (the IPC mapping the decode step uses) holds,
+// after the decode area, two prefill regions; one region is `rows` partial
+// output rows [rows][H] followed by `rows` per-row sums of squares.  A rank
+// writes only its own regions; the others read them over NVLink after a flag
+// sync.  Per layer:
+//
+//   attention -> sub-norm input scaled by its weight, row sums of squares out
+//   -> o_proj partial rows (region 0) -> sync -> residual += inv_rms * sum of
+//   the ranks' partial rows (rank order) -> ffn_norm -> gate/up -> the same
+//   with down (region 1).
+//
+// The sub-norm's 1/rms needs the squares of the full row, which the ranks hold
+// in parts; o_proj and down are linear, so each rank multiplies its shard
+// un-normalised and the reduction applies the factor of the summed squares
+// (as the decode step's fold does).  A region is rewritten one exchange after
+// its sync: by then every rank has signalled the next sync, which it does only
+// after its reads of the region, so two regions need no extra sync.
+#include "tp_prefill.h"
+
+#include <algorithm>
+
+namespace tvb {
+
+// One thread: order this rank's earlier writes (previous kernels of the
+// stream) at system scope, signal every rank, wait (bounded) for all of them.
+__global__ void tp_sync_kernel(const __grid_constant__ TpArgs t, StepState* st) {
+    const unsigned e = st->tp_epoch + 1u;
+    tp_signal(t, e);
+    if (tp_wait(t, e, &st->abort, &st->status)) st->tp_epoch = e;
+}
+
+// Row s of x [S][H] += inv_s * (sum over ranks, in rank order, of their partial
+// row s at float offset `off`), inv_s = 1/sqrt(sum_r ss_r[s] / norm_n + eps)
+// (tensor.cpp:672-673) or 1 without a sub-norm (norm_n == 0).
+__global__ void tp_reduce_rows_kernel(const __grid_constant__ TpArgs t, size_t off, int S, int H, int norm_n,
+                                      float eps, float* __restrict__ x) {
+    const int row = blockIdx.x, tid = threadIdx.x;
+    __shared__ float s_inv;
+    if (tid == 0) {
+        float inv = 1.0f;
+        if (norm_n > 0) {
+            float ss = 0.f;
+            for (int r = 0; r < t.world; ++r) ss += __ldcg(t.peer[r] + off + (size_t)S * H + row);
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)norm_n), eps)));
+        }
+        s_inv = inv;
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    const size_t base = off + (size_t)row * H;
+    float4* x4 = reinterpret_cast<float4*>(x + (size_t)row * H);
+    for (int k = tid; k < (H >> 2); k += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < t.world; ++r) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(t.peer[r] + base) + k);
+            acc = make_float4(acc.x + p.x, acc.y + p.y, acc.z + p.z, acc.w + p.w);
+        }
+        float4 v = x4[k];
+        v = make_float4(__fadd_rn(v.x, acc.x * inv), __fadd_rn(v.y, acc.y * inv), __fadd_rn(v.z, acc.z * inv),
+                        __fadd_rn(v.w, acc.w * inv));
+        x4[k] = v;
+    }
+}
+
+size_t tp_prefill_region_floats(int rows, int H) {
+    return ((size_t)rows * H + (size_t)rows + 63) / 64 * 64;
+}
+
+tvb_status tp_sync(const TpArgs& t, StepState* st, cudaStream_t stream) {
+    tp_sync_kernel<<<1, 1, 0, stream>>>(t, st);
+    return check_launch("tp_sync_kernel");
+}
+
+tvb_status tp_reduce_rows(const TpArgs& t, size_t off, int S, int H, int norm_n, float eps, float* x,
+                          cudaStream_t stream) {
+    TVB_REQUIRE(S > 0 && H % 4 == 0 && off % 4 == 0, "tp_reduce_rows: bad arguments");
+    tp_reduce_rows_kernel<<<S, 256, 0, stream>>>(t, off, S, H, norm_n, eps, x);
+    return check_launch("tp_reduce_rows_kernel");
+}
+
+}  // namespace tvb

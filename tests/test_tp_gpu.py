@@ -1,7 +1,8 @@
-"""Tensor-parallel decode on 2 (and 4) GPUs against the single-GPU path.
+"""Tensor-parallel prefill and decode on 2 (and 4) GPUs against the single-GPU path.
 
 Each rank is a process on its own GPU (spawned), holds its shard of a small
-model merged from the same synthetic I2_S + LoRA weights, and runs prefill and
+model merged from the same synthetic I2_S + LoRA weights, and runs the batched
+prefill (partial rows exchanged through the ranks' IPC-mapped regions) and
 greedy decode steps whose row-parallel exchanges go over NVLink inside the
 decode-step kernel.  Checked: every rank produces the same tokens; the ranks'
 vocabulary slices of the logits, put together, match the single-GPU decode
@@ -97,13 +98,16 @@ def _run(world, cfg, prompt, n_new):
     return res
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tp_decode_matches_single_gpu(world):
+@pytest.mark.parametrize("world,prompt_len,max_prefill", [(2, 9, 256), (4, 9, 256), (2, 150, 64)])
+def test_tp_decode_matches_single_gpu(world, prompt_len, max_prefill):
+    """The batched tensor-parallel prefill (one chunk, or three chunks of at
+    most 64 rows) followed by tensor-parallel decode steps."""
     from ternative_b200.backend import Config
     # 8 query / 4 KV heads, FFN 2048: shards of whole heads and 128-column blocks at 2 and 4 ranks
     cfg = Config(vocab_size=4096, hidden_size=512, num_layers=3, num_heads=8, num_kv_heads=4,
-                 head_dim=128, intermediate_size=2048, max_seq_len=256, max_prefill=256)
-    prompt = np.random.default_rng(world).integers(0, cfg.vocab_size, 9).astype(np.int32)
+                 head_dim=128, intermediate_size=2048, max_seq_len=256, max_prefill=max_prefill)
+    prompt = np.random.default_rng(world + prompt_len).integers(0, cfg.vocab_size,
+                                                                prompt_len).astype(np.int32)
     res = _run(world, cfg, prompt, 12)
     toks = res[0]["toks"]
     for r in range(world):
