@@ -161,6 +161,9 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
             phase_gemv<TP>(ph, smem, G, pos, token, buf, best, push0);
             if (ph.mode == GM_LMHEAD) lmhead_finish<TP>(ph.g, best, epoch0);
         } else {
+            // No weight chunks are in flight across an attention phase (it has
+            // none to prefetch); saying so frees the chunk registers for it.
+            buf = ChunkBuf{};
             __syncthreads();
             if (b < ph.at.nkv * ph.at.nsplit) attn_item(ph.at, b, smem + 1024, pos);
         }
