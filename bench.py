@@ -230,8 +230,10 @@ def run_tp_8b(args, world, rank):
     from ternative_b200.tp import TPModel, shard_config
 
     cfg = SHAPES["8b"]
-    cfg = dataclasses.replace(cfg, max_seq_len=max(cfg.max_seq_len, args.tp_prompt + args.warmup
-                                                   + args.steps + 8))
+    # KV for the batch-1 run and the batch of 8 sequences (slots 0..7); each
+    # sequence needs its prompt plus the warm-up and timed steps
+    cfg = dataclasses.replace(cfg, max_seq_len=args.tp_prompt + args.warmup + args.steps + 8,
+                              max_batch=TP_BATCH)
 
     def all_gather(obj):
         if world == 1:
@@ -297,12 +299,127 @@ def run_tp_8b(args, world, rank):
            "peak_kind": kind, "prefill_ms": prefill_ms,
            "prefill_tok_s": args.tp_prompt / (prefill_ms * 1e-3),
            "prefill_path": "batched tensor cores" + (", partial rows exchanged over NVLink" if world > 1 else "")}
+    res["batch8"] = tp_batch_decode(args, be, cfg, world, stream, n_w, hbm)
     if world > 1:
         dist.barrier()
     m.close()
     del synth
     torch.cuda.empty_cache()
     return res
+
+
+TP_BATCH = 8
+
+
+def tp_batch_decode(args, be, cfg, world, stream, n_w, hbm):
+    """Batch of TP_BATCH concurrent sequences on the 8B shape: each prompt
+    (tp_prompt random ids) prefilled into its own KV slot, then greedy steps
+    that advance all sequences by one token (tvb_decode_batch: one tensor-core
+    GEMM per projection over the B rows, every weight read once per step).
+    Timed: `steps` host-driven batched steps (each returns the B next tokens to
+    the host), CUDA events on the context stream, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from ternative_b200.tp import shard_config
+    B = TP_BATCH
+    rng = np.random.default_rng(7)
+    be.clear_kv_d()
+    cur = np.empty(B, np.int32)
+    for b in range(B):
+        prompt = rng.integers(0, cfg.vocab_size, args.tp_prompt).astype(np.int32)
+        _, cur[b] = be.prefill_slot(b, prompt, want_logits=False)
+    pos = np.full(B, args.tp_prompt, np.int32)
+    for _ in range(args.warmup):
+        _, cur = be.decode_batch(cur, pos, want_logits=False)
+        pos += 1
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, cur = be.decode_batch(cur, pos, want_logits=False)
+        pos += 1
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    local = shard_config(cfg, world)
+    kv = B * cfg.num_layers * 2 * (int(pos.mean()) - args.steps // 2) * local.num_kv_heads * 128 * 4
+    per_gpu = (n_w + kv) / (ms / args.steps * 1e-3) / 1e9
+    return {"sequences": B, "tok_s": B * args.steps / (ms * 1e-3), "ms_per_step": ms / args.steps,
+            "per_gpu_GB/s": per_gpu, "frac_of_hbm": per_gpu / hbm,
+            "note": f"{B} sequences after {args.tp_prompt}-token prompts; tok_s counts every sequence's "
+                    "token; bytes = this rank's weights once per step + the 8 sequences' KV rows"}
+
+
+def gemv_tp_sweep(be, m, cfg, stream, world, rank, hbm):
+    """The GEMV sweep's large shapes split over the job's ranks, one rank per
+    GPU: column split on N (gate 6912x2560 and the 128256x2560 lm_head: each
+    rank streams N/T rows, no exchange) and row split on K (down 2560x6912:
+    each rank streams its K/T columns, then an NCCL all-reduce of the N
+    partial outputs).  Each rank's shard is a contiguous copy per layer, so the
+    rotation over the layers' copies keeps the weights coming from HBM.  Time
+    per GEMV = CUDA events on the backend stream, max over ranks; GB/s = the
+    whole matrix's bytes / that time (aggregate over the ranks)."""
+    import torch
+    import torch.distributed as dist
+    from ternative_b200.model import proj_shape
+
+    def timed(run, reps):
+        for i in range(3):
+            run(i)
+        be.sync_d()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            run(i)
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / reps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    out = {}
+    cases = [("w_gate", "column"), ("w_down", "row")]
+    for name, split in cases:
+        N, K = proj_shape(cfg, name)
+        if split == "column":
+            n = N // world
+            shards = [m.weights[li][name][rank * n:(rank + 1) * n].contiguous() for li in range(cfg.num_layers)]
+            x = torch.randn(K, device="cuda")
+            y = torch.empty(n, device="cuda")
+            us = timed(lambda i: be.gemv_d2d(y, x, shards[i % len(shards)], K, n), 2 * cfg.num_layers)
+        else:
+            k = K // world
+            shards = [m.weights[li][name][:, rank * k:(rank + 1) * k].contiguous()
+                      for li in range(cfg.num_layers)]
+            x = torch.randn(k, device="cuda")
+            y = torch.empty(N, device="cuda")
+
+            def run(i):
+                be.gemv_d2d(y, x, shards[i % len(shards)], k, N)
+                with torch.cuda.stream(stream):
+                    dist.all_reduce(y)
+            us = timed(run, 2 * cfg.num_layers)
+        gb = (N * K * 2 + 4 * K + 4 * N) / (us * 1e-6) / 1e9
+        out[f"{N}x{K}_f16_{split}"] = {"us": us, "GB/s": gb, "per_gpu_frac": gb / world / hbm}
+        del shards
+    N, K = cfg.vocab_size, cfg.hidden_size
+    n = N // world
+    head = m.tok_embd[rank * n:(rank + 1) * n]
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(n, device="cuda")
+    us = timed(lambda i: be.gemv_d2d(y, x, head, K, n), 10)
+    gb = (N * K * 2 + 4 * K + 4 * N) / (us * 1e-6) / 1e9
+    out[f"{N}x{K}_f16_column"] = {"us": us, "GB/s": gb, "per_gpu_frac": gb / world / hbm}
+    out["note"] = (f"split over {world} ranks; row split includes the NCCL all-reduce of the {cfg.hidden_size} "
+                   "partial outputs; time = max over ranks; GB/s = whole matrix bytes / time")
+    return out
 
 
 def run_ours(args, world, rank, local):
@@ -529,6 +646,8 @@ def run_ours(args, world, rank, local):
     gemv[f"{N}x{K}_f16"] = {"us": us, "GB/s": gb, "frac": gb / hbm}
     gemv["note"] = ("one tvb_gemv_* launch per call (includes the launch), rotating over the 30 layers' "
                     "copies (lm_head: one 657 MB copy); bytes = weights + scales + x + y")
+    if world > 1:
+        gemv["tensor_parallel"] = gemv_tp_sweep(be, m, cfg, stream, world, rank, hbm)
 
     # ---- load-time merge: all 210 projections, F16 and per-row INT8 ---------------
     merge = {}

@@ -205,6 +205,7 @@ typedef struct {
     float rope_theta;
     float rms_norm_eps;
     int max_prefill;     /* largest prefill batch (0 -> 1024) */
+    int max_batch;       /* KV cache slots for batched decode (0 -> 1) */
 } tvb_model_config;
 
 typedef struct tvb_context tvb_context;
@@ -313,6 +314,26 @@ tvb_status tvb_decode_enqueue(tvb_context* ctx, int token, int pos, int n_steps)
  * (and its argmax).  Synchronises. */
 tvb_status tvb_prefill(tvb_context* ctx, const int* tokens_host, int S, float* last_logits_host,
                        int* argmax_host);
+
+/* Batched decode of up to max_batch independent sequences (no reference
+ * counterpart: the reference serves one sequence; its batch of 8 is 8
+ * sequential Model::forward_gpu runs, model.cpp:1354-1582).  Sequence b lives
+ * in KV cache slot b.
+ *
+ * tvb_prefill_slot: tvb_prefill into slot `slot` (slot 0 is the KV cache of
+ * the single-sequence calls); like tvb_prefill it leaves the step state at
+ * (S, argmax).
+ *
+ * tvb_decode_batch: one greedy step of sequences 0 .. B-1: tokens[b] at
+ * positions[b] of slot b (KV row positions[b] is written, attention over rows
+ * [0, positions[b]]).  next_tokens[b] = argmax of row b's logits; logits
+ * (optional, host [B][vocab / tp_world], this rank's slice) receives them.
+ * Every weight byte is read once for all B rows (tensor-core GEMM with B
+ * activation rows).  Synchronises. */
+tvb_status tvb_prefill_slot(tvb_context* ctx, int slot, const int* tokens_host, int S,
+                            float* last_logits_host, int* argmax_host);
+tvb_status tvb_decode_batch(tvb_context* ctx, const int* tokens_host, const int* positions_host, int B,
+                            float* logits_host, int* next_tokens_host);
 
 #ifdef __cplusplus
 }

@@ -42,7 +42,8 @@ class ModelConfig(C.Structure):
     _fields_ = [("vocab_size", C.c_int), ("hidden_size", C.c_int), ("num_layers", C.c_int),
                 ("num_heads", C.c_int), ("num_kv_heads", C.c_int), ("head_dim", C.c_int),
                 ("intermediate_size", C.c_int), ("max_seq_len", C.c_int),
-                ("rope_theta", C.c_float), ("rms_norm_eps", C.c_float), ("max_prefill", C.c_int)]
+                ("rope_theta", C.c_float), ("rms_norm_eps", C.c_float), ("max_prefill", C.c_int),
+                ("max_batch", C.c_int)]
 
 
 class Buffers(C.Structure):
@@ -115,6 +116,8 @@ _SIGS = {
     "tvb_generate_greedy": [_P, _I, _I, _I, _P],
     "tvb_decode_enqueue": [_P, _I, _I, _I],
     "tvb_prefill": [_P, _P, _I, _P, _P],
+    "tvb_prefill_slot": [_P, _I, _P, _I, _P, _P],
+    "tvb_decode_batch": [_P, _P, _P, _I, _P, _P],
     "tvb_tp_init": [_P, _I, _I, C.POINTER(C.c_void_p)],
     "tvb_tp_set_peers": [_P, C.POINTER(C.c_void_p)],
     "tvb_ipc_export": [_P, C.POINTER(IpcHandle)],

@@ -54,11 +54,13 @@ class Config:
     rope_theta: float = 500000.0
     rms_norm_eps: float = 1e-5
     max_prefill: int = 1024
+    max_batch: int = 1      # KV cache slots for batched decode
 
     def to_c(self) -> ModelConfig:
         return ModelConfig(self.vocab_size, self.hidden_size, self.num_layers, self.num_heads,
                            self.num_kv_heads, self.head_dim, self.intermediate_size,
-                           self.max_seq_len, self.rope_theta, self.rms_norm_eps, self.max_prefill)
+                           self.max_seq_len, self.rope_theta, self.rms_norm_eps, self.max_prefill,
+                           self.max_batch)
 
 
 @dataclass
@@ -300,6 +302,30 @@ class CUDABackend:
         call("tvb_prefill", self.ctx, t.ctypes.data, t.size,
              None if logits is None else logits.ctypes.data, C.byref(am))
         return logits, am.value
+
+    def prefill_slot(self, slot: int, tokens, want_logits: bool = True):
+        """prefill() into KV cache slot `slot` (batched decode); slot 0 is the
+        single-sequence cache."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        am = C.c_int()
+        logits = np.empty(self.n_logits(), np.float32) if want_logits else None
+        call("tvb_prefill_slot", self.ctx, slot, t.ctypes.data, t.size,
+             None if logits is None else logits.ctypes.data, C.byref(am))
+        return logits, am.value
+
+    def decode_batch(self, tokens, positions, want_logits: bool = True):
+        """One greedy step of sequences 0..B-1 (sequence b in KV slot b, token
+        tokens[b] at positions[b]).  Returns (logits [B][n_logits] or None,
+        next tokens [B])."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        if t.shape != p.shape or t.ndim != 1:
+            raise ValueError("tokens and positions must be 1-D of the same length")
+        nxt = np.empty(t.size, np.int32)
+        logits = np.empty((t.size, self.n_logits()), np.float32) if want_logits else None
+        call("tvb_decode_batch", self.ctx, t.ctypes.data, p.ctypes.data, t.size,
+             None if logits is None else logits.ctypes.data, nxt.ctypes.data)
+        return logits, nxt
 
     def close(self):
         if self.ctx is not None:

@@ -12,6 +12,7 @@
 #include "decode.cuh"
 #include "prefill.h"
 #include "tp_prefill.h"
+#include "batch_decode.h"
 
 #include <algorithm>
 #include <cmath>
@@ -136,7 +137,9 @@ struct tvb_context {
     float *e_x = nullptr, *e_q = nullptr, *e_attn = nullptr, *e_h = nullptr, *e_logits = nullptr;
     float* attn_part = nullptr;
     int nsplit = 8;    // attention splits per KV head, merged by the o_proj phase
-    float *kcache = nullptr, *vcache = nullptr;
+    float *kcache = nullptr, *vcache = nullptr;   // slots x [L][max_seq][Hk]; slot 0 is the step's
+    int slots = 1;                                // KV cache slots (batched decode)
+    size_t slot_floats = 0;                       // floats per slot
     float *rope_cos = nullptr, *rope_sin = nullptr;
     StepState* st = nullptr;
     int* hist = nullptr;
@@ -175,6 +178,14 @@ struct tvb_context {
     float* e_x2 = nullptr;
     int n_push = 0;   // row-parallel exchanges per launch (both graphs)
     size_t tp_pf_off = 0;   // float offset of the prefill region in every rank's exchange buffer
+    size_t tp_key_off = 0;  // float offset of the batched step's argmax keys
+    // batched decode / split-K workspace (pf_workspace)
+    float* pf_part = nullptr;   // split-K partial sums
+    size_t pf_part_floats = 0;
+    float* bd_attn_part = nullptr;   // [max_batch][nh][splits][hd + 4]
+    float* bd_logits = nullptr;      // [max_batch][V]
+    int* bd_io = nullptr;            // [tokens | positions | next tokens] x kMaxBatch
+    unsigned long long* bd_keys = nullptr;
     float* pf_inv = nullptr;   // per-row 1/rms of a tensor-parallel sub-norm
     uint16_t* pf_w16 = nullptr;
     size_t pf_w16_elems = 0;
@@ -430,6 +441,11 @@ tvb_status check_status(tvb_context* c) {
 
 // ---- batched prefill (Model::forward_prefill, model.cpp:1139-1234) -----------------
 
+// Split-K partial sums of the tensor-core GEMM: a split is chosen only while
+// (tiles x row blocks x splits) fits the SMs, so rows-per-row-block x SMs x 256
+// columns bounds every projection's partials.
+constexpr int kPfPartRows = 128;
+
 tvb_status pf_workspace(tvb_context* c) {
     if (c->pf_cap) return TVB_OK;
     const int cap = std::min(c->cfg.max_prefill, c->cfg.max_seq_len);
@@ -440,8 +456,14 @@ tvb_status pf_workspace(tvb_context* c) {
         {(void**)&c->pf_xh, cap * kmax * 2},          {(void**)&c->pf_xl, cap * kmax * 2},
         {(void**)&c->pf_exp, (size_t)cap * 4},        {(void**)&c->pf_tok, (size_t)c->cfg.max_seq_len * 4},
         {(void**)&c->pf_inv, (size_t)cap * 4},
+        {(void**)&c->pf_part, (size_t)kPfPartRows * num_sms() * 256 * 4},
+        {(void**)&c->bd_attn_part, (size_t)c->slots * c->cfg.num_heads * kMaxAttnSplits * (c->cfg.head_dim + 4) * 4},
+        {(void**)&c->bd_logits, (size_t)c->slots * c->V * 4},
+        {(void**)&c->bd_io, (size_t)3 * kMaxBatch * 4},
+        {(void**)&c->bd_keys, (size_t)kMaxBatch * 8},
     };
     for (auto& a : allocs) TVB_TRY(alloc_dev(a.p, a.b));
+    c->pf_part_floats = (size_t)kPfPartRows * num_sms() * 256;
     if (pf_attention_tc_supported(c->cfg.num_heads, c->cfg.num_kv_heads, c->cfg.head_dim))
         TVB_TRY(alloc_dev(&c->pf_planes, pf_attn_planes_bytes(cap, c->cfg.max_seq_len, c->cfg.num_heads,
                                                               c->cfg.num_kv_heads)));
@@ -496,8 +518,10 @@ tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size
 // every rank adds all ranks' partial rows, in rank order, to its copy of the
 // residual.  The lm_head takes this rank's vocabulary slice and the ranks agree
 // on the argmax through the decode step's key exchange.
-tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
+tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot) {
     TVB_TRY(pf_workspace(c));
+    float* const kslot = c->kcache + (size_t)slot * c->slot_floats;
+    float* const vslot = c->vcache + (size_t)slot * c->slot_floats;
     const cudaStream_t st = c->stream;
     const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
     const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
@@ -533,10 +557,12 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
         TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), c->pf_tok + p0, n, H, c->pf_x, st));
         for (int l = 0; l < c->L; ++l) {
             const tvb_layer_weights& lw = c->layers[l];
-            float* kl = c->kcache + (size_t)l * c->cfg.max_seq_len * Hk;
-            float* vl = c->vcache + (size_t)l * c->cfg.max_seq_len * Hk;
+            float* kl = kslot + (size_t)l * c->cfg.max_seq_len * Hk;
+            float* vl = vslot + (size_t)l * c->cfg.max_seq_len * Hk;
             size_t off = 0;
             PfGemm g;
+            g.part = c->pf_part;
+            g.part_floats = c->pf_part_floats;
             g.S = n;
             g.xh = c->pf_xh;
             g.xl = c->pf_xl;
@@ -622,6 +648,160 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S) {
     return launch_gemv<GM_LMHEAD, WT_F16, 1, true>(a, st, false);
 }
 
+// One greedy step of B sequences (tvb_decode_batch): row b is sequence b (KV
+// slot b) with token tokens[b] at position positions[b].  The layer sequence is
+// the batched prefill's with one row per sequence: the GEMMs read every weight
+// once for all B rows (split over K so the few rows keep the SMs streaming),
+// RoPE and the KV append use each row's own position and slot, and attention
+// runs per sequence over its slot.  Under tensor parallelism the row-parallel
+// partials are exchanged as in the batched prefill and every rank takes the
+// largest of the ranks' per-row argmax keys.  Leaves the B next tokens in
+// h_io[2B ..) after the stream is synchronised, the logits of this rank's
+// vocabulary slice in bd_logits [B][V / world].
+tvb_status decode_batch(tvb_context* c, const int* tokens, const int* positions, int B) {
+    const cudaStream_t st = c->stream;
+    const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
+    const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
+    const bool tp = c->tp_world > 1;
+    TpArgs tpa = {};
+    size_t reg_off[2] = {0, 0};
+    float* reg[2] = {nullptr, nullptr};
+    if (tp) {
+        tpa.world = c->tp_world;
+        tpa.rank = c->tp_rank;
+        tpa.ld = H + 4;
+        for (int r = 0; r < c->tp_world; ++r) tpa.peer[r] = c->tp_peer[r];
+        tpa.index = -1;
+        tpa.fold = -1;
+        const size_t region = tp_prefill_region_floats(c->pf_cap, H);
+        for (int j = 0; j < 2; ++j) {
+            reg_off[j] = c->tp_pf_off + j * region;
+            reg[j] = c->tp_xchg + reg_off[j];
+        }
+    }
+    auto exchange = [&](int j, const void* sub_norm, int k_local) -> tvb_status {
+        TVB_TRY(tp_sync(tpa, c->st, st));
+        return tp_reduce_rows(tpa, reg_off[j], B, H, sub_norm ? k_local * c->tp_world : 0, eps, c->pf_x, st);
+    };
+    int* d_tok = c->bd_io;
+    int* d_pos = c->bd_io + kMaxBatch;
+    int* d_next = c->bd_io + 2 * kMaxBatch;
+    for (int b = 0; b < B; ++b) {
+        c->h_io[b] = tokens[b];
+        c->h_io[B + b] = positions[b];
+    }
+    TVB_CUDA(cudaMemcpyAsync(d_tok, c->h_io, (size_t)B * 4, cudaMemcpyHostToDevice, st));
+    TVB_CUDA(cudaMemcpyAsync(d_pos, c->h_io + B, (size_t)B * 4, cudaMemcpyHostToDevice, st));
+    TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), d_tok, B, H, c->pf_x, st));
+    // attention splits: enough (kv head, split, sequence) CTAs to cover the SMs
+    const int nkv = c->cfg.num_kv_heads;
+    const int nsplit = std::max(1, std::min(kMaxAttnSplits, (num_sms() + nkv * B - 1) / (nkv * B)));
+    for (int l = 0; l < c->L; ++l) {
+        const tvb_layer_weights& lw = c->layers[l];
+        float* kl = c->kcache + (size_t)l * c->cfg.max_seq_len * Hk;   // slot 0; row b adds b slots
+        float* vl = c->vcache + (size_t)l * c->cfg.max_seq_len * Hk;
+        size_t off = 0;
+        PfGemm g;
+        g.S = B;
+        g.xh = c->pf_xh;
+        g.xl = c->pf_xl;
+        g.row_exp = c->pf_exp;
+        g.status = &c->st->status;
+        g.part = c->pf_part;
+        g.part_floats = c->pf_part_floats;
+        // attn_norm -> q, k, v -> RoPE at each row's position -> KV slot rows
+        TVB_TRY(pf_norm_split(c->pf_x, lw.attn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+        g.mode = PF_QKV;
+        g.K = H;
+        TVB_TRY(pf_operand(c, lw.wq, Hq, H, off, g.m[0]));
+        TVB_TRY(pf_operand(c, lw.wk, Hk, H, off, g.m[1]));
+        TVB_TRY(pf_operand(c, lw.wv, Hk, H, off, g.m[2]));
+        g.nh = c->cfg.num_heads;
+        g.nkv = nkv;
+        g.hd = hd;
+        g.q_out = c->pf_q;
+        g.kcache = kl;
+        g.vcache = vl;
+        g.rope_cos = c->rope_cos;
+        g.rope_sin = c->rope_sin;
+        g.row_pos = d_pos;
+        g.kv_slot_stride = c->slot_floats;
+        TVB_TRY(pf_gemm(g, st));
+        g.row_pos = nullptr;
+        TVB_TRY(batch_attention(c->pf_q, kl, vl, c->slot_floats, d_pos, B, g.nh, nkv, hd, nsplit, scale,
+                                c->bd_attn_part, c->pf_attn, st));
+        // attn_sub_norm -> o_proj -> residual
+        TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, B, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
+                              tp ? reg[0] + (size_t)B * H : nullptr));
+        off = 0;
+        g.mode = tp ? PF_STORE : PF_RESID;
+        g.K = Hq;
+        TVB_TRY(pf_operand(c, lw.wo, H, Hq, off, g.m[0]));
+        g.y = tp ? reg[0] : c->pf_x;
+        g.ldy = H;
+        TVB_TRY(pf_gemm(g, st));
+        if (tp) TVB_TRY(exchange(0, lw.attn_sub_norm, Hq));
+        // ffn_norm -> gate/up -> relu^2 * up
+        TVB_TRY(pf_norm_split(c->pf_x, lw.ffn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+        off = 0;
+        g.mode = PF_GATEUP;
+        g.K = H;
+        TVB_TRY(pf_operand(c, lw.w_gate, I, H, off, g.m[0]));
+        TVB_TRY(pf_operand(c, lw.w_up, I, H, off, g.m[1]));
+        g.y = c->pf_h;
+        g.ldy = I;
+        TVB_TRY(pf_gemm(g, st));
+        // ffn_sub_norm -> down -> residual
+        TVB_TRY(pf_norm_split(c->pf_h, lw.ffn_sub_norm, B, I, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
+                              tp ? reg[1] + (size_t)B * H : nullptr));
+        off = 0;
+        g.mode = tp ? PF_STORE : PF_RESID;
+        g.K = I;
+        TVB_TRY(pf_operand(c, lw.w_down, H, I, off, g.m[0]));
+        g.y = tp ? reg[1] : c->pf_x;
+        g.ldy = H;
+        TVB_TRY(pf_gemm(g, st));
+        if (tp) TVB_TRY(exchange(1, lw.ffn_sub_norm, I));
+    }
+    // output_norm + tied lm_head over this rank's vocabulary slice, then the
+    // per-row greedy argmax (model.cpp:1571-1580 per sequence)
+    const int vs = c->V / c->tp_world;
+    TVB_TRY(pf_norm_split(c->pf_x, c->output_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+    PfGemm g;
+    g.mode = PF_STORE;
+    g.S = B;
+    g.K = H;
+    g.xh = c->pf_xh;
+    g.xl = c->pf_xl;
+    g.row_exp = c->pf_exp;
+    g.status = &c->st->status;
+    g.part = c->pf_part;
+    g.part_floats = c->pf_part_floats;
+    g.m[0].w = static_cast<const uint16_t*>(c->tok_embd) + (size_t)c->tp_rank * vs * H;
+    g.m[0].rows = vs;
+    g.y = c->bd_logits;
+    g.ldy = vs;
+    TVB_TRY(pf_gemm(g, st));
+    KeySources src = {};
+    if (tp) {
+        // every rank publishes its B keys in its own buffer, then takes the
+        // largest over the ranks (the next step's syncs order the reuse)
+        unsigned long long* own = reinterpret_cast<unsigned long long*>(c->tp_xchg + c->tp_key_off);
+        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, c->tp_rank * vs, own, st));
+        TVB_TRY(tp_sync(tpa, c->st, st));
+        src.n = c->tp_world;
+        for (int r = 0; r < c->tp_world; ++r)
+            src.p[r] = reinterpret_cast<const unsigned long long*>(c->tp_peer[r] + c->tp_key_off);
+    } else {
+        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, 0, c->bd_keys, st));
+        src.n = 1;
+        src.p[0] = c->bd_keys;
+    }
+    TVB_TRY(batch_pick(src, B, d_next, st));
+    TVB_CUDA(cudaMemcpyAsync(c->h_io + 2 * B, d_next, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+    return TVB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -665,7 +845,9 @@ tvb_status tvb_context_create(const tvb_model_config* cfg, tvb_context** out) {
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
         return fail(cuda_error(cudaGetLastError(), "cudaStreamCreate"));
     const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, V = c->V;
-    const size_t kv = (size_t)c->L * m.max_seq_len * Hk;
+    c->slots = std::max(1, m.max_batch);
+    c->slot_floats = (size_t)c->L * m.max_seq_len * Hk;
+    const size_t kv = c->slot_floats * c->slots;
     struct { void** p; size_t b; } allocs[] = {
         {(void**)&c->d_x, H * 4ull}, {(void**)&c->d_norm, std::max(H, I) * 4ull},
         {(void**)&c->d_q, Hq * 4ull}, {(void**)&c->d_k, Hk * 4ull}, {(void**)&c->d_v, Hk * 4ull},
@@ -723,7 +905,8 @@ tvb_status tvb_context_destroy(tvb_context* c) {
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
                    c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
-                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes, c->pf_inv};
+                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes, c->pf_inv, c->pf_part, c->bd_attn_part,
+                   c->bd_logits, c->bd_io, c->bd_keys};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* pin[] = {c->h_qkv, c->h_attn, c->h_logit, c->h_st, c->h_io, c->h_hist};
@@ -747,7 +930,8 @@ tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
     const size_t decode_floats = (size_t)kTpSlots + 2ull * world * (c->H + 4);
     c->tp_pf_off = (decode_floats + 63) / 64 * 64;
     const int pf_rows = std::min(c->cfg.max_prefill, c->cfg.max_seq_len);
-    const size_t floats = c->tp_pf_off + 2 * tp_prefill_region_floats(pf_rows, c->H);
+    c->tp_key_off = c->tp_pf_off + 2 * tp_prefill_region_floats(pf_rows, c->H);
+    const size_t floats = c->tp_key_off + 2 * kMaxBatch;   // + the batched step's argmax keys (u64)
     TVB_TRY(alloc_dev((void**)&c->tp_xchg, floats * 4));
     TVB_CUDA(cudaMemset(c->tp_xchg, 0, floats * 4));
     c->tp_world = world;
@@ -806,7 +990,7 @@ tvb_status tvb_context_buffers(tvb_context* c, tvb_buffers* o) {
 
 tvb_status tvb_kv_clear(tvb_context* c) {
     TVB_REQUIRE(c, "kv_clear: null context");
-    const size_t b = (size_t)c->L * c->cfg.max_seq_len * c->Hk * 4;
+    const size_t b = c->slot_floats * c->slots * 4;   // every slot
     TVB_CUDA(cudaMemsetAsync(c->kcache, 0, b, c->stream));
     TVB_CUDA(cudaMemsetAsync(c->vcache, 0, b, c->stream));
     return TVB_OK;
@@ -943,7 +1127,13 @@ tvb_status tvb_decode_enqueue(tvb_context* c, int token, int pos, int n_steps) {
 }
 
 tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_logits, int* argmax_host) {
+    return tvb_prefill_slot(c, 0, tokens, S, last_logits, argmax_host);
+}
+
+tvb_status tvb_prefill_slot(tvb_context* c, int slot, const int* tokens, int S, float* last_logits,
+                            int* argmax_host) {
     TVB_REQUIRE(c && tokens, "prefill: null argument");
+    TVB_REQUIRE(slot >= 0 && slot < c->slots, "prefill: slot %d of %d", slot, c->slots);
     TVB_REQUIRE(S > 0 && S <= c->cfg.max_seq_len, "prefill: S=%d outside (0, %d]", S, c->cfg.max_seq_len);
     for (int i = 0; i < S; ++i)
         TVB_REQUIRE(tokens[i] >= 0 && tokens[i] < c->V, "prefill: token[%d]=%d outside vocab", i, tokens[i]);
@@ -951,6 +1141,7 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
     // the pinned staging is about to be rewritten: let earlier copies from it finish
     TVB_CUDA(cudaStreamSynchronize(c->stream));
     if (!pf_batched_supported(c)) {
+        TVB_REQUIRE(slot == 0, "prefill: KV slots other than 0 need the batched (tensor-core) prefill");
         // shapes the tensor-core kernels do not tile: one decode-step launch
         // per prompt row; row s attends to KV rows [0, s] as in
         // forward_prefill (model.cpp:1084 kv_len = s + 1)
@@ -961,7 +1152,7 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
             TVB_CUDA(cudaGraphLaunch(s + 1 < S ? c->g_layers : c->g_step, c->stream));
         }
     } else {
-        TVB_TRY(prefill_batched(c, tokens, S));
+        TVB_TRY(prefill_batched(c, tokens, S, slot));
     }
     TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
     const size_t nl = (size_t)(c->V / c->tp_world);   // this rank's logits
@@ -971,6 +1162,31 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
     TVB_TRY(check_status(c));
     if (last_logits) std::memcpy(last_logits, c->h_logit, nl * 4);
     if (argmax_host) *argmax_host = c->h_st->next_token;
+    return TVB_OK;
+}
+
+tvb_status tvb_decode_batch(tvb_context* c, const int* tokens, const int* positions, int B, float* logits,
+                            int* next_tokens) {
+    TVB_REQUIRE(c && tokens && positions && next_tokens, "decode_batch: null argument");
+    TVB_REQUIRE(B >= 1 && B <= c->slots && B <= kMaxBatch && 3 * B <= 2 * c->cfg.max_seq_len,
+                "decode_batch: B=%d (context slots %d, at most %d)", B, c->slots, kMaxBatch);
+    for (int b = 0; b < B; ++b) {
+        TVB_REQUIRE(tokens[b] >= 0 && tokens[b] < c->V, "decode_batch: token[%d]=%d outside vocab", b, tokens[b]);
+        TVB_REQUIRE(positions[b] >= 0 && positions[b] < c->cfg.max_seq_len,
+                    "decode_batch: position[%d]=%d outside [0, %d)", b, positions[b], c->cfg.max_seq_len);
+    }
+    TVB_REQUIRE(pf_batched_supported(c), "decode_batch: shapes the tensor-core GEMM does not tile");
+    if (c->tp_world > 1) TVB_REQUIRE(c->tp_ready, "decode_batch: peers not set (tvb_tp_set_peers)");
+    TVB_TRY(pf_workspace(c));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));   // the pinned staging is reused
+    TVB_TRY(decode_batch(c, tokens, positions, B));
+    const int vs = c->V / c->tp_world;
+    if (logits)
+        TVB_CUDA(cudaMemcpyAsync(logits, c->bd_logits, (size_t)B * vs * 4, cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_TRY(check_status(c));
+    for (int b = 0; b < B; ++b) next_tokens[b] = c->h_io[2 * B + b];
     return TVB_OK;
 }
 

@@ -64,8 +64,18 @@ struct PfArgs {
     float* vcache;
     const float* rope_cos;
     const float* rope_sin;
+    const int* row_pos;      // per-row positions (rows are sequences), or nullptr
+    size_t kv_slot_stride;   // per-row KV cache offset when row_pos is given
     unsigned* status;
+    float* part;             // split-K: raw partials [ksplit][S][width]
+    int ksplit, width;       // width = tiles * 128 * NH
 };
+
+// Position of activation row s, and the offset of its KV cache slot.
+__device__ __forceinline__ int pf_pos(const PfArgs& a, int s) { return a.row_pos ? __ldg(a.row_pos + s) : a.pos0 + s; }
+__device__ __forceinline__ size_t pf_slot(const PfArgs& a, int s) {
+    return a.row_pos ? (size_t)s * a.kv_slot_stride : 0;
+}
 
 // Which matrix and first row feed half `h` (128 rows) of column tile `tile`
 // (NH halves per tile).
@@ -139,7 +149,9 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, s0 = blockIdx.y * kPfBM;
-    const int nkb = a.nk;
+    // split-K: this CTA's k-blocks [kb0, kb0 + nkb)
+    const int kb0 = (int)((long long)a.nk * blockIdx.z / gridDim.z);
+    const int nkb = (int)((long long)a.nk * (blockIdx.z + 1) / gridDim.z) - kb0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kPfStages; ++i) {
@@ -176,7 +188,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
             (uint32_t)(kPfPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
         int i = 0;
         for (; i < nkb; ++i) {
-            const int s = i % kPfStages, r = i / kPfStages, kx = i * kPfBK;
+            const int s = i % kPfStages, r = i / kPfStages, kx = (kb0 + i) * kPfBK;
             if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
                 pf_fail(a, abort_flag);
                 break;
@@ -231,7 +243,18 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
             const float e2 = (srow && a.row_exp) ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
             uint32_t r0[32], r1[32];
             float v0[32], v1[32];
-            if (a.mode == PF_GATEUP) {
+            if (gridDim.z > 1) {
+                // split-K: raw sums of this k range; pf_splitk_epilogue finishes
+                float* dst = a.part + ((size_t)blockIdx.z * a.S + s) * a.width + (size_t)tile * 128 * NH;
+                for (int c = 0; c < 4 * NH; ++c) {
+                    __syncwarp();
+                    fetch(c * 32, r0);
+                    if (!srow) continue;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v0[j] = __uint_as_float(r0[j]);
+                    pf_store32(dst + c * 32, v0, 32, false);
+                }
+            } else if (a.mode == PF_GATEUP) {
                 // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
                 for (int c = 0; c < 4; ++c) {
                     __syncwarp();
@@ -259,7 +282,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                         fetch(h * 128 + c * 32, r0);
                         fetch(h * 128 + half + c * 32, r1);
                         if (!(srow && hv[h])) continue;
-                        const int pos = a.pos0 + s;
+                        const int pos = pf_pos(a, s);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int d = c * 32 + j;
@@ -281,7 +304,8 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                         float* dst;
                         if (mi[h] == 0) dst = a.q_out + (size_t)s * a.nh * a.hd + head * a.hd;
                         else
-                            dst = (mi[h] == 1 ? a.kcache : a.vcache) + (size_t)pos * a.nkv * a.hd + head * a.hd;
+                            dst = (mi[h] == 1 ? a.kcache : a.vcache) + pf_slot(a, s) + (size_t)pos * a.nkv * a.hd +
+                                  head * a.hd;
                         pf_store32(dst + c * 32, v0, 32, false);
                         pf_store32(dst + half + c * 32, v1, 32, false);
                     }
@@ -317,6 +341,62 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols)
                      : "memory");
+    }
+}
+
+// Split-K completion: one thread per (row, output element or RoPE/gate-up
+// pair): the ksplit partial sums added in split order, then the epilogue of
+// pf_gemm_kernel (same arithmetic after the sum).
+template <int NH>
+__global__ void pf_splitk_epilogue(const __grid_constant__ PfArgs a) {
+    const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (idx >= (size_t)a.S * a.width) return;
+    const int s = (int)(idx / a.width), v = (int)(idx % a.width);
+    const int tile = v / (128 * NH), h = (v / 128) % NH, c = v % 128;
+    int mi, row;
+    if (!pf_half(a, NH, tile, h, mi, row)) return;
+    const size_t plane = (size_t)a.S * a.width;
+    auto sum = [&](int col) {
+        const float* p = a.part + (size_t)s * a.width + col;
+        float t = 0.f;
+        for (int z = 0; z < a.ksplit; ++z) t += p[z * plane];
+        return t;
+    };
+    const float e2 = a.row_exp ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
+    if (a.mode == PF_GATEUP) {
+        // the gate half (h 0) finishes the pair with its up half (h 1)
+        const int n = row + c;
+        if (h != 0 || n >= a.rows[0]) return;
+        const float g = __fmul_rn(sum(v) * e2, pf_row_scale(a, 0, n));
+        const float u = __fmul_rn(sum(v + 128) * e2, pf_row_scale(a, 1, n));
+        const float gr = fmaxf(g, 0.0f);
+        a.y[(size_t)s * a.ldy + n] = __fmul_rn(__fmul_rn(gr, gr), u);
+    } else if (a.mode == PF_QKV) {
+        const int half = a.hd >> 1;
+        if (c >= half) return;
+        const int head = row / a.hd, pos = pf_pos(a, s);
+        float y0 = __fmul_rn(sum(v) * e2, pf_row_scale(a, mi, row + c));
+        float y1 = __fmul_rn(sum(v + half) * e2, pf_row_scale(a, mi, row + c + half));
+        if (mi < 2) {
+            // NeoX pair (d, d + hd/2), tensor.cpp:918-925
+            const float cs = __ldg(a.rope_cos + (size_t)pos * half + c);
+            const float sn = __ldg(a.rope_sin + (size_t)pos * half + c);
+            const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+            const float t1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+            y0 = t0;
+            y1 = t1;
+        }
+        float* dst = mi == 0 ? a.q_out + (size_t)s * a.nh * a.hd + head * a.hd
+                             : (mi == 1 ? a.kcache : a.vcache) + pf_slot(a, s) + (size_t)pos * a.nkv * a.hd +
+                                   head * a.hd;
+        dst[c] = y0;
+        dst[c + half] = y1;
+    } else {
+        const int n = row + c;
+        if (n >= a.rows[0]) return;
+        const float val = __fmul_rn(sum(v) * e2, pf_row_scale(a, 0, n));
+        float* y = a.y + (size_t)s * a.ldy + n;
+        *y = a.mode == PF_RESID ? __fadd_rn(*y, val) : val;
     }
 }
 
@@ -413,6 +493,8 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
     a.vcache = g.vcache;
     a.rope_cos = g.rope_cos;
     a.rope_sin = g.rope_sin;
+    a.row_pos = g.row_pos;
+    a.kv_slot_stride = g.kv_slot_stride;
     a.status = g.status;
     TVB_TRY(encode_f16(&maps.xh, g.xh, g.S, g.K));
     if (g.xl) TVB_TRY(encode_f16(&maps.xl, g.xl, g.S, g.K));
@@ -453,10 +535,27 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
             tiles = halves;
         }
     }
-    const dim3 grid((unsigned)tiles, (unsigned)mtiles);
+    // split-K when the tiles leave most SMs idle (few activation rows): each
+    // split keeps at least 8 k-blocks for its TMA/MMA pipeline
+    int ksplit = 1;
+    if (g.part) {
+        const int sms = num_sms();
+        ksplit = std::max(1, std::min(sms / (tiles * mtiles), a.nk / 8));
+        a.width = tiles * 128 * nh;
+        while (ksplit > 1 && (size_t)ksplit * g.S * a.width > g.part_floats) --ksplit;
+        a.part = g.part;
+        a.ksplit = ksplit;
+    }
+    const dim3 grid((unsigned)tiles, (unsigned)mtiles, (unsigned)ksplit);
     if (nh == 2) pf_gemm_kernel<2><<<grid, kPfThreads, pf_smem_bytes(2), stream>>>(maps, a);
     else pf_gemm_kernel<1><<<grid, kPfThreads, pf_smem_bytes(1), stream>>>(maps, a);
-    return check_launch("pf_gemm_kernel");
+    TVB_TRY(check_launch("pf_gemm_kernel"));
+    if (ksplit == 1) return TVB_OK;
+    const size_t n = (size_t)g.S * a.width;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (nh == 2) pf_splitk_epilogue<2><<<blocks, 256, 0, stream>>>(a);
+    else pf_splitk_epilogue<1><<<blocks, 256, 0, stream>>>(a);
+    return check_launch("pf_splitk_epilogue");
 }
 
 // ---------------------------------------------------------------------------

@@ -46,7 +46,17 @@ struct PfGemm {
     float* vcache = nullptr;
     const float* rope_cos = nullptr;   // [max_seq][hd / 2]
     const float* rope_sin = nullptr;
+    // rows that are different sequences (batched decode): row s is at position
+    // row_pos[s] and writes its K/V rows kv_slot_stride floats further per row
+    const int* row_pos = nullptr;
+    size_t kv_slot_stride = 0;
     unsigned* status = nullptr;     // device word; kStatusTimeout on a pipeline stall
+    // split-K workspace: with few activation rows the weight tiles alone do not
+    // keep the SMs busy, so the K range is cut over CTAs that store raw partial
+    // sums here and a second kernel adds them (in split order) and applies the
+    // epilogue; nullptr or too small: no split
+    float* part = nullptr;
+    size_t part_floats = 0;
 };
 
 

@@ -8,6 +8,7 @@ decode-step kernel.  Checked: every rank produces the same tokens; the ranks'
 vocabulary slices of the logits, put together, match the single-GPU decode
 steps over the same tokens within 2e-3 relative; the tokens are the argmax of
 those single-GPU logits.  Skipped on machines with fewer GPUs than ranks."""
+import dataclasses
 import socket
 
 import numpy as np
@@ -73,7 +74,67 @@ def _child(rank, world, port, cfg, prompt, n_new, q):
         dist.destroy_process_group()
 
 
-def _run(world, cfg, prompt, n_new):
+def _child_batch(rank, world, port, cfg, prompts, steps, q):
+    """Batched decode under tensor parallelism: every prompt prefilled into
+    its KV slot, then `steps` batched greedy steps; rank 0 checks each
+    sequence against the single-GPU single-sequence path (teacher-forced)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        from ternative_b200.model import Model, SyntheticModel
+        from ternative_b200.tp import TPModel
+
+        def all_gather(obj):
+            out = [None] * world
+            dist.all_gather_object(out, obj)
+            return out
+
+        synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=4)
+        m = TPModel(synth, world, rank, all_gather)
+        be = m.backend
+        be.clear_kv_d()
+        toks = []
+        for b, p in enumerate(prompts):
+            _, am = be.prefill_slot(b, p, want_logits=False)
+            toks.append([int(t) for t in p] + [am])
+        logits = []
+        for _ in range(steps):
+            cur = np.array([t[-1] for t in toks], np.int32)
+            pos = np.array([len(t) - 1 for t in toks], np.int32)
+            lg, nxt = be.decode_batch(cur, pos)
+            for b in range(len(prompts)):
+                toks[b].append(int(nxt[b]))
+            logits.append(lg)
+        parts = all_gather(np.stack(logits))           # [steps][B][V / world] per rank
+        res = {"rank": rank, "toks": toks}
+        if rank == 0:
+            full = np.concatenate(parts, axis=2)         # [steps][B][V]
+            ref = Model.load(SyntheticModel.generate(dataclasses.replace(cfg, max_batch=1), rank=16,
+                                                     alpha=32.0, seed=4))
+            errs = []
+            for b, p in enumerate(prompts):
+                ref.backend.clear_kv_d()
+                ref.backend.prefill(p, want_logits=False)
+                for i in range(steps):
+                    lg, _ = ref.backend.decode_step(toks[b][len(p) + i], len(p) + i)
+                    errs.append(float(np.abs(full[i][b].astype(np.float64) - lg).max() / np.abs(lg).max()))
+                    assert int(np.argmax(full[i][b])) == toks[b][len(p) + i + 1]
+            res["errs"] = errs
+            ref.backend.close()
+        dist.barrier()
+        m.close()
+        q.put(res)
+    except Exception as e:   # report, do not hang the parent
+        q.put({"rank": rank, "error": repr(e)})
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(world, cfg, prompt, n_new, child=None, args=None):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -81,7 +142,7 @@ def _run(world, cfg, prompt, n_new):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_child, args=(r, world, port, cfg, prompt, n_new, q))
+    procs = [ctx.Process(target=child or _child, args=(r, world, port, cfg) + (args or (prompt, n_new)) + (q,))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -118,3 +179,18 @@ def test_tp_decode_matches_single_gpu(world, prompt_len, max_prefill):
         err = float(np.abs(full[i].astype(np.float64) - ref[i]).max() / np.abs(ref[i]).max())
         assert err < RTOL, (i, err)
         assert int(np.argmax(ref[i])) == toks[len(prompt) + i]
+
+
+def test_tp_batch_decode_matches_single_gpu():
+    """Three sequences decoded together on 2 ranks (row-parallel partials of all
+    rows exchanged per projection, per-row argmax keys exchanged) against the
+    single-GPU single-sequence path."""
+    from ternative_b200.backend import Config
+    cfg = Config(vocab_size=4096, hidden_size=512, num_layers=3, num_heads=8, num_kv_heads=4,
+                 head_dim=128, intermediate_size=2048, max_seq_len=256, max_prefill=256, max_batch=3)
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, cfg.vocab_size, n).astype(np.int32) for n in (6, 19, 44)]
+    res = _run(2, cfg, None, None, child=_child_batch, args=(prompts, 5))
+    for r in range(2):
+        assert res[r]["toks"] == res[0]["toks"]
+    assert max(res[0]["errs"]) < RTOL, res[0]["errs"]
