@@ -335,6 +335,46 @@ tvb_status tvb_prefill_slot(tvb_context* ctx, int slot, const int* tokens_host, 
 tvb_status tvb_decode_batch(tvb_context* ctx, const int* tokens_host, const int* positions_host, int B,
                             float* logits_host, int* next_tokens_host);
 
+/* ---- merged-weight cache (.tvcache) ---------------------------------------
+ * ModelCache::save / ModelCache::try_load (src/cache.cpp:263-470, format
+ * include/ternative/cache.h:28-62), fed from and into device memory: the merge
+ * output is written without a host copy of the model, and a cached model is
+ * uploaded chunk by chunk.  Files without INT8 tensors are byte-identical to
+ * the reference's (version 1); per-row INT8 weights (ggml type 24 plus an F32
+ * "<name>.row_scale" entry) make a version-2 file, which the reference's
+ * reader refuses.  Pointers may be host or device memory. */
+typedef struct {
+    uint64_t base_size;        /* the reference writes 0 */
+    uint8_t base_sha256[32];   /* SHA-256 of the base GGUF (ModelCache::compute_key) */
+    uint64_t lora_size;        /* the reference writes 0 */
+    uint8_t lora_sha256[32];   /* zeros without LoRA */
+    float lora_alpha;
+    uint32_t lora_rank;
+} tvb_cache_key;
+
+typedef struct {
+    const char* name;          /* "tok_embd", "output_norm", "blk.<l>.attn_q", ... */
+    int ggml_type;             /* 0 F32, 1 F16, 24 I8 (per-row INT8 codes) */
+    int n_dims;                /* 1..4 */
+    int64_t shape[4];          /* ggml order: shape[0] = ne0 (the row length) */
+    const void* data;
+    const float* row_scales;   /* I8: shape[1] F32 scales */
+} tvb_cache_tensor;
+
+typedef struct tvb_cache tvb_cache;
+
+/* Writes `path` (via <path>.tmp and a rename, as ModelCache::save). */
+tvb_status tvb_cache_write(const char* path, const tvb_cache_key* key, const tvb_cache_tensor* tensors, int n);
+/* Opens a cache file and reads its header and tensor table. */
+tvb_status tvb_cache_open(const char* path, tvb_cache** out);
+int        tvb_cache_count(const tvb_cache* cache);
+tvb_status tvb_cache_info(const tvb_cache* cache, tvb_cache_key* key, int* version);
+/* Entry i: name (valid while open), type, dims, shape; data pointers unset. */
+tvb_status tvb_cache_entry(const tvb_cache* cache, int i, tvb_cache_tensor* info, uint64_t* nbytes);
+/* Reads tensor `name` into dst (capacity bytes, host or device). */
+tvb_status tvb_cache_read(tvb_cache* cache, const char* name, void* dst, uint64_t capacity);
+tvb_status tvb_cache_close(tvb_cache* cache);
+
 #ifdef __cplusplus
 }
 #endif

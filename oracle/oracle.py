@@ -194,6 +194,11 @@ class Reference:
         L.tvref_kv_set_seq_len.argtypes = [C.c_void_p, C.c_int]
         L.tvref_omp_threads.restype = C.c_int
         L.tvref_omp_threads.argtypes = []
+        L.tvref_cache_save.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_float, C.c_int]
+        L.tvref_cache_load.argtypes = [C.c_void_p, C.c_char_p]
+        L.tvref_model_get.restype = C.c_longlong
+        L.tvref_model_get.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.tvref_model_lora.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int)]
         L.tvref_time_decode.restype = C.c_double
         L.tvref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         self.L = L
@@ -319,7 +324,7 @@ class ReferenceModel:
     LAYER_KEYS = ["attn_norm", "wq", "wk", "wv", "wo", "attn_sub_norm", "ffn_norm",
                   "w_gate", "w_up", "w_down", "ffn_sub_norm"]
 
-    def __init__(self, ref: Reference, shape: ModelShape, weights: dict):
+    def __init__(self, ref: Reference, shape: ModelShape, weights: dict = None):
         self.ref = ref
         self.shape = shape
         L = ref.L
@@ -327,6 +332,8 @@ class ReferenceModel:
                                       shape.kv_heads, shape.inter, shape.max_seq,
                                       shape.rope_theta, shape.eps)
         self._keep = []
+        if weights is None:   # an empty model (e.g. to load a .tvcache into)
+            return
 
         def put(which, layer, arr):
             arr = np.ascontiguousarray(arr)
@@ -340,6 +347,30 @@ class ReferenceModel:
             lw = weights["layers"][li]
             for j, key in enumerate(self.LAYER_KEYS):
                 put(2 + j, li, lw[key])
+
+    # ---- the reference's .tvcache (cache.cpp:263-470) ------------------------------
+    def cache_save(self, path: str, base_hex: str = "", lora_hex: str = "", alpha: float = 0.0,
+                   rank: int = 0):
+        """ModelCache::save of this model's tensors."""
+        self.ref.L.tvref_cache_save(self.h, path.encode(), base_hex.encode(), lora_hex.encode(), alpha, rank)
+
+    def cache_load(self, path: str) -> bool:
+        """ModelCache::try_load into this model."""
+        return self.ref.L.tvref_cache_load(self.h, path.encode()) == 1
+
+    def get(self, which: int, layer: int = -1):
+        """Raw bytes of a tensor (numbering of tvref_model_set), or None if empty."""
+        n = self.ref.L.tvref_model_get(self.h, which, layer, None)
+        if n < 0:
+            return None
+        out = np.empty(n, np.uint8)
+        self.ref.L.tvref_model_get(self.h, which, layer, out.ctypes.data)
+        return out
+
+    def lora(self):
+        a, r = C.c_float(), C.c_int()
+        self.ref.L.tvref_model_lora(self.h, C.byref(a), C.byref(r))
+        return a.value, r.value
 
     def forward_prefill(self, tokens):
         tokens = _c(tokens, np.int32)

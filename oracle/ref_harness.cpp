@@ -265,6 +265,47 @@ int tvref_forward(tvref_model* h, int token, int pos, int prefill, float* logits
 
 void tvref_kv_set_seq_len(tvref_model* h, int n) { h->m.kv_cache.seq_len = n; }
 
+// cache.cpp:263-375 -- ModelCache::save of this model's tensors; the key's
+// SHA-256 fields as hex strings ("" = none), as compute_key returns them.
+int tvref_cache_save(tvref_model* h, const char* path, const char* base_hex, const char* lora_hex, float alpha,
+                     int rank) {
+    CacheKey key;
+    key.base_sha256_hex = base_hex ? base_hex : "";
+    key.lora_sha256_hex = lora_hex ? lora_hex : "";
+    key.lora_alpha = alpha;
+    key.lora_rank = (uint32_t)rank;
+    h->m.lora_alpha = alpha;
+    h->m.lora_rank = rank;
+    ModelCache::save(h->m, path, key);
+    return 0;
+}
+
+// cache.cpp:378-470 -- ModelCache::try_load into this model: 1 loaded, 0 refused.
+int tvref_cache_load(tvref_model* h, const char* path) { return ModelCache::try_load(h->m, path) ? 1 : 0; }
+
+// Tensor `which` (the numbering of tvref_model_set) copied to out when out is
+// not null; returns its byte count, -1 when the tensor is empty.
+long long tvref_model_get(tvref_model* h, int which, int layer, void* out) {
+    Model& m = h->m;
+    const Tensor* t = nullptr;
+    if (which == 0) t = &m.tok_embd;
+    else if (which == 1) t = &m.output_norm;
+    else if (layer >= 0 && layer < (int)m.layers.size()) {
+        const LayerWeights& w = m.layers[layer];
+        const Tensor* per[] = {&w.attn_norm, &w.wq, &w.wk, &w.wv, &w.wo, &w.attn_sub_norm,
+                               &w.ffn_norm, &w.w_gate, &w.w_up, &w.w_down, &w.ffn_sub_norm};
+        if (which >= 2 && which <= 12) t = per[which - 2];
+    }
+    if (!t || t->data.empty()) return -1;
+    if (out) std::memcpy(out, t->data.data(), t->data.size());
+    return (long long)t->data.size();
+}
+
+void tvref_model_lora(tvref_model* h, float* alpha, int* rank) {
+    *alpha = h->m.lora_alpha;
+    *rank = h->m.lora_rank;
+}
+
 // Copy one layer's CPU KV cache rows [0, n) (layout [pos][n_kv][hd], F32).
 int tvref_kv_read(tvref_model* h, int layer, int n, float* k, float* v) {
     const auto& c = h->m.config;

@@ -64,6 +64,16 @@ class LayerWeights(C.Structure):
                 ("w_down", Weight)]
 
 
+class CacheKey(C.Structure):
+    _fields_ = [("base_size", C.c_uint64), ("base_sha256", C.c_ubyte * 32), ("lora_size", C.c_uint64),
+                ("lora_sha256", C.c_ubyte * 32), ("lora_alpha", C.c_float), ("lora_rank", C.c_uint32)]
+
+
+class CacheTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("ggml_type", C.c_int), ("n_dims", C.c_int),
+                ("shape", C.c_int64 * 4), ("data", C.c_void_p), ("row_scales", C.c_void_p)]
+
+
 class IpcHandle(C.Structure):
     _fields_ = [("bytes", C.c_ubyte * 64)]
 
@@ -117,6 +127,13 @@ _SIGS = {
     "tvb_decode_enqueue": [_P, _I, _I, _I],
     "tvb_prefill": [_P, _P, _I, _P, _P],
     "tvb_prefill_slot": [_P, _I, _P, _I, _P, _P],
+    "tvb_cache_write": [C.c_char_p, _P, _P, _I],
+    "tvb_cache_open": [C.c_char_p, _P],
+    "tvb_cache_count": [_P],
+    "tvb_cache_info": [_P, _P, _P],
+    "tvb_cache_entry": [_P, _I, _P, _P],
+    "tvb_cache_read": [_P, C.c_char_p, _P, C.c_uint64],
+    "tvb_cache_close": [_P],
     "tvb_decode_batch": [_P, _P, _P, _I, _P, _P],
     "tvb_tp_init": [_P, _I, _I, C.POINTER(C.c_void_p)],
     "tvb_tp_set_peers": [_P, C.POINTER(C.c_void_p)],
@@ -130,6 +147,7 @@ _RESTYPES = {
     "tvb_last_error": C.c_char_p,
     "tvb_context_stream": C.c_void_p,
     "tvb_kv_capacity": C.c_int,
+    "tvb_cache_count": C.c_int,
 }
 
 EXPORTED = tuple(_SIGS)

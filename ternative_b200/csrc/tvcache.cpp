@@ -1,0 +1,343 @@
+// The merged-weight cache file (.tvcache) written straight from device memory
+// and read back into it.
+//
+// File layout (the reference's ModelCache format, include/ternative/cache.h:
+// 28-62, writer src/cache.cpp:263-375, reader :378-470), kept byte-for-byte so
+// either side reads the other's files:
+//
+//   [0, 256)          header: "TVCACHE\0", version, dtype, key (SHA-256 of the
+//                     base and LoRA GGUF files, LoRA alpha and rank), tensor
+//                     count, table offset (256), data offset, file size
+//   [256, ...)        one 192-byte entry per tensor: name, ggml type, dims,
+//                     shape (ggml order), offset in the data section, bytes
+//   [data, ...)       tensor bytes, each tensor starting on a 64-byte boundary;
+//                     the data section starts on a 4096-byte boundary
+//
+// Extension: per-row INT8 weights (the codes as ggml type 24, I8, plus an F32
+// entry "<name>.row_scale") are written as version 2, which the reference's
+// reader refuses instead of misreading; files without them are version 1.
+//
+// Device tensors are staged through two pinned buffers: the copy of chunk
+// i + 1 runs while chunk i is written to (or read from) the file.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace {
+
+#pragma pack(push, 1)
+struct FileHeader {
+    char magic[8];
+    uint32_t version;
+    uint32_t dtype;
+    uint64_t base_size;
+    uint8_t base_sha256[32];
+    uint64_t lora_size;
+    uint8_t lora_sha256[32];
+    float lora_alpha;
+    uint32_t lora_rank;
+    uint32_t num_tensors;
+    uint64_t table_offset;
+    uint64_t data_offset;
+    uint64_t total_size;
+    uint8_t reserved[124];
+};
+struct FileTensor {
+    char name[128];
+    uint32_t dtype;
+    uint32_t n_dims;
+    uint64_t shape[4];
+    uint64_t data_offset;
+    uint64_t nbytes;
+    uint8_t pad[8];
+};
+#pragma pack(pop)
+static_assert(sizeof(FileHeader) == 256, "header is 256 bytes");
+static_assert(sizeof(FileTensor) == 192, "table entry is 192 bytes");
+
+constexpr uint32_t kTypeF32 = 0, kTypeF16 = 1, kTypeI8 = 24;
+constexpr size_t kChunk = 32u << 20;   // staging chunk
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+// Whether p is device memory the runtime knows (host memory, or no GPU, is not).
+bool on_device(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+// Two pinned staging buffers and a stream for device <-> file transfers.
+struct Staging {
+    void* buf[2] = {nullptr, nullptr};
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    tvb_status init() {
+        if (st) return TVB_OK;
+        for (int i = 0; i < 2; ++i) {
+            TVB_CUDA(cudaHostAlloc(&buf[i], kChunk, cudaHostAllocDefault));
+            TVB_CUDA(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+        }
+        TVB_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        return TVB_OK;
+    }
+    ~Staging() {
+        if (st) cudaStreamSynchronize(st);
+        for (int i = 0; i < 2; ++i) {
+            if (buf[i]) cudaFreeHost(buf[i]);
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        }
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+struct File {
+    FILE* f = nullptr;
+    ~File() {
+        if (f) fclose(f);
+    }
+};
+
+tvb_status write_bytes(FILE* f, const void* p, size_t n, const char* what) {
+    if (n && fwrite(p, 1, n, f) != n) return tvb::set_error(TVB_ERR_INVALID, "tvcache: short write (%s)", what);
+    return TVB_OK;
+}
+
+// One tensor's bytes to the file, from host memory or through the staging.
+tvb_status write_tensor(FILE* f, const void* src, size_t n, Staging& sg) {
+    if (!on_device(src)) return write_bytes(f, src, n, "tensor data");
+    TVB_TRY(sg.init());
+    const char* s = static_cast<const char*>(src);
+    size_t done = 0;
+    int cur = 0;
+    size_t len = n < kChunk ? n : kChunk;
+    TVB_CUDA(cudaMemcpyAsync(sg.buf[cur], s, len, cudaMemcpyDeviceToHost, sg.st));
+    TVB_CUDA(cudaEventRecord(sg.ev[cur], sg.st));
+    while (done < n) {
+        const size_t next = done + len;
+        size_t nlen = 0;
+        if (next < n) {   // the next chunk's copy overlaps this chunk's write
+            nlen = n - next < kChunk ? n - next : kChunk;
+            TVB_CUDA(cudaMemcpyAsync(sg.buf[cur ^ 1], s + next, nlen, cudaMemcpyDeviceToHost, sg.st));
+            TVB_CUDA(cudaEventRecord(sg.ev[cur ^ 1], sg.st));
+        }
+        TVB_CUDA(cudaEventSynchronize(sg.ev[cur]));
+        TVB_TRY(write_bytes(f, sg.buf[cur], len, "tensor data"));
+        done = next;
+        len = nlen;
+        cur ^= 1;
+    }
+    return TVB_OK;
+}
+
+}  // namespace
+
+struct tvb_cache {
+    File file;
+    FileHeader hdr;
+    std::vector<FileTensor> table;
+    std::string path;
+};
+
+extern "C" {
+
+tvb_status tvb_cache_write(const char* path, const tvb_cache_key* key, const tvb_cache_tensor* tensors, int n) {
+    TVB_REQUIRE(path && key && (tensors || n == 0) && n >= 0, "cache_write: bad arguments");
+    // table: every tensor, and a row-scale entry after each per-row INT8 one
+    std::vector<FileTensor> table;
+    std::vector<const void*> src;
+    bool int8 = false;
+    uint64_t off = 0;
+    auto add = [&](const char* name, uint32_t type, int n_dims, const int64_t* shape, uint64_t nbytes,
+                   const void* data) -> tvb_status {
+        FileTensor e;
+        std::memset(&e, 0, sizeof(e));
+        TVB_REQUIRE(std::strlen(name) < sizeof(e.name), "cache_write: tensor name '%s' too long", name);
+        std::strncpy(e.name, name, sizeof(e.name) - 1);
+        e.dtype = type;
+        e.n_dims = (uint32_t)n_dims;
+        for (int d = 0; d < n_dims; ++d) e.shape[d] = (uint64_t)shape[d];
+        e.data_offset = off;
+        e.nbytes = nbytes;
+        off = align_up(off + nbytes, 64);
+        table.push_back(e);
+        src.push_back(data);
+        return TVB_OK;
+    };
+    for (int i = 0; i < n; ++i) {
+        const tvb_cache_tensor& t = tensors[i];
+        TVB_REQUIRE(t.name && t.n_dims >= 1 && t.n_dims <= 4 && t.data, "cache_write: tensor %d incomplete", i);
+        uint64_t count = 1;
+        for (int d = 0; d < t.n_dims; ++d) {
+            TVB_REQUIRE(t.shape[d] > 0, "cache_write: tensor '%s' dim %d is %lld", t.name, d, (long long)t.shape[d]);
+            count *= (uint64_t)t.shape[d];
+        }
+        if (t.ggml_type == (int)kTypeI8) {
+            TVB_REQUIRE(t.n_dims == 2 && t.row_scales, "cache_write: INT8 tensor '%s' needs 2 dims and row scales",
+                        t.name);
+            TVB_TRY(add(t.name, kTypeI8, 2, t.shape, count, t.data));
+            const std::string sname = std::string(t.name) + ".row_scale";
+            const int64_t rows[1] = {t.shape[1]};
+            TVB_TRY(add(sname.c_str(), kTypeF32, 1, rows, (uint64_t)t.shape[1] * 4, t.row_scales));
+            int8 = true;
+        } else {
+            TVB_REQUIRE(t.ggml_type == (int)kTypeF16 || t.ggml_type == (int)kTypeF32,
+                        "cache_write: tensor '%s' type %d (F32, F16 or I8)", t.name, t.ggml_type);
+            TVB_TRY(add(t.name, (uint32_t)t.ggml_type, t.n_dims, t.shape,
+                        count * (t.ggml_type == (int)kTypeF16 ? 2 : 4), t.data));
+        }
+    }
+    FileHeader h;
+    std::memset(&h, 0, sizeof(h));
+    std::memcpy(h.magic, "TVCACHE\0", 8);
+    h.version = int8 ? 2u : 1u;
+    h.dtype = int8 ? 2u : 1u;
+    h.base_size = key->base_size;
+    std::memcpy(h.base_sha256, key->base_sha256, 32);
+    h.lora_size = key->lora_size;
+    std::memcpy(h.lora_sha256, key->lora_sha256, 32);
+    h.lora_alpha = key->lora_alpha;
+    h.lora_rank = key->lora_rank;
+    h.num_tensors = (uint32_t)table.size();
+    h.table_offset = sizeof(FileHeader);
+    h.data_offset = align_up(sizeof(FileHeader) + table.size() * sizeof(FileTensor), 4096);
+    h.total_size = h.data_offset + off;
+
+    // written to <path>.tmp, renamed over <path> once complete
+    const std::string tmp = std::string(path) + ".tmp";
+    Staging sg;
+    {
+        File f;
+        f.f = std::fopen(tmp.c_str(), "wb");
+        TVB_REQUIRE(f.f, "cache_write: cannot create %s", tmp.c_str());
+        TVB_TRY(write_bytes(f.f, &h, sizeof(h), "header"));
+        TVB_TRY(write_bytes(f.f, table.data(), table.size() * sizeof(FileTensor), "table"));
+        static const char zeros[4096] = {};
+        TVB_TRY(write_bytes(f.f, zeros, h.data_offset - sizeof(h) - table.size() * sizeof(FileTensor), "padding"));
+        for (size_t i = 0; i < table.size(); ++i) {
+            TVB_TRY(write_tensor(f.f, src[i], table[i].nbytes, sg));
+            TVB_TRY(write_bytes(f.f, zeros, align_up(table[i].nbytes, 64) - table[i].nbytes, "padding"));
+        }
+        const bool ok = std::fflush(f.f) == 0;
+        std::fclose(f.f);
+        f.f = nullptr;
+        if (!ok) {
+            std::remove(tmp.c_str());
+            return tvb::set_error(TVB_ERR_INVALID, "cache_write: flush of %s failed", tmp.c_str());
+        }
+    }
+    std::remove(path);
+    if (std::rename(tmp.c_str(), path) != 0) {
+        std::remove(tmp.c_str());
+        return tvb::set_error(TVB_ERR_INVALID, "cache_write: rename to %s failed", path);
+    }
+    return TVB_OK;
+}
+
+tvb_status tvb_cache_open(const char* path, tvb_cache** out) {
+    TVB_REQUIRE(path && out, "cache_open: null argument");
+    *out = nullptr;
+    auto* c = new (std::nothrow) tvb_cache();
+    if (!c) return tvb::set_error(TVB_ERR_OOM, "cache_open: host allocation");
+    c->path = path;
+    c->file.f = std::fopen(path, "rb");
+    auto fail = [&](tvb_status s) {
+        delete c;
+        return s;
+    };
+    if (!c->file.f) return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: cannot open %s", path));
+    if (std::fread(&c->hdr, 1, sizeof(c->hdr), c->file.f) != sizeof(c->hdr) ||
+        std::memcmp(c->hdr.magic, "TVCACHE\0", 8) != 0)
+        return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: %s is not a .tvcache file", path));
+    if (c->hdr.version != 1 && c->hdr.version != 2)
+        return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: version %u", c->hdr.version));
+    c->table.resize(c->hdr.num_tensors);
+    if (std::fseek(c->file.f, (long)c->hdr.table_offset, SEEK_SET) != 0 ||
+        std::fread(c->table.data(), sizeof(FileTensor), c->table.size(), c->file.f) != c->table.size())
+        return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: truncated tensor table in %s", path));
+    for (auto& e : c->table) {
+        e.name[sizeof(e.name) - 1] = 0;
+        if (e.n_dims > 4 || c->hdr.data_offset + e.data_offset + e.nbytes > c->hdr.total_size)
+            return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: entry '%s' out of range", e.name));
+    }
+    *out = c;
+    return TVB_OK;
+}
+
+int tvb_cache_count(const tvb_cache* c) { return c ? (int)c->table.size() : 0; }
+
+tvb_status tvb_cache_info(const tvb_cache* c, tvb_cache_key* key, int* version) {
+    TVB_REQUIRE(c, "cache_info: null cache");
+    if (key) {
+        key->base_size = c->hdr.base_size;
+        std::memcpy(key->base_sha256, c->hdr.base_sha256, 32);
+        key->lora_size = c->hdr.lora_size;
+        std::memcpy(key->lora_sha256, c->hdr.lora_sha256, 32);
+        key->lora_alpha = c->hdr.lora_alpha;
+        key->lora_rank = c->hdr.lora_rank;
+    }
+    if (version) *version = (int)c->hdr.version;
+    return TVB_OK;
+}
+
+tvb_status tvb_cache_entry(const tvb_cache* c, int i, tvb_cache_tensor* info, uint64_t* nbytes) {
+    TVB_REQUIRE(c && info && i >= 0 && i < (int)c->table.size(), "cache_entry: bad arguments");
+    const FileTensor& e = c->table[i];
+    std::memset(info, 0, sizeof(*info));
+    info->name = e.name;
+    info->ggml_type = (int)e.dtype;
+    info->n_dims = (int)e.n_dims;
+    for (uint32_t d = 0; d < e.n_dims; ++d) info->shape[d] = (int64_t)e.shape[d];
+    if (nbytes) *nbytes = e.nbytes;
+    return TVB_OK;
+}
+
+tvb_status tvb_cache_read(tvb_cache* c, const char* name, void* dst, uint64_t capacity) {
+    TVB_REQUIRE(c && name && dst, "cache_read: null argument");
+    const FileTensor* e = nullptr;
+    for (const auto& t : c->table)
+        if (std::strcmp(t.name, name) == 0) e = &t;
+    TVB_REQUIRE(e, "cache_read: no tensor '%s' in %s", name, c->path.c_str());
+    TVB_REQUIRE(capacity >= e->nbytes, "cache_read: '%s' needs %llu bytes, destination has %llu", name,
+                (unsigned long long)e->nbytes, (unsigned long long)capacity);
+    if (std::fseek(c->file.f, (long)(c->hdr.data_offset + e->data_offset), SEEK_SET) != 0)
+        return tvb::set_error(TVB_ERR_INVALID, "cache_read: seek failed for '%s'", name);
+    if (!on_device(dst)) {
+        if (std::fread(dst, 1, e->nbytes, c->file.f) != e->nbytes)
+            return tvb::set_error(TVB_ERR_INVALID, "cache_read: short read of '%s'", name);
+        return TVB_OK;
+    }
+    // file -> pinned chunk -> device, the upload of chunk i overlapping the read of chunk i + 1
+    Staging sg;
+    TVB_TRY(sg.init());
+    char* d = static_cast<char*>(dst);
+    size_t done = 0;
+    int cur = 0;
+    while (done < e->nbytes) {
+        const size_t len = e->nbytes - done < kChunk ? e->nbytes - done : kChunk;
+        TVB_CUDA(cudaEventSynchronize(sg.ev[cur]));   // the buffer's previous upload is done
+        if (std::fread(sg.buf[cur], 1, len, c->file.f) != len)
+            return tvb::set_error(TVB_ERR_INVALID, "cache_read: short read of '%s'", name);
+        TVB_CUDA(cudaMemcpyAsync(d + done, sg.buf[cur], len, cudaMemcpyHostToDevice, sg.st));
+        TVB_CUDA(cudaEventRecord(sg.ev[cur], sg.st));
+        done += len;
+        cur ^= 1;
+    }
+    TVB_CUDA(cudaStreamSynchronize(sg.st));
+    return TVB_OK;
+}
+
+tvb_status tvb_cache_close(tvb_cache* c) {
+    delete c;
+    return TVB_OK;
+}
+
+}  // extern "C"

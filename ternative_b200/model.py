@@ -223,6 +223,12 @@ class Model:
                 **{name: self.device_weight(li, name) for name in PROJ})
         self.backend.set_output(self.tok_embd, self.output_norm)
 
+    def save_cache(self, path: str, key=None) -> None:
+        """ModelCache::save of the merged device weights (no host copy of the
+        model; .tvcache format of cache.cpp:263-375)."""
+        from . import cache
+        cache.write(path, key if key is not None else cache.make_key(), cache.model_entries(self))
+
     # ---- reference Model API on the fused path ----------------------------------
     def forward_gpu(self, token: int, pos: int):
         return self.backend.decode_step(token, pos)
