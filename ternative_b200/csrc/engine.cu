@@ -160,6 +160,13 @@ struct tvb_context {
     cudaGraphExec_t g_step = nullptr;    // layers + lm_head
     cudaGraphExec_t g_layers = nullptr;  // layers only (prefill rows before the last)
     bool dirty = true;
+    unsigned gen = 0;   // weights / tensor-parallel setup changes (invalidate captured graphs)
+    // the batched step as a graph per batch size: a size is run once eagerly
+    // (lazy set-up: kernel attributes, scratch) and captured on its next call
+    cudaGraphExec_t bd_graph = nullptr;
+    int bd_graph_B = 0;
+    unsigned bd_gen = 0;
+    unsigned long long bd_eager = 0;   // bit B: run eagerly at generation bd_gen
     // batched-prefill workspace (allocated by the first tvb_prefill): rows of
     // the prompt chunk in flight, F16 hi/lo activation planes for the tensor
     // cores, and the F16 widening of one projection group of an INT8 layer
@@ -657,8 +664,9 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot) {
 // partials are exchanged as in the batched prefill and every rank takes the
 // largest of the ranks' per-row argmax keys.  Leaves the B next tokens in
 // h_io[2B ..) after the stream is synchronised, the logits of this rank's
-// vocabulary slice in bd_logits [B][V / world].
-tvb_status decode_batch(tvb_context* c, const int* tokens, const int* positions, int B) {
+// vocabulary slice in bd_logits [B][V / world].  The tokens and positions are
+// read from the pinned staging h_io[0, 2B), so the step can be captured.
+tvb_status decode_batch(tvb_context* c, int B) {
     const cudaStream_t st = c->stream;
     const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
     const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
@@ -686,10 +694,6 @@ tvb_status decode_batch(tvb_context* c, const int* tokens, const int* positions,
     int* d_tok = c->bd_io;
     int* d_pos = c->bd_io + kMaxBatch;
     int* d_next = c->bd_io + 2 * kMaxBatch;
-    for (int b = 0; b < B; ++b) {
-        c->h_io[b] = tokens[b];
-        c->h_io[B + b] = positions[b];
-    }
     TVB_CUDA(cudaMemcpyAsync(d_tok, c->h_io, (size_t)B * 4, cudaMemcpyHostToDevice, st));
     TVB_CUDA(cudaMemcpyAsync(d_pos, c->h_io + B, (size_t)B * 4, cudaMemcpyHostToDevice, st));
     TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), d_tok, B, H, c->pf_x, st));
@@ -901,6 +905,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->g_step) cudaGraphExecDestroy(c->g_step);
     if (c->g_layers) cudaGraphExecDestroy(c->g_layers);
+    if (c->bd_graph) cudaGraphExecDestroy(c->bd_graph);
     void* dev[] = {c->d_x, c->d_norm, c->d_q, c->d_k, c->d_v, c->d_gate, c->d_up, c->e_x, c->e_q,
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
@@ -939,6 +944,7 @@ tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
     c->tp_ready = world == 1;
     if (world == 1) c->tp_peer[0] = c->tp_xchg;
     c->dirty = true;
+    ++c->gen;
     *exchange = c->tp_xchg;
     return TVB_OK;
 }
@@ -955,6 +961,7 @@ tvb_status tvb_tp_set_peers(tvb_context* c, void* const* exchanges) {
     }
     c->tp_ready = true;
     c->dirty = true;
+    ++c->gen;
     return TVB_OK;
 }
 
@@ -1056,6 +1063,7 @@ tvb_status tvb_set_layer(tvb_context* c, int layer, const tvb_layer_weights* lw)
     c->layers[layer] = *lw;
     c->layer_set[layer] = true;
     c->dirty = true;
+    ++c->gen;
     return TVB_OK;
 }
 
@@ -1065,6 +1073,7 @@ tvb_status tvb_set_output(tvb_context* c, const void* tok_embd, const float* out
     c->tok_embd = tok_embd;
     c->output_norm = output_norm;
     c->dirty = true;
+    ++c->gen;
     return TVB_OK;
 }
 
@@ -1179,7 +1188,41 @@ tvb_status tvb_decode_batch(tvb_context* c, const int* tokens, const int* positi
     if (c->tp_world > 1) TVB_REQUIRE(c->tp_ready, "decode_batch: peers not set (tvb_tp_set_peers)");
     TVB_TRY(pf_workspace(c));
     TVB_CUDA(cudaStreamSynchronize(c->stream));   // the pinned staging is reused
-    TVB_TRY(decode_batch(c, tokens, positions, B));
+    for (int b = 0; b < B; ++b) {
+        c->h_io[b] = tokens[b];
+        c->h_io[B + b] = positions[b];
+    }
+    // ~10 launches per layer: replayed as one graph once this batch size has
+    // run eagerly (its lazy set-up done) under the current weights
+    if (c->bd_gen != c->gen) {
+        if (c->bd_graph) cudaGraphExecDestroy(c->bd_graph);
+        c->bd_graph = nullptr;
+        c->bd_eager = 0;
+        c->bd_gen = c->gen;
+    }
+    const unsigned long long bit = 1ull << B;
+    if (c->bd_graph && c->bd_graph_B == B) {
+        TVB_CUDA(cudaGraphLaunch(c->bd_graph, c->stream));
+    } else if (c->bd_eager & bit) {
+        if (c->bd_graph) cudaGraphExecDestroy(c->bd_graph);
+        c->bd_graph = nullptr;
+        TVB_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        const tvb_status s = decode_batch(c, B);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+        if (s != TVB_OK || e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return s != TVB_OK ? s : cuda_error(e, "cudaStreamEndCapture");
+        }
+        const cudaError_t ie = cudaGraphInstantiate(&c->bd_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return cuda_error(ie, "cudaGraphInstantiate (batched step)");
+        c->bd_graph_B = B;
+        TVB_CUDA(cudaGraphLaunch(c->bd_graph, c->stream));
+    } else {
+        TVB_TRY(decode_batch(c, B));
+        c->bd_eager |= bit;
+    }
     const int vs = c->V / c->tp_world;
     if (logits)
         TVB_CUDA(cudaMemcpyAsync(logits, c->bd_logits, (size_t)B * vs * 4, cudaMemcpyDeviceToHost, c->stream));

@@ -561,9 +561,10 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
 // ---------------------------------------------------------------------------
 // RMSNorm + hi/lo split, embedding gather, INT8 widening
 // ---------------------------------------------------------------------------
-constexpr int kNsThreads = 256;
+// one CTA per row: 256 threads, or 1024 when the rows alone leave most SMs idle
 
-__global__ void __launch_bounds__(kNsThreads)
+template <int NT>
+__global__ void __launch_bounds__(NT)
 pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
                      __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp,
                      float* __restrict__ ss_out) {
@@ -571,12 +572,12 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
     const float4* w4 = reinterpret_cast<const float4*>(w);
     const int K4 = K >> 2;
-    __shared__ float red[kNsThreads / 32];
+    __shared__ float red[NT / 32];
     __shared__ float s_inv, s_max;
     float inv = 1.0f;
     if (w) {
         float ss = 0.f;
-        for (int k = tid; k < K4; k += kNsThreads) {
+        for (int k = tid; k < K4; k += NT) {
             const float4 v = x4[k];
             ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
@@ -585,7 +586,7 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
         __syncthreads();
         if (tid == 0) {
             float t = 0.f;
-            for (int i = 0; i < kNsThreads / 32; ++i) t += red[i];
+            for (int i = 0; i < NT / 32; ++i) t += red[i];
             // tensor.cpp:672-673: rms = sqrt(ss/n + eps); inv_rms = 1/rms.  A
             // sub-norm whose row spans the tensor-parallel ranks is deferred:
             // the row's sum of squares goes out and the consumer scales by the
@@ -602,7 +603,7 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     }
     // the normalised row x * (inv_rms * w) (the vectorised path of tensor_rms_norm)
     float mx = 0.f;
-    for (int k = tid; k < K4; k += kNsThreads) {
+    for (int k = tid; k < K4; k += NT) {
         float4 v = x4[k];
         if (w) {
             const float4 g = w4[k];
@@ -616,7 +617,7 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     __syncthreads();
     if (tid == 0) {
         float t = 0.f;
-        for (int i = 0; i < kNsThreads / 32; ++i) t = fmaxf(t, red[i]);
+        for (int i = 0; i < NT / 32; ++i) t = fmaxf(t, red[i]);
         s_max = t;
     }
     __syncthreads();
@@ -627,7 +628,7 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     const float sc = ldexpf(1.0f, -e);
     __half2* h2 = reinterpret_cast<__half2*>(xh + (size_t)row * K);
     __half2* l2 = reinterpret_cast<__half2*>(xl + (size_t)row * K);
-    for (int k = tid; k < K4; k += kNsThreads) {
+    for (int k = tid; k < K4; k += NT) {
         float4 v = x4[k];
         if (w) {
             const float4 g = w4[k];
@@ -667,8 +668,12 @@ __global__ void pf_i8_kernel(const int8_t* __restrict__ q, size_t n, __half* __r
 tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh, uint16_t* xl,
                          int* row_exp, cudaStream_t st, float* ss_out) {
     TVB_REQUIRE(x && xh && xl && row_exp && S > 0 && K > 0 && K % 4 == 0, "norm_split: bad arguments");
-    pf_norm_split_kernel<<<S, kNsThreads, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
-                                                   reinterpret_cast<__half*>(xl), row_exp, ss_out);
+    if (S < num_sms())
+        pf_norm_split_kernel<1024><<<S, 1024, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
+                                                       reinterpret_cast<__half*>(xl), row_exp, ss_out);
+    else
+        pf_norm_split_kernel<256><<<S, 256, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
+                                                     reinterpret_cast<__half*>(xl), row_exp, ss_out);
     return check_launch("pf_norm_split_kernel");
 }
 
