@@ -344,6 +344,230 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
     }
 }
 
+// ---------------------------------------------------------------------------
+// Few activation rows (S <= 16: batched decode, short chunks): the operands
+// swap roles so the MMA is M = 128 weight rows x N = 16 rows of x.  With the
+// tokens as M (pf_gemm_kernel) a 128-row MMA would compute 112+ empty token
+// rows per weight tile; here the tensor work per weight byte is 8x smaller and
+// the shared memory holds 6 weight stages in flight instead of 3.  TMEM: 32
+// columns, half h (128 weight rows) in columns [16h, 16h + 16), column = row
+// of x; warp w of the epilogue reads TMEM lanes 32*(w%4).. = its weight rows.
+// ---------------------------------------------------------------------------
+constexpr int kPsN = 16;                        // rows of x per MMA (N)
+constexpr int kPsStages = 6;
+constexpr int kPsPlane = kPsN * kPfBK * 2;      // 2 KB activation plane per stage
+__host__ __device__ constexpr int ps_stage_bytes(int nh) { return 2 * kPsPlane + nh * kPfHalf; }
+__host__ __device__ constexpr int ps_smem_bytes(int nh) { return kPsStages * ps_stage_bytes(nh) + 1024 + 256; }
+
+template <int NH>
+__global__ void __launch_bounds__(kPfThreads, 1)
+pf_gemm_small_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfArgs a) {
+    constexpr int kStage = ps_stage_bytes(NH);
+    constexpr uint32_t kTmemCols = 32;
+    extern __shared__ unsigned char ps_smem_raw[];
+    const uint32_t raw = smem_u32(ps_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = ps_smem_raw + (base - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPsStages * kStage);
+    uint64_t* empty = full + kPsStages;
+    uint64_t* done = empty + kPsStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued = const_cast<int*>(abort_flag) + 1;
+    int* consumed = issued + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    const int kb0 = (int)((long long)a.nk * blockIdx.z / gridDim.z);
+    const int nkb = (int)((long long)a.nk * (blockIdx.z + 1) / gridDim.z) - kb0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPsStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        *issued = 0;
+        *consumed = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int mi[2], row[2];
+    bool hv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) hv[h] = h < NH && pf_half(a, NH, tile, h, mi[h], row[h]);
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: TMA ring (x planes: 16 rows; weight halves: 128 rows) -----
+        prefetch_tmap(&maps.xh);
+        if (a.use_lo) prefetch_tmap(&maps.xl);
+        const uint32_t bytes =
+            (uint32_t)(kPsPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
+        int i = 0;
+        for (; i < nkb; ++i) {
+            const int s = i % kPsStages, r = i / kPsStages, kx = (kb0 + i) * kPfBK;
+            if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
+                pf_fail(a, abort_flag);
+                break;
+            }
+            if (*abort_flag) break;
+            const uint32_t st = base + (uint32_t)(s * kStage);
+            mbar_expect_tx(&full[s], bytes);
+            tma_load_2d(st, &maps.xh, kx, 0, &full[s]);
+            if (a.use_lo) tma_load_2d(st + kPsPlane, &maps.xl, kx, 0, &full[s]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (hv[h]) tma_load_2d(st + 2 * kPsPlane + h * kPfHalf, &maps.w[mi[h]], kx, row[h], &full[s]);
+        }
+        *issued = i;
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer: D[weight row][x row] += W . X^T per half ----------------------
+        constexpr uint32_t idesc = umma_idesc_f16(128, kPsN);
+        int kb = 0;
+        for (; kb < nkb; ++kb) {
+            const int s = kb % kPsStages, r = kb / kPsStages;
+            if (!mbar_wait_bounded(&full[s], (uint32_t)(r & 1))) {
+                pf_fail(a, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t st = base + (uint32_t)(s * kStage);
+#pragma unroll
+            for (int kk = 0; kk < kPfBK / 16; ++kk) {
+                const uint64_t xhd = sw128_desc(st + kk * 32);
+                const uint64_t xld = sw128_desc(st + kPsPlane + kk * 32);
+#pragma unroll
+                for (int h = 0; h < NH; ++h) {
+                    if (!hv[h]) continue;
+                    const uint64_t wd = sw128_desc(st + 2 * kPsPlane + h * kPfHalf + kk * 32);
+                    tc_mma(tmem + (uint32_t)(h * kPsN), wd, xhd, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    if (a.use_lo) tc_mma(tmem + (uint32_t)(h * kPsN), wd, xld, idesc, 1u);
+                }
+            }
+            tc_commit(&empty[s]);
+        }
+        *consumed = kb;
+        tc_commit(done);
+    } else if (warp >= 4) {
+        // ---- epilogue: thread = weight row r of each half, its 16 columns = rows of x --
+        const int q = warp & 3;
+        const int r = 32 * q + lane;
+        const bool ok = mbar_wait_bounded(done, 0u);
+        tc_fence_after();
+        if (!ok) pf_fail(a, abort_flag);
+        uint32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16), acc);
+        tmem_wait_ld();
+        const bool run = ok && !*abort_flag;
+        const int S = a.S;
+        float e2[kPsN];
+#pragma unroll
+        for (int t = 0; t < kPsN; ++t) e2[t] = (t < S && a.row_exp) ? ldexpf(1.0f, __ldg(a.row_exp + t)) : 1.0f;
+        if (gridDim.z > 1) {
+            if (run) {
+#pragma unroll
+                for (int h = 0; h < NH; ++h) {
+                    if (!hv[h]) continue;
+                    float* dst = a.part + (size_t)blockIdx.z * S * a.width + (size_t)tile * 128 * NH + h * 128 + r;
+#pragma unroll
+                    for (int t = 0; t < kPsN; ++t)
+                        if (t < S) dst[(size_t)t * a.width] = __uint_as_float(acc[h * kPsN + t]);
+                }
+            }
+        } else if (a.mode == PF_GATEUP) {
+            // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
+            const int n = row[0] + r;
+            if (run && hv[0] && hv[1] && n < a.rows[0]) {
+                const float sg = pf_row_scale(a, 0, n), su = pf_row_scale(a, 1, n);
+#pragma unroll
+                for (int t = 0; t < kPsN; ++t) {
+                    if (t >= S) continue;
+                    const float g = __fmul_rn(__uint_as_float(acc[t]) * e2[t], sg);
+                    const float u = __fmul_rn(__uint_as_float(acc[kPsN + t]) * e2[t], su);
+                    const float gr = fmaxf(g, 0.0f);
+                    a.y[(size_t)t * a.ldy + n] = __fmul_rn(__fmul_rn(gr, gr), u);
+                }
+            }
+        } else if (a.mode == PF_QKV) {
+            // RoPE pairs rows (d, d + 64) of a head, held by warps q and q + 2:
+            // exchange through shared memory (the pipeline's stages are idle now)
+            float* ex = reinterpret_cast<float*>(smem);   // [NH][128][kPsN + 1]
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+#pragma unroll
+                for (int t = 0; t < kPsN; ++t) ex[(h * 128 + r) * (kPsN + 1) + t] = __uint_as_float(acc[h * kPsN + t]);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int half = a.hd >> 1;
+            if (run && r < half) {
+                const int d = r;
+#pragma unroll
+                for (int h = 0; h < NH; ++h) {
+                    if (!hv[h]) continue;
+                    const int head = row[h] / a.hd;
+                    const float s0 = pf_row_scale(a, mi[h], row[h] + d);
+                    const float s1 = pf_row_scale(a, mi[h], row[h] + d + half);
+                    for (int t = 0; t < S; ++t) {
+                        const int pos = pf_pos(a, t);
+                        float y0 = __fmul_rn(ex[(h * 128 + d) * (kPsN + 1) + t] * e2[t], s0);
+                        float y1 = __fmul_rn(ex[(h * 128 + d + half) * (kPsN + 1) + t] * e2[t], s1);
+                        if (mi[h] < 2) {
+                            // NeoX pair (d, d + hd/2), tensor.cpp:918-925
+                            const float cs = __ldg(a.rope_cos + (size_t)pos * half + d);
+                            const float sn = __ldg(a.rope_sin + (size_t)pos * half + d);
+                            const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+                            const float t1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+                            y0 = t0;
+                            y1 = t1;
+                        }
+                        float* dst = mi[h] == 0 ? a.q_out + (size_t)t * a.nh * a.hd + head * a.hd
+                                                : (mi[h] == 1 ? a.kcache : a.vcache) + pf_slot(a, t) +
+                                                      (size_t)pos * a.nkv * a.hd + head * a.hd;
+                        dst[d] = y0;
+                        dst[d + half] = y1;
+                    }
+                }
+            }
+        } else {
+            const bool add = a.mode == PF_RESID;
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+                const int n = row[h] + r;
+                if (!run || !hv[h] || n >= a.rows[0]) continue;
+                const float sc = pf_row_scale(a, 0, n);
+#pragma unroll
+                for (int t = 0; t < kPsN; ++t) {
+                    if (t >= S) continue;
+                    const float v = __fmul_rn(__uint_as_float(acc[h * kPsN + t]) * e2[t], sc);
+                    float* y = a.y + (size_t)t * a.ldy + n;
+                    *y = add ? __fadd_rn(*y, v) : v;
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort_flag) {
+        for (int kb = *consumed; kb < *issued; ++kb)
+            mbar_wait_bounded(&full[kb % kPsStages], (uint32_t)((kb / kPsStages) & 1));
+    }
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
 // Split-K completion: one thread per (row, output element or RoPE/gate-up
 // pair): the ksplit partial sums added in split order, then the epilogue of
 // pf_gemm_kernel (same arithmetic after the sum).
@@ -439,14 +663,14 @@ tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint6
 }
 
 // F16 matrix [rows][K] (row pitch K), boxes of 128 rows x 64 k, 128B swizzle.
-static tvb_status encode_f16(CUtensorMap* m, const void* p, int rows, int K) {
+static tvb_status encode_f16(CUtensorMap* m, const void* p, int rows, int K, int box_rows = 128) {
     tvb_status st;
     auto fn = encode_fn(&st);
     if (!fn) return st;
     TVB_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, "prefill gemm: operand not 16-byte aligned");
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kPfBK, 128u};
+    const cuuint32_t box[2] = {(cuuint32_t)kPfBK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1u, 1u};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(p), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -463,6 +687,12 @@ static tvb_status pf_prepare() {
         if (err == cudaSuccess)
             err = cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        pf_smem_bytes(1));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(pf_gemm_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ps_smem_bytes(2));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(pf_gemm_small_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ps_smem_bytes(1));
     });
     if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(pf_gemm_kernel)");
     return TVB_OK;
@@ -496,8 +726,9 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
     a.row_pos = g.row_pos;
     a.kv_slot_stride = g.kv_slot_stride;
     a.status = g.status;
-    TVB_TRY(encode_f16(&maps.xh, g.xh, g.S, g.K));
-    if (g.xl) TVB_TRY(encode_f16(&maps.xl, g.xl, g.S, g.K));
+    const bool small = g.S <= kPsN;   // few rows of x: the swapped-operand kernel
+    TVB_TRY(encode_f16(&maps.xh, g.xh, g.S, g.K, small ? kPsN : 128));
+    if (g.xl) TVB_TRY(encode_f16(&maps.xl, g.xl, g.S, g.K, small ? kPsN : 128));
     const int nm = g.mode == PF_QKV ? 3 : g.mode == PF_GATEUP ? 2 : 1;
     for (int i = 0; i < nm; ++i) {
         TVB_REQUIRE(g.m[i].w && g.m[i].rows > 0, "prefill gemm: matrix %d missing", i);
@@ -547,7 +778,9 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
         a.ksplit = ksplit;
     }
     const dim3 grid((unsigned)tiles, (unsigned)mtiles, (unsigned)ksplit);
-    if (nh == 2) pf_gemm_kernel<2><<<grid, kPfThreads, pf_smem_bytes(2), stream>>>(maps, a);
+    if (small && nh == 2) pf_gemm_small_kernel<2><<<grid, kPfThreads, ps_smem_bytes(2), stream>>>(maps, a);
+    else if (small) pf_gemm_small_kernel<1><<<grid, kPfThreads, ps_smem_bytes(1), stream>>>(maps, a);
+    else if (nh == 2) pf_gemm_kernel<2><<<grid, kPfThreads, pf_smem_bytes(2), stream>>>(maps, a);
     else pf_gemm_kernel<1><<<grid, kPfThreads, pf_smem_bytes(1), stream>>>(maps, a);
     TVB_TRY(check_launch("pf_gemm_kernel"));
     if (ksplit == 1) return TVB_OK;
