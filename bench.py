@@ -647,7 +647,10 @@ def run_ours(args, world, rank, local):
     gemv["note"] = ("one tvb_gemv_* launch per call (includes the launch), rotating over the 30 layers' "
                     "copies (lm_head: one 657 MB copy); bytes = weights + scales + x + y")
     if world > 1:
-        gemv["tensor_parallel"] = gemv_tp_sweep(be, m, cfg, stream, world, rank, hbm)
+        try:   # a failure here is the same on every rank (no rank is left in a collective)
+            gemv["tensor_parallel"] = gemv_tp_sweep(be, m, cfg, stream, world, rank, hbm)
+        except Exception as e:
+            gemv["tensor_parallel"] = {"unavailable": repr(e)}
 
     # ---- load-time merge: all 210 projections, F16 and per-row INT8 ---------------
     merge = {}
