@@ -17,6 +17,8 @@ namespace tvb {
 __global__ void __launch_bounds__(kGemvThreads, 1)
 batch_attn_kernel(const __grid_constant__ AttnArgs base, const int* __restrict__ pos, size_t slot_stride) {
     extern __shared__ __align__(128) unsigned char bd_smem[];
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int b = blockIdx.y;
     AttnArgs a = base;
     a.q = base.q + (size_t)b * base.nh * base.hd;
@@ -31,6 +33,8 @@ batch_attn_kernel(const __grid_constant__ AttnArgs base, const int* __restrict__
 // each lane owns 4 dimensions (hd == 128).
 __global__ void batch_attn_merge_kernel(const float* __restrict__ part, int nh, int nsplit, int hd,
                                         float* __restrict__ out) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int h = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
     const float* pb = part + ((size_t)b * nh + h) * nsplit * (hd + 4);
     float ms[kMaxAttnSplits], ls[kMaxAttnSplits];
@@ -73,6 +77,8 @@ __device__ __forceinline__ unsigned long long key_max(unsigned long long a, unsi
 
 __global__ void __launch_bounds__(kArgThreads)
 batch_argmax_kernel(const float* __restrict__ logits, int n, int ld, int vocab0, unsigned long long* __restrict__ keys) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int b = blockIdx.x, tid = threadIdx.x;
     const float* row = logits + (size_t)b * ld;
     unsigned long long k = 0ull;
@@ -93,6 +99,8 @@ batch_argmax_kernel(const float* __restrict__ logits, int n, int ld, int vocab0,
 }
 
 __global__ void batch_pick_kernel(const KeySources src, int B, int* __restrict__ next) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int b = threadIdx.x;
     if (b >= B) return;
     unsigned long long k = 0ull;
@@ -102,7 +110,7 @@ __global__ void batch_pick_kernel(const KeySources src, int B, int* __restrict__
 
 tvb_status batch_attention(const float* q, const float* kcache, const float* vcache, size_t slot_stride,
                            const int* pos, int B, int nh, int nkv, int hd, int nsplit, float scale, float* part,
-                           float* out, cudaStream_t st) {
+                           float* out, cudaStream_t st, bool pdl) {
     TVB_REQUIRE(q && kcache && vcache && pos && part && out && B > 0, "batch attention: bad arguments");
     TVB_REQUIRE(hd == 128 && nh % nkv == 0 && nsplit >= 1 && nsplit <= kMaxAttnSplits,
                 "batch attention: head_dim %d, heads %d/%d, splits %d", hd, nh, nkv, nsplit);
@@ -123,22 +131,25 @@ tvb_status batch_attention(const float* q, const float* kcache, const float* vca
     a.nsplit = nsplit;
     a.scale = scale;
     a.kv_len = -1;
-    batch_attn_kernel<<<dim3((unsigned)(nkv * nsplit), (unsigned)B), kGemvThreads, smem, st>>>(a, pos, slot_stride);
+    TVB_CUDA(launch_maybe_pdl(batch_attn_kernel, dim3((unsigned)(nkv * nsplit), (unsigned)B), dim3(kGemvThreads),
+                              (size_t)smem, st, pdl, a, pos, slot_stride));
     TVB_TRY(check_launch("batch_attn_kernel"));
-    batch_attn_merge_kernel<<<dim3((unsigned)nh, (unsigned)B), 32, 0, st>>>(part, nh, nsplit, hd, out);
+    TVB_CUDA(launch_maybe_pdl(batch_attn_merge_kernel, dim3((unsigned)nh, (unsigned)B), dim3(32), 0, st, pdl,
+                              (const float*)part, nh, nsplit, hd, out));
     return check_launch("batch_attn_merge_kernel");
 }
 
 tvb_status batch_argmax(const float* logits, int B, int n, int ld, int vocab0, unsigned long long* keys,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool pdl) {
     TVB_REQUIRE(logits && keys && B > 0 && n > 0 && ld >= n, "batch argmax: bad arguments");
-    batch_argmax_kernel<<<B, kArgThreads, 0, st>>>(logits, n, ld, vocab0, keys);
+    TVB_CUDA(launch_maybe_pdl(batch_argmax_kernel, dim3(B), dim3(kArgThreads), 0, st, pdl, logits, n, ld, vocab0,
+                              keys));
     return check_launch("batch_argmax_kernel");
 }
 
-tvb_status batch_pick(const KeySources& src, int B, int* next, cudaStream_t st) {
+tvb_status batch_pick(const KeySources& src, int B, int* next, cudaStream_t st, bool pdl) {
     TVB_REQUIRE(B > 0 && B <= kMaxBatch && src.n >= 1 && src.n <= kMaxTp && next, "batch pick: bad arguments");
-    batch_pick_kernel<<<1, 32, 0, st>>>(src, B, next);
+    TVB_CUDA(launch_maybe_pdl(batch_pick_kernel, dim3(1), dim3(32), 0, st, pdl, src, B, next));
     return check_launch("batch_pick_kernel");
 }
 

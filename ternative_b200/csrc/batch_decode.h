@@ -15,12 +15,12 @@ constexpr int kMaxBatch = 32;   // sequences per batched step (argmax key area)
 // B * nh * nsplit * (hd + 4) floats of split partials.
 tvb_status batch_attention(const float* q, const float* kcache, const float* vcache, size_t slot_stride,
                            const int* pos, int B, int nh, int nkv, int hd, int nsplit, float scale, float* part,
-                           float* out, cudaStream_t st);
+                           float* out, cudaStream_t st, bool pdl = false);
 
 // Per-row greedy argmax of logits [B][ld] (n valid columns, global index =
 // vocab0 + column): keys[b] = the packed (ordered value, ~index) maximum.
 tvb_status batch_argmax(const float* logits, int B, int n, int ld, int vocab0, unsigned long long* keys,
-                        cudaStream_t st);
+                        cudaStream_t st, bool pdl = false);
 
 // next[b] = index of the largest key over the sources (one per tensor-parallel
 // rank, in rank order; a single source without tensor parallelism).
@@ -28,6 +28,6 @@ struct KeySources {
     const unsigned long long* p[kMaxTp];
     int n;
 };
-tvb_status batch_pick(const KeySources& src, int B, int* next, cudaStream_t st);
+tvb_status batch_pick(const KeySources& src, int B, int* next, cudaStream_t st, bool pdl = false);
 
 }  // namespace tvb

@@ -487,10 +487,12 @@ bool pf_batched_supported(const tvb_context* c) {
 
 // One projection operand; INT8 weights are widened to F16 into the scratch at
 // `off` (exact), their scales applied by the GEMM epilogue.
-tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size_t& off, PfMatrix& m) {
+tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size_t& off, PfMatrix& m,
+                      bool pdl = false) {
     m.rows = rows;
     m.row_scales = nullptr;
     m.scale = 1.0f;
+    m.widened = w.dtype != TVB_F16;
     if (w.dtype == TVB_F16) {
         m.w = static_cast<const uint16_t*>(w.w);
         return TVB_OK;
@@ -505,7 +507,7 @@ tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size
         c->pf_w16_elems = need;
     }
     TVB_REQUIRE(off + n <= c->pf_w16_elems, "prefill: INT8 widening scratch too small");
-    TVB_TRY(pf_i8_to_f16(static_cast<const int8_t*>(w.w), n, c->pf_w16 + off, c->stream));
+    TVB_TRY(pf_i8_to_f16(static_cast<const int8_t*>(w.w), n, c->pf_w16 + off, c->stream, pdl));
     m.w = c->pf_w16 + off;
     off += n;
     if (w.dtype == TVB_I8_ROW) m.row_scales = w.row_scales;
@@ -671,6 +673,9 @@ tvb_status decode_batch(tvb_context* c, int B) {
     const int H = c->H, Hq = c->Hq, Hk = c->Hk, I = c->I, hd = c->cfg.head_dim;
     const float eps = c->cfg.rms_norm_eps, scale = 1.0f / std::sqrt((float)hd);
     const bool tp = c->tp_world > 1;
+    // programmatic dependent launch between the step's kernels: each may start
+    // (TMEM, barriers, weight requests) while its predecessor finishes
+    const bool pdl = !g_disable_pdl;
     TpArgs tpa = {};
     size_t reg_off[2] = {0, 0};
     float* reg[2] = {nullptr, nullptr};
@@ -688,15 +693,15 @@ tvb_status decode_batch(tvb_context* c, int B) {
         }
     }
     auto exchange = [&](int j, const void* sub_norm, int k_local) -> tvb_status {
-        TVB_TRY(tp_sync(tpa, c->st, st));
-        return tp_reduce_rows(tpa, reg_off[j], B, H, sub_norm ? k_local * c->tp_world : 0, eps, c->pf_x, st);
+        TVB_TRY(tp_sync(tpa, c->st, st, pdl));
+        return tp_reduce_rows(tpa, reg_off[j], B, H, sub_norm ? k_local * c->tp_world : 0, eps, c->pf_x, st, pdl);
     };
     int* d_tok = c->bd_io;
     int* d_pos = c->bd_io + kMaxBatch;
     int* d_next = c->bd_io + 2 * kMaxBatch;
     TVB_CUDA(cudaMemcpyAsync(d_tok, c->h_io, (size_t)B * 4, cudaMemcpyHostToDevice, st));
     TVB_CUDA(cudaMemcpyAsync(d_pos, c->h_io + B, (size_t)B * 4, cudaMemcpyHostToDevice, st));
-    TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), d_tok, B, H, c->pf_x, st));
+    TVB_TRY(pf_embed(static_cast<const uint16_t*>(c->tok_embd), d_tok, B, H, c->pf_x, st, pdl));
     // attention splits: enough (kv head, split, sequence) CTAs to cover the SMs
     const int nkv = c->cfg.num_kv_heads;
     const int nsplit = std::max(1, std::min(kMaxAttnSplits, (num_sms() + nkv * B - 1) / (nkv * B)));
@@ -713,13 +718,14 @@ tvb_status decode_batch(tvb_context* c, int B) {
         g.status = &c->st->status;
         g.part = c->pf_part;
         g.part_floats = c->pf_part_floats;
+        g.pdl = pdl;
         // attn_norm -> q, k, v -> RoPE at each row's position -> KV slot rows
-        TVB_TRY(pf_norm_split(c->pf_x, lw.attn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+        TVB_TRY(pf_norm_split(c->pf_x, lw.attn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st, nullptr, pdl));
         g.mode = PF_QKV;
         g.K = H;
-        TVB_TRY(pf_operand(c, lw.wq, Hq, H, off, g.m[0]));
-        TVB_TRY(pf_operand(c, lw.wk, Hk, H, off, g.m[1]));
-        TVB_TRY(pf_operand(c, lw.wv, Hk, H, off, g.m[2]));
+        TVB_TRY(pf_operand(c, lw.wq, Hq, H, off, g.m[0], pdl));
+        TVB_TRY(pf_operand(c, lw.wk, Hk, H, off, g.m[1], pdl));
+        TVB_TRY(pf_operand(c, lw.wv, Hk, H, off, g.m[2], pdl));
         g.nh = c->cfg.num_heads;
         g.nkv = nkv;
         g.hd = hd;
@@ -733,35 +739,35 @@ tvb_status decode_batch(tvb_context* c, int B) {
         TVB_TRY(pf_gemm(g, st));
         g.row_pos = nullptr;
         TVB_TRY(batch_attention(c->pf_q, kl, vl, c->slot_floats, d_pos, B, g.nh, nkv, hd, nsplit, scale,
-                                c->bd_attn_part, c->pf_attn, st));
+                                c->bd_attn_part, c->pf_attn, st, pdl));
         // attn_sub_norm -> o_proj -> residual
         TVB_TRY(pf_norm_split(c->pf_attn, lw.attn_sub_norm, B, Hq, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
-                              tp ? reg[0] + (size_t)B * H : nullptr));
+                              tp ? reg[0] + (size_t)B * H : nullptr, pdl));
         off = 0;
         g.mode = tp ? PF_STORE : PF_RESID;
         g.K = Hq;
-        TVB_TRY(pf_operand(c, lw.wo, H, Hq, off, g.m[0]));
+        TVB_TRY(pf_operand(c, lw.wo, H, Hq, off, g.m[0], pdl));
         g.y = tp ? reg[0] : c->pf_x;
         g.ldy = H;
         TVB_TRY(pf_gemm(g, st));
         if (tp) TVB_TRY(exchange(0, lw.attn_sub_norm, Hq));
         // ffn_norm -> gate/up -> relu^2 * up
-        TVB_TRY(pf_norm_split(c->pf_x, lw.ffn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+        TVB_TRY(pf_norm_split(c->pf_x, lw.ffn_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st, nullptr, pdl));
         off = 0;
         g.mode = PF_GATEUP;
         g.K = H;
-        TVB_TRY(pf_operand(c, lw.w_gate, I, H, off, g.m[0]));
-        TVB_TRY(pf_operand(c, lw.w_up, I, H, off, g.m[1]));
+        TVB_TRY(pf_operand(c, lw.w_gate, I, H, off, g.m[0], pdl));
+        TVB_TRY(pf_operand(c, lw.w_up, I, H, off, g.m[1], pdl));
         g.y = c->pf_h;
         g.ldy = I;
         TVB_TRY(pf_gemm(g, st));
         // ffn_sub_norm -> down -> residual
         TVB_TRY(pf_norm_split(c->pf_h, lw.ffn_sub_norm, B, I, eps, c->pf_xh, c->pf_xl, c->pf_exp, st,
-                              tp ? reg[1] + (size_t)B * H : nullptr));
+                              tp ? reg[1] + (size_t)B * H : nullptr, pdl));
         off = 0;
         g.mode = tp ? PF_STORE : PF_RESID;
         g.K = I;
-        TVB_TRY(pf_operand(c, lw.w_down, H, I, off, g.m[0]));
+        TVB_TRY(pf_operand(c, lw.w_down, H, I, off, g.m[0], pdl));
         g.y = tp ? reg[1] : c->pf_x;
         g.ldy = H;
         TVB_TRY(pf_gemm(g, st));
@@ -770,7 +776,7 @@ tvb_status decode_batch(tvb_context* c, int B) {
     // output_norm + tied lm_head over this rank's vocabulary slice, then the
     // per-row greedy argmax (model.cpp:1571-1580 per sequence)
     const int vs = c->V / c->tp_world;
-    TVB_TRY(pf_norm_split(c->pf_x, c->output_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st));
+    TVB_TRY(pf_norm_split(c->pf_x, c->output_norm, B, H, eps, c->pf_xh, c->pf_xl, c->pf_exp, st, nullptr, pdl));
     PfGemm g;
     g.mode = PF_STORE;
     g.S = B;
@@ -781,6 +787,7 @@ tvb_status decode_batch(tvb_context* c, int B) {
     g.status = &c->st->status;
     g.part = c->pf_part;
     g.part_floats = c->pf_part_floats;
+    g.pdl = pdl;
     g.m[0].w = static_cast<const uint16_t*>(c->tok_embd) + (size_t)c->tp_rank * vs * H;
     g.m[0].rows = vs;
     g.y = c->bd_logits;
@@ -791,17 +798,17 @@ tvb_status decode_batch(tvb_context* c, int B) {
         // every rank publishes its B keys in its own buffer, then takes the
         // largest over the ranks (the next step's syncs order the reuse)
         unsigned long long* own = reinterpret_cast<unsigned long long*>(c->tp_xchg + c->tp_key_off);
-        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, c->tp_rank * vs, own, st));
-        TVB_TRY(tp_sync(tpa, c->st, st));
+        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, c->tp_rank * vs, own, st, pdl));
+        TVB_TRY(tp_sync(tpa, c->st, st, pdl));
         src.n = c->tp_world;
         for (int r = 0; r < c->tp_world; ++r)
             src.p[r] = reinterpret_cast<const unsigned long long*>(c->tp_peer[r] + c->tp_key_off);
     } else {
-        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, 0, c->bd_keys, st));
+        TVB_TRY(batch_argmax(c->bd_logits, B, vs, vs, 0, c->bd_keys, st, pdl));
         src.n = 1;
         src.p[0] = c->bd_keys;
     }
-    TVB_TRY(batch_pick(src, B, d_next, st));
+    TVB_TRY(batch_pick(src, B, d_next, st, pdl));
     TVB_CUDA(cudaMemcpyAsync(c->h_io + 2 * B, d_next, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
     return TVB_OK;
 }

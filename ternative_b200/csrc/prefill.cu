@@ -69,6 +69,7 @@ struct PfArgs {
     unsigned* status;
     float* part;             // split-K: raw partials [ksplit][S][width]
     int ksplit, width;       // width = tiles * 128 * NH
+    int w_static;            // no earlier kernel of the stream writes the weights
 };
 
 // Position of activation row s, and the offset of its KV cache slot.
@@ -174,6 +175,8 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // (programmatic launch) the activations come from the previous kernel
+    pdl_launch_dependents();
 
     int mi[2], row[2];
     bool hv[2];
@@ -402,6 +405,8 @@ pf_gemm_small_kernel(const __grid_constant__ PfMaps maps, const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
+    if (!(warp == 0 && lane == 0)) pdl_wait();   // the producer waits after its first weight requests
 
     int mi[2], row[2];
     bool hv[2];
@@ -414,7 +419,25 @@ pf_gemm_small_kernel(const __grid_constant__ PfMaps maps, const __grid_constant_
         if (a.use_lo) prefetch_tmap(&maps.xl);
         const uint32_t bytes =
             (uint32_t)(kPsPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
-        int i = 0;
+        // Programmatic launch: weights that no earlier kernel of the stream
+        // writes are requested for the first stages before the wait for the
+        // previous kernel (whose output is x); then x for those stages.
+        const int pre = a.w_static ? (nkb < kPsStages ? nkb : kPsStages) : 0;
+        for (int j = 0; j < pre; ++j) {
+            const uint32_t st = base + (uint32_t)(j * kStage);
+            mbar_expect_tx(&full[j], bytes);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (hv[h])
+                    tma_load_2d(st + 2 * kPsPlane + h * kPfHalf, &maps.w[mi[h]], (kb0 + j) * kPfBK, row[h], &full[j]);
+        }
+        pdl_wait();
+        for (int j = 0; j < pre; ++j) {
+            const uint32_t st = base + (uint32_t)(j * kStage);
+            tma_load_2d(st, &maps.xh, (kb0 + j) * kPfBK, 0, &full[j]);
+            if (a.use_lo) tma_load_2d(st + kPsPlane, &maps.xl, (kb0 + j) * kPfBK, 0, &full[j]);
+        }
+        int i = pre;
         for (; i < nkb; ++i) {
             const int s = i % kPsStages, r = i / kPsStages, kx = (kb0 + i) * kPfBK;
             if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
@@ -573,6 +596,8 @@ pf_gemm_small_kernel(const __grid_constant__ PfMaps maps, const __grid_constant_
 // pf_gemm_kernel (same arithmetic after the sum).
 template <int NH>
 __global__ void pf_splitk_epilogue(const __grid_constant__ PfArgs a) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
     if (idx >= (size_t)a.S * a.width) return;
     const int s = (int)(idx / a.width), v = (int)(idx % a.width);
@@ -730,7 +755,9 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
     TVB_TRY(encode_f16(&maps.xh, g.xh, g.S, g.K, small ? kPsN : 128));
     if (g.xl) TVB_TRY(encode_f16(&maps.xl, g.xl, g.S, g.K, small ? kPsN : 128));
     const int nm = g.mode == PF_QKV ? 3 : g.mode == PF_GATEUP ? 2 : 1;
+    a.w_static = 1;
     for (int i = 0; i < nm; ++i) {
+        if (g.m[i].widened) a.w_static = 0;
         TVB_REQUIRE(g.m[i].w && g.m[i].rows > 0, "prefill gemm: matrix %d missing", i);
         TVB_TRY(encode_f16(&maps.w[i], g.m[i].w, g.m[i].rows, g.K));
         a.rows[i] = g.m[i].rows;
@@ -778,16 +805,19 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
         a.ksplit = ksplit;
     }
     const dim3 grid((unsigned)tiles, (unsigned)mtiles, (unsigned)ksplit);
-    if (small && nh == 2) pf_gemm_small_kernel<2><<<grid, kPfThreads, ps_smem_bytes(2), stream>>>(maps, a);
-    else if (small) pf_gemm_small_kernel<1><<<grid, kPfThreads, ps_smem_bytes(1), stream>>>(maps, a);
-    else if (nh == 2) pf_gemm_kernel<2><<<grid, kPfThreads, pf_smem_bytes(2), stream>>>(maps, a);
-    else pf_gemm_kernel<1><<<grid, kPfThreads, pf_smem_bytes(1), stream>>>(maps, a);
+    const dim3 block(kPfThreads);
+    cudaError_t le;
+    if (small && nh == 2) le = launch_maybe_pdl(pf_gemm_small_kernel<2>, grid, block, ps_smem_bytes(2), stream, g.pdl, maps, a);
+    else if (small) le = launch_maybe_pdl(pf_gemm_small_kernel<1>, grid, block, ps_smem_bytes(1), stream, g.pdl, maps, a);
+    else if (nh == 2) le = launch_maybe_pdl(pf_gemm_kernel<2>, grid, block, pf_smem_bytes(2), stream, g.pdl, maps, a);
+    else le = launch_maybe_pdl(pf_gemm_kernel<1>, grid, block, pf_smem_bytes(1), stream, g.pdl, maps, a);
+    if (le != cudaSuccess) return cuda_error(le, "launch pf_gemm_kernel");
     TVB_TRY(check_launch("pf_gemm_kernel"));
     if (ksplit == 1) return TVB_OK;
     const size_t n = (size_t)g.S * a.width;
     const unsigned blocks = (unsigned)((n + 255) / 256);
-    if (nh == 2) pf_splitk_epilogue<2><<<blocks, 256, 0, stream>>>(a);
-    else pf_splitk_epilogue<1><<<blocks, 256, 0, stream>>>(a);
+    if (nh == 2) TVB_CUDA(launch_maybe_pdl(pf_splitk_epilogue<2>, dim3(blocks), dim3(256), 0, stream, g.pdl, a));
+    else TVB_CUDA(launch_maybe_pdl(pf_splitk_epilogue<1>, dim3(blocks), dim3(256), 0, stream, g.pdl, a));
     return check_launch("pf_splitk_epilogue");
 }
 
@@ -801,6 +831,8 @@ __global__ void __launch_bounds__(NT)
 pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
                      __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp,
                      float* __restrict__ ss_out) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
     const float4* w4 = reinterpret_cast<const float4*>(w);
@@ -883,6 +915,8 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
 
 __global__ void pf_embed_kernel(const uint16_t* __restrict__ embd, const int* __restrict__ tokens, int H,
                                 float* __restrict__ x) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int s = blockIdx.x;
     const uint16_t* e = embd + (size_t)__ldg(tokens + s) * H;
     for (int k = threadIdx.x; k < H; k += blockDim.x)
@@ -890,6 +924,8 @@ __global__ void pf_embed_kernel(const uint16_t* __restrict__ embd, const int* __
 }
 
 __global__ void pf_i8_kernel(const int8_t* __restrict__ q, size_t n, __half* __restrict__ out) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const size_t n4 = n >> 2;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const char4 c = reinterpret_cast<const char4*>(q)[i];
@@ -899,27 +935,30 @@ __global__ void pf_i8_kernel(const int8_t* __restrict__ q, size_t n, __half* __r
 }
 
 tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh, uint16_t* xl,
-                         int* row_exp, cudaStream_t st, float* ss_out) {
+                         int* row_exp, cudaStream_t st, float* ss_out, bool pdl) {
     TVB_REQUIRE(x && xh && xl && row_exp && S > 0 && K > 0 && K % 4 == 0, "norm_split: bad arguments");
+    __half* h = reinterpret_cast<__half*>(xh);
+    __half* l = reinterpret_cast<__half*>(xl);
     if (S < num_sms())
-        pf_norm_split_kernel<1024><<<S, 1024, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
-                                                       reinterpret_cast<__half*>(xl), row_exp, ss_out);
+        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<1024>, dim3(S), dim3(1024), 0, st, pdl, x, w, K, eps, h, l,
+                                  row_exp, ss_out));
     else
-        pf_norm_split_kernel<256><<<S, 256, 0, st>>>(x, w, K, eps, reinterpret_cast<__half*>(xh),
-                                                     reinterpret_cast<__half*>(xl), row_exp, ss_out);
+        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<256>, dim3(S), dim3(256), 0, st, pdl, x, w, K, eps, h, l,
+                                  row_exp, ss_out));
     return check_launch("pf_norm_split_kernel");
 }
 
-tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st) {
+tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st, bool pdl) {
     TVB_REQUIRE(embd && tokens && x && S > 0 && H > 0, "embed: bad arguments");
-    pf_embed_kernel<<<S, 256, 0, st>>>(embd, tokens, H, x);
+    TVB_CUDA(launch_maybe_pdl(pf_embed_kernel, dim3(S), dim3(256), 0, st, pdl, embd, tokens, H, x));
     return check_launch("pf_embed_kernel");
 }
 
-tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st) {
+tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st, bool pdl) {
     TVB_REQUIRE(q && out && n % 4 == 0, "i8_to_f16: bad arguments");
     const int blocks = (int)std::min<size_t>((n / 4 + 255) / 256, (size_t)num_sms() * 8);
-    pf_i8_kernel<<<std::max(blocks, 1), 256, 0, st>>>(q, n, reinterpret_cast<__half*>(out));
+    TVB_CUDA(launch_maybe_pdl(pf_i8_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, st, pdl, q, n,
+                              reinterpret_cast<__half*>(out)));
     return check_launch("pf_i8_kernel");
 }
 

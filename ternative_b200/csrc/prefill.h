@@ -28,6 +28,7 @@ struct PfMatrix {
     int rows = 0;
     const float* row_scales = nullptr;   // per-row scale (INT8 per row), or nullptr
     float scale = 1.0f;                  // per-tensor scale (INT8 per tensor), else 1
+    bool widened = false;                // w was written by an earlier kernel of the stream
 };
 
 struct PfGemm {
@@ -57,13 +58,15 @@ struct PfGemm {
     // epilogue; nullptr or too small: no split
     float* part = nullptr;
     size_t part_floats = 0;
+    bool pdl = false;   // programmatic dependent launch after the kernel that writes x
 };
 
 
 tvb_status pf_gemm(const PfGemm& g, cudaStream_t st);
 
 // x[s] = f32(embd[tokens[s]])  (extract_embeddings_batched)
-tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st);
+tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float* x, cudaStream_t st,
+                    bool pdl = false);
 
 // RMSNorm of each row of x [S][K] (tensor.cpp:636-708, x * (inv_rms * w)),
 // written as F16 hi + lo planes for the tensor cores with a power-of-two row
@@ -73,7 +76,8 @@ tvb_status pf_embed(const uint16_t* embd, const int* tokens, int S, int H, float
 // w only and each row's sum of squares is written to ss_out[s] (a sub-norm
 // whose rows span the tensor-parallel ranks).
 tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps, uint16_t* xh,
-                         uint16_t* xl, int* row_exp, cudaStream_t st, float* ss_out = nullptr);
+                         uint16_t* xl, int* row_exp, cudaStream_t st, float* ss_out = nullptr,
+                         bool pdl = false);
 
 // Causal GQA attention of S query rows at positions pos0 .. pos0 + S - 1 over
 // KV rows [0, pos0 + s] (compute_batched_attention, model.cpp:1071-1137).
@@ -96,6 +100,6 @@ tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint6
                             const uint32_t* box);
 
 // INT8 -> F16 (exact: |q| <= 127).
-tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st);
+tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st, bool pdl = false);
 
 }  // namespace tvb

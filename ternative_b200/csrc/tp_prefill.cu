@@ -28,6 +28,8 @@ namespace tvb {
 // One thread: order this rank's earlier writes (previous kernels of the
 // stream) at system scope, signal every rank, wait (bounded) for all of them.
 __global__ void tp_sync_kernel(const __grid_constant__ TpArgs t, StepState* st) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const unsigned e = st->tp_epoch + 1u;
     tp_signal(t, e);
     if (tp_wait(t, e, &st->abort, &st->status)) st->tp_epoch = e;
@@ -38,6 +40,8 @@ __global__ void tp_sync_kernel(const __grid_constant__ TpArgs t, StepState* st) 
 // (tensor.cpp:672-673) or 1 without a sub-norm (norm_n == 0).
 __global__ void tp_reduce_rows_kernel(const __grid_constant__ TpArgs t, size_t off, int S, int H, int norm_n,
                                       float eps, float* __restrict__ x) {
+    pdl_wait();   // launched after the kernel that writes this one's inputs
+    pdl_launch_dependents();
     const int row = blockIdx.x, tid = threadIdx.x;
     __shared__ float s_inv;
     if (tid == 0) {
@@ -70,15 +74,15 @@ size_t tp_prefill_region_floats(int rows, int H) {
     return ((size_t)rows * H + (size_t)rows + 63) / 64 * 64;
 }
 
-tvb_status tp_sync(const TpArgs& t, StepState* st, cudaStream_t stream) {
-    tp_sync_kernel<<<1, 1, 0, stream>>>(t, st);
+tvb_status tp_sync(const TpArgs& t, StepState* st, cudaStream_t stream, bool pdl) {
+    TVB_CUDA(launch_maybe_pdl(tp_sync_kernel, dim3(1), dim3(1), 0, stream, pdl, t, st));
     return check_launch("tp_sync_kernel");
 }
 
 tvb_status tp_reduce_rows(const TpArgs& t, size_t off, int S, int H, int norm_n, float eps, float* x,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool pdl) {
     TVB_REQUIRE(S > 0 && H % 4 == 0 && off % 4 == 0, "tp_reduce_rows: bad arguments");
-    tp_reduce_rows_kernel<<<S, 256, 0, stream>>>(t, off, S, H, norm_n, eps, x);
+    TVB_CUDA(launch_maybe_pdl(tp_reduce_rows_kernel, dim3(S), dim3(256), 0, stream, pdl, t, off, S, H, norm_n, eps, x));
     return check_launch("tp_reduce_rows_kernel");
 }
 
