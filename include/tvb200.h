@@ -335,6 +335,24 @@ tvb_status tvb_prefill_slot(tvb_context* ctx, int slot, const int* tokens_host, 
 tvb_status tvb_decode_batch(tvb_context* ctx, const int* tokens_host, const int* positions_host, int B,
                             float* logits_host, int* next_tokens_host);
 
+/* ---- token sampler --------------------------------------------------------
+ * sample_token (src/sampler.cpp:11-148; SamplerConfig, include/ternative/
+ * sampler.h:8-14) on the device for B rows of logits (row b at logits + b*ld):
+ * temperature, repetition penalty over row b's seen tokens (seen + b*max_seen,
+ * n_seen[b] of them), softmax, top-k, top-p, renormalisation and the draw
+ * against u[b] in [0, 1) (the reference draws it from its own mt19937).
+ * out[b] receives the token.  All pointers are device memory; top_p in (0, 1)
+ * needs 1 <= top_k <= 1024.  Allocates a per-call workspace on `stream`. */
+typedef struct {
+    float temperature;
+    float top_p;
+    int top_k;
+    float repetition_penalty;
+} tvb_sampler_config;
+
+tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, const tvb_sampler_config* cfg,
+                      const int* seen, const int* n_seen, int max_seen, const float* u, int* out, void* stream);
+
 /* ---- merged-weight cache (.tvcache) ---------------------------------------
  * ModelCache::save / ModelCache::try_load (src/cache.cpp:263-470, format
  * include/ternative/cache.h:28-62), fed from and into device memory: the merge

@@ -199,6 +199,8 @@ class Reference:
         L.tvref_model_get.restype = C.c_longlong
         L.tvref_model_get.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.tvref_model_lora.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int)]
+        L.tvref_sample_token.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _i32p,
+                                         C.c_int]
         L.tvref_time_decode.restype = C.c_double
         L.tvref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         self.L = L
@@ -480,3 +482,50 @@ def forward_prefill(shape: ModelShape, weights: dict, tokens, f16_to_f32, return
     if return_hidden:
         return xn.astype(np.float32)
     return (xn @ f(weights["tok_embd"]).T).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# sample_token (src/sampler.cpp:11-148) restated with an explicit uniform draw
+# ---------------------------------------------------------------------------
+def sample_token(logits, temperature=0.8, top_p=0.9, top_k=40, penalty=1.1, seen=(), u=0.5,
+                 return_cdf=False):
+    """The reference's sampler with the draw `u` given (it draws u from its own
+    mt19937, sampler.cpp:120-131).  F32 values, F64 sums, as the reference."""
+    lg = np.asarray(logits, np.float32)
+    V = lg.size
+    p = lg.copy()
+    if temperature > 0.0 and temperature != 1.0:                       # :20-25
+        p = (p / np.float32(temperature)).astype(np.float32)
+    if penalty > 1.0 and len(seen):                                    # :27-37
+        done = set()
+        for t in seen:
+            if 0 <= t < V and t not in done:
+                p[t] = np.float32(p[t] / np.float32(penalty))
+                done.add(t)
+    mx = p.max()                                                       # :39-48
+    e = np.exp((p - mx).astype(np.float32)).astype(np.float32)
+    s = float(np.sum(e.astype(np.float64)))
+    p = (e.astype(np.float64) / s).astype(np.float32)
+    order = np.lexsort((np.arange(V), p))[::-1]                         # (p, index) descending
+    if 0 < top_k < V:                                                  # :50-72
+        keep = np.zeros(V, bool)
+        keep[order[:top_k]] = True
+        p[~keep] = 0.0
+    if 0.0 < top_p < 1.0:                                              # :74-103
+        idx = [i for i in np.lexsort((np.arange(V), p))[::-1] if p[i] > 0.0]
+        cum = np.float32(0.0)
+        nucleus = np.zeros(V, bool)
+        for i in idx:
+            cum = np.float32(cum + p[i])
+            nucleus[i] = True
+            if cum >= np.float32(top_p):
+                break
+        p[~nucleus] = 0.0
+    s2 = float(np.sum(p.astype(np.float64)))                           # :105-121
+    if s2 <= 0.0:
+        return int(np.argmax(lg)) if not return_cdf else (int(np.argmax(lg)), None)
+    p = (p.astype(np.float64) / s2).astype(np.float32)
+    cdf = np.cumsum(p, dtype=np.float32)                               # :133-147 (sequential)
+    hit = np.nonzero(np.float32(u) <= cdf)[0]
+    tok = int(hit[0]) if hit.size else V - 1
+    return (tok, cdf) if return_cdf else tok

@@ -306,6 +306,19 @@ void tvref_model_lora(tvref_model* h, float* alpha, int* rank) {
     *rank = h->m.lora_rank;
 }
 
+// sampler.cpp:11-148 -- sample_token with the reference's own (randomly seeded)
+// draw; deterministic only where the configuration leaves one candidate.
+int tvref_sample_token(const float* logits, int vocab, float temperature, float top_p, int top_k,
+                       float penalty, const int* seen, int n_seen) {
+    SamplerConfig cfg;
+    cfg.temperature = temperature;
+    cfg.top_p = top_p;
+    cfg.top_k = top_k;
+    cfg.repetition_penalty = penalty;
+    std::vector<int> prompt(seen, seen + n_seen);
+    return sample_token(logits, vocab, cfg, prompt);
+}
+
 // Copy one layer's CPU KV cache rows [0, n) (layout [pos][n_kv][hd], F32).
 int tvref_kv_read(tvref_model* h, int layer, int n, float* k, float* v) {
     const auto& c = h->m.config;

@@ -74,6 +74,11 @@ class CacheTensor(C.Structure):
                 ("shape", C.c_int64 * 4), ("data", C.c_void_p), ("row_scales", C.c_void_p)]
 
 
+class SamplerConfig(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int),
+                ("repetition_penalty", C.c_float)]
+
+
 class IpcHandle(C.Structure):
     _fields_ = [("bytes", C.c_ubyte * 64)]
 
@@ -127,6 +132,7 @@ _SIGS = {
     "tvb_decode_enqueue": [_P, _I, _I, _I],
     "tvb_prefill": [_P, _P, _I, _P, _P],
     "tvb_prefill_slot": [_P, _I, _P, _I, _P, _P],
+    "tvb_sample": [_P, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P],
     "tvb_cache_write": [C.c_char_p, _P, _P, _I],
     "tvb_cache_open": [C.c_char_p, _P],
     "tvb_cache_count": [_P],

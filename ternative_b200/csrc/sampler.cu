@@ -1,0 +1,268 @@
+// The token sampler on the device (sample_token, src/sampler.cpp:11-148) for B
+// rows of logits, so a batched decode step need not copy 128k logits per row
+// to the host.  One CTA of 1024 threads per row runs the reference's steps in
+// its order and arithmetic:
+//
+//   1. logits / temperature (when temperature > 0 and != 1)
+//   2. repetition penalty: each distinct seen token's value / penalty once
+//   3. softmax: exp(v - max) in F32, the sum in F64, p = (float)(e / sum)
+//   4. top-k: keep the k largest (p, index) pairs (ties: the larger index)
+//   5. top-p: of the kept p > 0, sorted by (p, index) descending, the shortest
+//      prefix whose F32 running sum reaches top_p
+//   6. renormalise (F64 sum, F32 result); nothing left -> argmax of the logits
+//   7. F32 running sum in index order; the first index whose sum >= u
+//
+// The uniform draw u of step 7 is the caller's (the reference draws it from
+// its own mt19937).  Sums the reference takes in index order are taken as
+// trees here: the F64 sums differ from it only far below F32 resolution, and
+// the step-7 running sum runs sequentially in index order over the entries
+// that can be nonzero, as the reference's.  Top-p works on at most 1024
+// candidates, so it requires 1 <= top_k <= 1024.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace tvb {
+
+constexpr int kSampThreads = 1024;
+constexpr int kSampCand = 1024;
+
+struct SampArgs {
+    const float* logits;
+    int vocab, ld;
+    float temperature, penalty, top_p;
+    int top_k;
+    const int* seen;      // [B][max_seen]
+    const int* n_seen;    // [B]
+    int max_seen;
+    const float* u;       // [B]
+    int* out;             // [B]
+    float* work;          // [B][vocab] probabilities
+    unsigned* bits;       // [B][vocab / 32 + 1] penalty marks
+};
+
+__device__ __forceinline__ unsigned long long samp_key(float p, int i) {
+    return ((unsigned long long)__float_as_uint(p) << 32) | (unsigned)i;   // p >= 0: bit order = value order
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = red[lane];   // 32 warps
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+__global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_constant__ SampArgs a) {
+    const int b = blockIdx.x, tid = threadIdx.x, V = a.vocab;
+    const float* lg = a.logits + (size_t)b * a.ld;
+    float* p = a.work + (size_t)b * V;
+    unsigned* bits = a.bits + (size_t)b * (V / 32 + 1);
+    __shared__ double red_d[32];
+    __shared__ float red_f[32];
+    __shared__ unsigned long long red_k[32];
+    __shared__ unsigned long long cand[kSampCand];
+    __shared__ int s_count, s_keep, s_token;
+    __shared__ unsigned hist[256];
+
+    // 1-2. temperature, then the repetition penalty on first occurrences
+    const bool temp = a.temperature > 0.0f && a.temperature != 1.0f;
+    for (int i = tid; i < V; i += kSampThreads) p[i] = temp ? lg[i] / a.temperature : lg[i];
+    for (int i = tid; i < V / 32 + 1; i += kSampThreads) bits[i] = 0u;
+    __syncthreads();
+    if (a.penalty > 1.0f) {
+        const int n = a.n_seen[b];
+        // distinct tokens only: the first thread to mark a token divides it
+        for (int j = tid; j < n; j += kSampThreads) {
+            const int t = a.seen[(size_t)b * a.max_seen + j];
+            if (t < 0 || t >= V) continue;
+            const unsigned m = 1u << (t & 31);
+            if (!(atomicOr(&bits[t >> 5], m) & m)) p[t] = p[t] / a.penalty;
+        }
+        __syncthreads();
+    }
+    // 3. softmax
+    float mx = -FLT_MAX;
+    for (int i = tid; i < V; i += kSampThreads) mx = fmaxf(mx, p[i]);
+    mx = block_reduce(mx, [](float x, float y) { return fmaxf(x, y); }, red_f);
+    double sum = 0.0;
+    for (int i = tid; i < V; i += kSampThreads) {
+        const float e = expf(p[i] - mx);
+        p[i] = e;
+        sum += (double)e;
+    }
+    sum = block_reduce(sum, [](double x, double y) { return x + y; }, red_d);
+    for (int i = tid; i < V; i += kSampThreads) p[i] = (float)((double)p[i] / sum);
+    __syncthreads();
+
+    const bool topk = a.top_k > 0 && a.top_k < V;
+    const bool topp = a.top_p > 0.0f && a.top_p < 1.0f;   // (the host requires top_k <= 1024 with it)
+    if (topk) {
+        // 4. the k-th largest (p, index) key by an 8-bit radix select, then
+        //    everything below it set to 0
+        unsigned long long prefix = 0ull, mask = 0ull;
+        int need = a.top_k;   // rank of the wanted key among those matching the prefix
+        for (int shift = 56; shift >= 0; shift -= 8) {
+            for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0u;
+            __syncthreads();
+            for (int i = tid; i < V; i += kSampThreads) {
+                const unsigned long long k = samp_key(p[i], i);
+                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                int d = 255;
+                for (; d > 0; --d) {
+                    if ((int)hist[d] >= need) break;
+                    need -= (int)hist[d];
+                }
+                s_keep = d;
+                s_count = need;
+            }
+            __syncthreads();
+            prefix |= (unsigned long long)s_keep << shift;
+            mask |= 255ull << shift;
+            need = s_count;
+            __syncthreads();
+        }
+        const unsigned long long kth = prefix;   // exactly top_k keys are >= kth
+        for (int i = tid; i < V; i += kSampThreads)
+            if (samp_key(p[i], i) < kth) p[i] = 0.0f;
+        __syncthreads();
+    }
+    if (topp) {
+        // 5. the kept p > 0 (at most top_k <= 1024 of them) sorted descending
+        if (tid == 0) s_count = 0;
+        __syncthreads();
+        for (int i = tid; i < V; i += kSampThreads)
+            if (p[i] > 0.0f) {
+                const int at = atomicAdd(&s_count, 1);
+                if (at < kSampCand) cand[at] = samp_key(p[i], i);
+            }
+        __syncthreads();
+        const int n = min(s_count, kSampCand);
+        for (int i = n + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
+        __syncthreads();
+        // bitonic sort, descending
+        for (int size = 2; size <= kSampCand; size <<= 1) {
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const int i = tid, j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long x = cand[i], y = cand[j];
+                    if (desc ? (x < y) : (x > y)) {
+                        cand[i] = y;
+                        cand[j] = x;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (tid == 0) {
+            float cum = 0.0f;
+            int m = 0;
+            while (m < n) {
+                cum += __uint_as_float((unsigned)(cand[m] >> 32));
+                ++m;
+                if (cum >= a.top_p) break;
+            }
+            s_keep = m;   // the nucleus is cand[0, m)
+        }
+        __syncthreads();
+        const int m = s_keep;
+        // zero every p outside the nucleus (the nucleus keys are the m largest)
+        const unsigned long long lo = m > 0 ? cand[m - 1] : ~0ull;
+        for (int i = tid; i < V; i += kSampThreads)
+            if (p[i] > 0.0f && samp_key(p[i], i) < lo) p[i] = 0.0f;
+        __syncthreads();
+    }
+    // 6. renormalise
+    double s2 = 0.0;
+    for (int i = tid; i < V; i += kSampThreads) s2 += (double)p[i];
+    s2 = block_reduce(s2, [](double x, double y) { return x + y; }, red_d);
+    if (s2 <= 0.0) {
+        // nothing left: the first index of the largest logit
+        unsigned long long best = 0ull;
+        for (int i = tid; i < V; i += kSampThreads) {
+            const float v = lg[i];
+            const unsigned ob = __float_as_uint(v);
+            const unsigned ord = (ob & 0x80000000u) ? ~ob : (ob | 0x80000000u);
+            const unsigned long long k = ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (unsigned)i);
+            best = k > best ? k : best;
+        }
+        best = block_reduce(best, [](unsigned long long x, unsigned long long y) { return x > y ? x : y; }, red_k);
+        if (tid == 0) a.out[b] = (int)(0xFFFFFFFFu - (unsigned)(best & 0xFFFFFFFFu));
+        return;
+    }
+    for (int i = tid; i < V; i += kSampThreads) p[i] = (float)((double)p[i] / s2);
+    __syncthreads();
+    // 7. running F32 sum in index order; zeros leave it unchanged, so only the
+    //    nonzero entries (in index order) are visited when a filter ran
+    if (tid == 0) {
+        const float u = a.u[b];
+        float acc = 0.0f;
+        int tok = u <= 0.0f ? 0 : V - 1;   // u == 0: index 0 (its running sum is >= 0)
+        for (int i = 0; i < V && u > 0.0f; ++i) {
+            const float v = p[i];
+            if (v == 0.0f) continue;
+            acc += v;
+            if (u <= acc) {
+                tok = i;
+                break;
+            }
+        }
+        s_token = tok;
+    }
+    __syncthreads();
+    if (tid == 0) a.out[b] = s_token;
+}
+
+}  // namespace tvb
+
+extern "C" tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, const tvb_sampler_config* cfg,
+                                 const int* seen, const int* n_seen, int max_seen, const float* u, int* out,
+                                 void* stream) {
+    using namespace tvb;
+    TVB_REQUIRE(logits && cfg && u && out && B > 0 && vocab > 0 && ld >= vocab, "sample: bad arguments");
+    TVB_REQUIRE(!(cfg->repetition_penalty > 1.0f) || (seen && n_seen && max_seen >= 0),
+                "sample: repetition penalty needs the seen tokens");
+    const bool topp = cfg->top_p > 0.0f && cfg->top_p < 1.0f;
+    TVB_REQUIRE(!topp || (cfg->top_k >= 1 && cfg->top_k <= kSampCand),
+                "sample: top_p %g needs top_k in [1, %d] (got %d)", cfg->top_p, kSampCand, cfg->top_k);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t words = (size_t)vocab / 32 + 1;
+    void* ws = nullptr;
+    TVB_CUDA(cudaMallocAsync(&ws, (size_t)B * ((size_t)vocab * 4 + words * 4), st));
+    SampArgs a;
+    a.logits = logits;
+    a.vocab = vocab;
+    a.ld = ld;
+    a.temperature = cfg->temperature;
+    a.penalty = cfg->repetition_penalty;
+    a.top_p = cfg->top_p;
+    a.top_k = cfg->top_k;
+    a.seen = seen;
+    a.n_seen = n_seen;
+    a.max_seen = max_seen;
+    a.u = u;
+    a.out = out;
+    a.work = static_cast<float*>(ws);
+    a.bits = reinterpret_cast<unsigned*>(static_cast<float*>(ws) + (size_t)B * vocab);
+    sample_kernel<<<B, kSampThreads, 0, st>>>(a);
+    const cudaError_t le = cudaGetLastError();
+    cudaFreeAsync(ws, st);
+    if (le != cudaSuccess) return cuda_error(le, "sample_kernel");
+    return TVB_OK;
+}

@@ -1,0 +1,69 @@
+"""The device sampler (tvb_sample) against the restatement of the reference's
+sample_token (pinned by tests/test_sampler.py) with the same uniform draws:
+the same token for every row, except where a draw lies within 1e-5 of a
+boundary of the cumulative distribution (the device's expf and tree sums may
+move a boundary by a few F32 ulps)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle.oracle import sample_token
+
+pytestmark = pytest.mark.gpu
+
+
+def run(lib, torch, logits, cfg, seen, u):
+    from ternative_b200._lib import SamplerConfig
+    B, V = logits.shape
+    max_seen = max(1, max(len(s) for s in seen))
+    sd = np.zeros((B, max_seen), np.int32)
+    for b, s in enumerate(seen):
+        sd[b, :len(s)] = s
+    d_lg = torch.from_numpy(logits).cuda()
+    d_seen = torch.from_numpy(sd).cuda()
+    d_n = torch.tensor([len(s) for s in seen], dtype=torch.int32).cuda()
+    d_u = torch.from_numpy(np.asarray(u, np.float32)).cuda()
+    d_out = torch.full((B,), -1, dtype=torch.int32).cuda()
+    c = SamplerConfig(*cfg)
+    st = lib.tvb_sample(d_lg.data_ptr(), B, V, V, C.byref(c), d_seen.data_ptr(), d_n.data_ptr(), max_seen,
+                        d_u.data_ptr(), d_out.data_ptr(), None)
+    torch.cuda.synchronize()
+    return st, d_out.cpu().numpy()
+
+
+@pytest.mark.parametrize("V", [1000, 128256])
+@pytest.mark.parametrize("cfg", [(0.8, 0.9, 40, 1.1), (1.0, 1.0, 0, 1.0), (0.5, 0.95, 1024, 1.2),
+                                 (0.0, 0.5, 1, 1.0), (1.3, 1.0, 7, 1.0)])
+def test_device_sampler_matches_restatement(V, cfg):
+    import torch
+    from ternative_b200 import load
+    lib = load()
+    rng = np.random.default_rng(V + int(cfg[2]))
+    B = 6
+    logits = (rng.standard_normal((B, V)) * 2.5).astype(np.float32)
+    seen = [rng.integers(0, V, n).tolist() for n in (0, 5, 40, 200, 3, 77)]
+    u = rng.random(B).astype(np.float32)
+    u[0] = 0.0   # the first index whose running sum is >= 0
+    st, got = run(lib, torch, logits, cfg, seen, u)
+    assert st == 0, lib.tvb_last_error()
+    T, tp, tk, pen = cfg
+    checked = 0
+    for b in range(B):
+        tok, cdf = sample_token(logits[b], T, tp, tk, pen, seen[b], u=float(u[b]), return_cdf=True)
+        if cdf is not None and u[b] > 0:
+            nz = np.unique(cdf)
+            if np.min(np.abs(nz.astype(np.float64) - float(u[b]))) < 1e-5:
+                continue
+        assert got[b] == tok, (b, got[b], tok)
+        checked += 1
+    assert checked >= B - 1
+
+
+def test_device_sampler_rejects_top_p_without_top_k():
+    import torch
+    from ternative_b200 import load
+    lib = load()
+    logits = np.zeros((1, 100), np.float32)
+    st, _ = run(lib, torch, logits, (0.8, 0.9, 0, 1.0), [[]], [0.5])
+    assert st != 0 and b"top_k" in lib.tvb_last_error()
