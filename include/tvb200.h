@@ -335,6 +335,14 @@ tvb_status tvb_prefill_slot(tvb_context* ctx, int slot, const int* tokens_host, 
 tvb_status tvb_decode_batch(tvb_context* ctx, const int* tokens_host, const int* positions_host, int B,
                             float* logits_host, int* next_tokens_host);
 
+/* Model::score_logprobs (model.cpp:1746-1831): prefill the T tokens (KV slot 0)
+ * and, for every position p in [max(1, start_pos), T), the log-probability of
+ * tokens[p] given tokens[0, p) (logprobs[p - first]) and the k largest
+ * log-probabilities with their ids (top_*[(p - first) * k + j], descending).
+ * k <= 64; single-GPU contexts.  Synchronises. */
+tvb_status tvb_score_logprobs(tvb_context* ctx, const int* tokens_host, int T, int start_pos, int k,
+                              float* logprobs_host, int* top_ids_host, float* top_logprobs_host);
+
 /* ---- token sampler --------------------------------------------------------
  * sample_token (src/sampler.cpp:11-148; SamplerConfig, include/ternative/
  * sampler.h:8-14) on the device for B rows of logits (row b at logits + b*ld):

@@ -201,6 +201,7 @@ class Reference:
         L.tvref_model_lora.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int)]
         L.tvref_sample_token.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _i32p,
                                          C.c_int]
+        L.tvref_score_logprobs.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, _f32p, _i32p, _f32p]
         L.tvref_time_decode.restype = C.c_double
         L.tvref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         self.L = L
@@ -373,6 +374,16 @@ class ReferenceModel:
         a, r = C.c_float(), C.c_int()
         self.ref.L.tvref_model_lora(self.h, C.byref(a), C.byref(r))
         return a.value, r.value
+
+    def score_logprobs(self, tokens, k: int, start: int = 0):
+        """Model::score_logprobs: (logprobs [n], top ids [n][k], top logprobs [n][k])."""
+        tokens = _c(tokens, np.int32)
+        n = max(0, tokens.size - max(1, start))
+        lp = np.zeros(max(n, 1), np.float32)
+        ids = np.zeros(max(n * k, 1), np.int32)
+        top = np.zeros(max(n * k, 1), np.float32)
+        got = self.ref.L.tvref_score_logprobs(self.h, tokens, tokens.size, k, start, lp, ids, top)
+        return lp[:got], ids[:got * k].reshape(got, k), top[:got * k].reshape(got, k)
 
     def forward_prefill(self, tokens):
         tokens = _c(tokens, np.int32)

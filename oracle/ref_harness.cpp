@@ -319,6 +319,23 @@ int tvref_sample_token(const float* logits, int vocab, float temperature, float 
     return sample_token(logits, vocab, cfg, prompt);
 }
 
+// model.cpp:1746-1831 -- Model::score_logprobs: for positions [max(1, start), T)
+// the token's log-probability and the top k (ids, log-probabilities).
+// Returns the number of scored positions.
+int tvref_score_logprobs(tvref_model* h, const int* tokens, int T, int k, int start, float* lp, int* ids,
+                         float* top) {
+    std::vector<int> t(tokens, tokens + T);
+    auto res = h->m.score_logprobs(t, k, start);
+    for (size_t i = 0; i < res.logprobs.size(); ++i) {
+        lp[i] = res.logprobs[i].logprob;
+        for (int j = 0; j < (int)res.logprobs[i].top_logprobs.size() && j < k; ++j) {
+            ids[i * k + j] = res.logprobs[i].top_logprobs[j].token_id;
+            top[i * k + j] = res.logprobs[i].top_logprobs[j].logprob;
+        }
+    }
+    return (int)res.logprobs.size();
+}
+
 // Copy one layer's CPU KV cache rows [0, n) (layout [pos][n_kv][hd], F32).
 int tvref_kv_read(tvref_model* h, int layer, int n, float* k, float* v) {
     const auto& c = h->m.config;

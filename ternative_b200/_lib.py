@@ -133,6 +133,7 @@ _SIGS = {
     "tvb_prefill": [_P, _P, _I, _P, _P],
     "tvb_prefill_slot": [_P, _I, _P, _I, _P, _P],
     "tvb_sample": [_P, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P],
+    "tvb_score_logprobs": [_P, _P, _I, _I, _I, _P, _P, _P],
     "tvb_cache_write": [C.c_char_p, _P, _P, _I],
     "tvb_cache_open": [C.c_char_p, _P],
     "tvb_cache_count": [_P],

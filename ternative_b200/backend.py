@@ -303,6 +303,18 @@ class CUDABackend:
              None if logits is None else logits.ctypes.data, C.byref(am))
         return logits, am.value
 
+    def score_logprobs(self, tokens, k: int = 5, start_pos: int = 0):
+        """Model::score_logprobs: (logprob of each scored token [n], top ids [n][k],
+        top logprobs [n][k]) for positions max(1, start_pos) .. len(tokens) - 1."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        n = max(0, t.size - max(1, start_pos))
+        lp = np.empty(max(n, 1), np.float32)
+        ids = np.empty(max(n * k, 1), np.int32)
+        top = np.empty(max(n * k, 1), np.float32)
+        call("tvb_score_logprobs", self.ctx, t.ctypes.data, t.size, start_pos, k, lp.ctypes.data,
+             ids.ctypes.data, top.ctypes.data)
+        return lp[:n], ids[:n * k].reshape(n, k), top[:n * k].reshape(n, k)
+
     def prefill_slot(self, slot: int, tokens, want_logits: bool = True):
         """prefill() into KV cache slot `slot` (batched decode); slot 0 is the
         single-sequence cache."""

@@ -13,6 +13,7 @@
 #include "prefill.h"
 #include "tp_prefill.h"
 #include "batch_decode.h"
+#include "sampler.h"
 
 #include <algorithm>
 #include <cmath>
@@ -527,7 +528,21 @@ tvb_status pf_operand(tvb_context* c, const tvb_weight& w, int rows, int K, size
 // every rank adds all ranks' partial rows, in rank order, to its copy of the
 // residual.  The lm_head takes this rank's vocabulary slice and the ranks agree
 // on the argmax through the decode step's key exchange.
-tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot) {
+// Scoring job of tvb_score_logprobs: after the layers of each prompt chunk, the
+// rows that predict a scored token get their logits (output norm + tied
+// lm_head, up to kLpRows at a time) and their log-probabilities.
+struct LpJob {
+    int first;          // first scored position (row first - 1 predicts it)
+    int k;
+    const int* target;  // device: the scored tokens, tokens[first ..]
+    float* logits;      // device [kLpRows][V]
+    float* lp;          // device [n]
+    int* ids;           // device [n][k]
+    float* top;         // device [n][k]
+};
+constexpr int kLpRows = 64;
+
+tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot, const LpJob* job = nullptr) {
     TVB_TRY(pf_workspace(c));
     float* const kslot = c->kcache + (size_t)slot * c->slot_floats;
     float* const vslot = c->vcache + (size_t)slot * c->slot_floats;
@@ -631,6 +646,34 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot) {
             g.ldy = H;
             TVB_TRY(pf_gemm(g, st));
             if (tp) TVB_TRY(exchange(1, n, lw.ffn_sub_norm, I));
+        }
+        if (job) {
+            // rows p0 + r predicting scored tokens: r in [first - 1 - p0, S - 1 - p0) of this chunk
+            const int r0 = std::max(0, job->first - 1 - p0), r1 = std::min(n, S - 1 - p0);
+            for (int a0 = r0; a0 < r1; a0 += kLpRows) {
+                const int cnt = std::min(kLpRows, r1 - a0);
+                const int j0 = p0 + a0 - (job->first - 1);   // index of the first scored token
+                TVB_TRY(pf_norm_split(c->pf_x + (size_t)a0 * H, c->output_norm, cnt, H, eps, c->pf_xh, c->pf_xl,
+                                      c->pf_exp, st));
+                PfGemm lg;
+                lg.mode = PF_STORE;
+                lg.S = cnt;
+                lg.K = H;
+                lg.xh = c->pf_xh;
+                lg.xl = c->pf_xl;
+                lg.row_exp = c->pf_exp;
+                lg.status = &c->st->status;
+                lg.part = c->pf_part;
+                lg.part_floats = c->pf_part_floats;
+                lg.m[0].w = static_cast<const uint16_t*>(c->tok_embd);
+                lg.m[0].rows = c->V;
+                lg.y = job->logits;
+                lg.ldy = c->V;
+                TVB_TRY(pf_gemm(lg, st));
+                TVB_TRY(logprob_rows(job->logits, cnt, c->V, c->V, job->target + j0, job->k, job->lp + j0,
+                                     job->k ? job->ids + (size_t)j0 * job->k : nullptr,
+                                     job->k ? job->top + (size_t)j0 * job->k : nullptr, st));
+            }
         }
     }
     // output_norm + lm_head + argmax of the last row (the decode step's last
@@ -1179,6 +1222,51 @@ tvb_status tvb_prefill_slot(tvb_context* c, int slot, const int* tokens, int S, 
     if (last_logits) std::memcpy(last_logits, c->h_logit, nl * 4);
     if (argmax_host) *argmax_host = c->h_st->next_token;
     return TVB_OK;
+}
+
+tvb_status tvb_score_logprobs(tvb_context* c, const int* tokens, int T, int start_pos, int k, float* logprobs,
+                              int* top_ids, float* top_logprobs) {
+    TVB_REQUIRE(c && tokens && logprobs, "score_logprobs: null argument");
+    TVB_REQUIRE(T > 0 && T <= c->cfg.max_seq_len, "score_logprobs: T=%d outside (0, %d]", T, c->cfg.max_seq_len);
+    TVB_REQUIRE(k >= 0 && k <= kMaxLogprobsHost && (k == 0 || (top_ids && top_logprobs)),
+                "score_logprobs: k=%d (0 .. %d, with output arrays)", k, kMaxLogprobsHost);
+    TVB_REQUIRE(c->tp_world == 1, "score_logprobs: not built for tensor-parallel contexts");
+    TVB_REQUIRE(pf_batched_supported(c), "score_logprobs: shapes the tensor-core GEMM does not tile");
+    for (int i = 0; i < T; ++i)
+        TVB_REQUIRE(tokens[i] >= 0 && tokens[i] < c->V, "score_logprobs: token[%d]=%d outside vocab", i, tokens[i]);
+    const int first = std::max(1, start_pos);
+    const int n = T - first;
+    TVB_TRY(ensure_graphs(c));
+    TVB_TRY(pf_workspace(c));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    if (n <= 0) return tvb_prefill(c, tokens, T, nullptr, nullptr);
+    // per call: the scored tokens, one logits block, the results
+    const size_t bytes = (size_t)n * 4 + (size_t)kLpRows * c->V * 4 + (size_t)n * 4 + (size_t)n * k * 8;
+    char* ws = nullptr;
+    TVB_CUDA(cudaMallocAsync((void**)&ws, bytes, c->stream));
+    LpJob job;
+    job.first = first;
+    job.k = k;
+    job.target = reinterpret_cast<const int*>(ws);
+    job.logits = reinterpret_cast<float*>(ws + (size_t)n * 4);
+    job.lp = job.logits + (size_t)kLpRows * c->V;
+    job.ids = reinterpret_cast<int*>(job.lp + n);
+    job.top = reinterpret_cast<float*>(job.ids + (size_t)n * k);
+    tvb_status s = TVB_OK;
+    if (cudaMemcpyAsync(ws, tokens + first, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        s = cuda_error(cudaGetLastError(), "score_logprobs: token upload");
+    if (s == TVB_OK) s = prefill_batched(c, tokens, T, 0, &job);
+    if (s == TVB_OK) {
+        cudaMemcpyAsync(logprobs, job.lp, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream);
+        if (k) {
+            cudaMemcpyAsync(top_ids, job.ids, (size_t)n * k * 4, cudaMemcpyDeviceToHost, c->stream);
+            cudaMemcpyAsync(top_logprobs, job.top, (size_t)n * k * 4, cudaMemcpyDeviceToHost, c->stream);
+        }
+    }
+    cudaFreeAsync(ws, c->stream);
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    if (s != TVB_OK) return s;
+    return check_status(c);
 }
 
 tvb_status tvb_decode_batch(tvb_context* c, const int* tokens, const int* positions, int B, float* logits,

@@ -22,12 +22,13 @@
 
 #include <cfloat>
 
-#include "common.cuh"
+#include "sampler.h"
 
 namespace tvb {
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampCand = 1024;
+constexpr int kMaxLogprobs = kMaxLogprobsHost;
 
 struct SampArgs {
     const float* logits;
@@ -227,6 +228,105 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
     }
     __syncthreads();
     if (tid == 0) a.out[b] = s_token;
+}
+
+// ---------------------------------------------------------------------------
+// Log-probabilities of scored tokens (Model::score_logprobs, model.cpp:1746-
+// 1831): per row of logits [n][V], lp = (l - max) - log(sum exp(l - max)),
+// the target token's lp and the k largest lps (descending; equal lps: the
+// smaller index first).  One CTA of 1024 threads per row; the top k by the
+// 8-bit radix select of the sampler on order-preserving keys.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long lp_key(float v, int i) {
+    const unsigned b = __float_as_uint(v);
+    const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);   // float order as unsigned order
+    return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (unsigned)i);   // equal values: smaller index larger
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+logprob_kernel(const float* __restrict__ logits, int V, int ld, const int* __restrict__ target, int k,
+               float* __restrict__ out_lp, int* __restrict__ out_ids, float* __restrict__ out_top) {
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const float* lg = logits + (size_t)r * ld;
+    __shared__ float red_f[32];
+    __shared__ unsigned long long cand[kSampCand];
+    __shared__ int s_keep, s_count;
+    __shared__ unsigned hist[256];
+    float mx = -1e30f;   // model.cpp:1793
+    for (int i = tid; i < V; i += kSampThreads) mx = fmaxf(mx, lg[i]);
+    mx = block_reduce(mx, [](float x, float y) { return fmaxf(x, y); }, red_f);
+    float se = 0.f;
+    for (int i = tid; i < V; i += kSampThreads) se += expf(lg[i] - mx);
+    se = block_reduce(se, [](float x, float y) { return x + y; }, red_f);
+    const float lse = logf(se);
+    auto lp = [&](int i) { return (lg[i] - mx) - lse; };
+    if (tid == 0) out_lp[r] = lp(target[r]);
+    if (k <= 0) return;
+    // the k-th largest key
+    unsigned long long prefix = 0ull, mask = 0ull;
+    int need = k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < V; i += kSampThreads) {
+            const unsigned long long key = lp_key(lp(i), i);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int d = 255;
+            for (; d > 0; --d) {
+                if ((int)hist[d] >= need) break;
+                need -= (int)hist[d];
+            }
+            s_keep = d;
+            s_count = need;
+        }
+        __syncthreads();
+        prefix |= (unsigned long long)s_keep << shift;
+        mask |= 255ull << shift;
+        need = s_count;
+        __syncthreads();
+    }
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += kSampThreads) {
+        const unsigned long long key = lp_key(lp(i), i);
+        if (key >= prefix) {
+            const int at = atomicAdd(&s_count, 1);
+            if (at < kSampCand) cand[at] = key;
+        }
+    }
+    __syncthreads();
+    for (int i = min(s_count, kSampCand) + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
+    __syncthreads();
+    for (int size = 2; size <= kSampCand; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const int i = tid, j = i ^ stride;
+            if (j > i) {
+                const bool desc = (i & size) == 0;
+                const unsigned long long x = cand[i], y = cand[j];
+                if (desc ? (x < y) : (x > y)) {
+                    cand[i] = y;
+                    cand[j] = x;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (tid < k) {
+        const int id = (int)(0xFFFFFFFFu - (unsigned)(cand[tid] & 0xFFFFFFFFu));
+        out_ids[(size_t)r * k + tid] = id;
+        out_top[(size_t)r * k + tid] = lp(id);
+    }
+}
+
+tvb_status logprob_rows(const float* logits, int n, int V, int ld, const int* target, int k, float* out_lp,
+                        int* out_ids, float* out_top, cudaStream_t st) {
+    TVB_REQUIRE(logits && target && out_lp && n > 0 && V > 0 && k >= 0 && k <= kMaxLogprobs && (k == 0 || (out_ids && out_top)),
+                "logprobs: bad arguments (k %d, at most %d)", k, kMaxLogprobs);
+    logprob_kernel<<<n, kSampThreads, 0, st>>>(logits, V, ld, target, k, out_lp, out_ids, out_top);
+    return check_launch("logprob_kernel");
 }
 
 }  // namespace tvb
