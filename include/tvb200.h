@@ -401,6 +401,22 @@ tvb_status tvb_cache_entry(const tvb_cache* cache, int i, tvb_cache_tensor* info
 tvb_status tvb_cache_read(tvb_cache* cache, const char* name, void* dst, uint64_t capacity);
 tvb_status tvb_cache_close(tvb_cache* cache);
 
+/* ---- GGUF ingest -----------------------------------------------------------
+ * gguf_load (src/gguf.cpp:220-249, parse :254-307) reads the whole file into
+ * host memory.  These read only the header and tensor table, then stream one
+ * tensor at a time from the file into device (or host) memory through pinned
+ * staging -- e.g. the I2_S codes and LoRA factors straight into the merge's
+ * inputs.  Sizes as the reference's Tensor (tensor.cpp:108-121): F32, F16,
+ * BF16 and I2_S (32 bytes per 128 weights + the F32 scale). */
+typedef struct tvb_gguf tvb_gguf;
+tvb_status tvb_gguf_open(const char* path, tvb_gguf** out);
+int        tvb_gguf_count(const tvb_gguf* gguf);
+/* Entry i: name (valid while open), ggml type, dims, shape; nbytes 0 for types
+ * this reader does not size. */
+tvb_status tvb_gguf_tensor(const tvb_gguf* gguf, int i, tvb_cache_tensor* info, uint64_t* nbytes);
+tvb_status tvb_gguf_read(tvb_gguf* gguf, const char* name, void* dst, uint64_t capacity);
+tvb_status tvb_gguf_close(tvb_gguf* gguf);
+
 #ifdef __cplusplus
 }
 #endif

@@ -202,6 +202,9 @@ class Reference:
         L.tvref_sample_token.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _i32p,
                                          C.c_int]
         L.tvref_score_logprobs.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, C.c_int, _f32p, _i32p, _f32p]
+        L.tvref_gguf_tensor.restype = C.c_longlong
+        L.tvref_gguf_tensor.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p, C.POINTER(C.c_int),
+                                        C.POINTER(C.c_int), C.POINTER(C.c_longlong)]
         L.tvref_time_decode.restype = C.c_double
         L.tvref_time_decode.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         self.L = L
@@ -540,3 +543,15 @@ def sample_token(logits, temperature=0.8, top_p=0.9, top_k=40, penalty=1.1, seen
     hit = np.nonzero(np.float32(u) <= cdf)[0]
     tok = int(hit[0]) if hit.size else V - 1
     return (tok, cdf) if return_cdf else tok
+
+
+def reference_gguf_tensor(ref, path: str, name: str):
+    """gguf_load's view of one tensor: (ggml type, shape, raw bytes), or None."""
+    t, nd = C.c_int(), C.c_int()
+    shape = (C.c_longlong * 8)()
+    n = ref.L.tvref_gguf_tensor(path.encode(), name.encode(), None, C.byref(t), C.byref(nd), shape)
+    if n < 0:
+        return None
+    out = np.empty(n, np.uint8)
+    ref.L.tvref_gguf_tensor(path.encode(), name.encode(), out.ctypes.data, C.byref(t), C.byref(nd), shape)
+    return t.value, tuple(shape[:nd.value]), out

@@ -336,6 +336,24 @@ int tvref_score_logprobs(tvref_model* h, const int* tokens, int T, int k, int st
     return (int)res.logprobs.size();
 }
 
+// gguf.cpp:220-307 -- gguf_load, then tensor `name` sized as the reference's
+// Tensor (tensor.cpp:108-121) and copied from its data section.  Returns the
+// byte count (out may be null), -1 when absent; type and shape via pointers.
+long long tvref_gguf_tensor(const char* path, const char* name, void* out, int* type, int* n_dims,
+                            long long* shape) {
+    auto g = gguf_load(path);
+    if (!g) return -2;
+    const TensorInfo* ti = g->find_tensor(name);
+    if (!ti) return -1;
+    std::vector<int64_t> sh(ti->shape.begin(), ti->shape.end());
+    Tensor t(sh, ti->type);
+    *type = (int)ti->type;
+    *n_dims = (int)sh.size();
+    for (size_t d = 0; d < sh.size() && d < 8; ++d) shape[d] = sh[d];
+    if (out) std::memcpy(out, g->tensor_data.data() + ti->offset, t.data.size());
+    return (long long)t.data.size();
+}
+
 // Copy one layer's CPU KV cache rows [0, n) (layout [pos][n_kv][hd], F32).
 int tvref_kv_read(tvref_model* h, int layer, int n, float* k, float* v) {
     const auto& c = h->m.config;

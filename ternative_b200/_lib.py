@@ -141,6 +141,11 @@ _SIGS = {
     "tvb_cache_entry": [_P, _I, _P, _P],
     "tvb_cache_read": [_P, C.c_char_p, _P, C.c_uint64],
     "tvb_cache_close": [_P],
+    "tvb_gguf_open": [C.c_char_p, _P],
+    "tvb_gguf_count": [_P],
+    "tvb_gguf_tensor": [_P, _I, _P, _P],
+    "tvb_gguf_read": [_P, C.c_char_p, _P, C.c_uint64],
+    "tvb_gguf_close": [_P],
     "tvb_decode_batch": [_P, _P, _P, _I, _P, _P],
     "tvb_tp_init": [_P, _I, _I, C.POINTER(C.c_void_p)],
     "tvb_tp_set_peers": [_P, C.POINTER(C.c_void_p)],
@@ -155,6 +160,7 @@ _RESTYPES = {
     "tvb_context_stream": C.c_void_p,
     "tvb_kv_capacity": C.c_int,
     "tvb_cache_count": C.c_int,
+    "tvb_gguf_count": C.c_int,
 }
 
 EXPORTED = tuple(_SIGS)

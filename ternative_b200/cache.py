@@ -131,3 +131,40 @@ def model_entries(model) -> List[Entry]:
             else:
                 out.append(Entry(name, GGML_F32, (norm_len(cfg, key),), model.norms[li][key].data_ptr()))
     return out
+
+
+class GGUFFile:
+    """A GGUF v3 file's tensor table (gguf.cpp's parse) and single tensors
+    streamed into host or device buffers (tvb_gguf_*), without reading the
+    whole file into memory as gguf_load does."""
+
+    def __init__(self, path: str):
+        self.lib = load()
+        self.h = C.c_void_p()
+        call("tvb_gguf_open", path.encode(), C.byref(self.h))
+        self.entries = {}
+        for i in range(self.lib.tvb_gguf_count(self.h)):
+            t = CacheTensor()
+            n = C.c_uint64()
+            call("tvb_gguf_tensor", self.h, i, C.byref(t), C.byref(n))
+            self.entries[t.name.decode()] = (t.ggml_type, tuple(t.shape[:t.n_dims]), n.value)
+
+    def read(self, name: str, dst: int, capacity: int) -> None:
+        call("tvb_gguf_read", self.h, name.encode(), dst, capacity)
+
+    def read_numpy(self, name: str) -> np.ndarray:
+        _, _, n = self.entries[name]
+        out = np.empty(n, np.uint8)
+        self.read(name, out.ctypes.data, n)
+        return out
+
+    def close(self):
+        if self.h:
+            self.lib.tvb_gguf_close(self.h)
+            self.h = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()

@@ -138,6 +138,33 @@ tvb_status write_tensor(FILE* f, const void* src, size_t n, Staging& sg) {
     return TVB_OK;
 }
 
+// n bytes from the file's position into dst: host memory directly, device
+// memory through the staging (the upload of chunk i overlaps the read of
+// chunk i + 1).
+tvb_status read_into(FILE* f, void* dst, uint64_t n, const char* name) {
+    if (!on_device(dst)) {
+        if (std::fread(dst, 1, n, f) != n) return tvb::set_error(TVB_ERR_INVALID, "short read of '%s'", name);
+        return TVB_OK;
+    }
+    Staging sg;
+    TVB_TRY(sg.init());
+    char* d = static_cast<char*>(dst);
+    size_t done = 0;
+    int cur = 0;
+    while (done < n) {
+        const size_t len = n - done < kChunk ? n - done : kChunk;
+        TVB_CUDA(cudaEventSynchronize(sg.ev[cur]));   // the buffer's previous upload is done
+        if (std::fread(sg.buf[cur], 1, len, f) != len)
+            return tvb::set_error(TVB_ERR_INVALID, "short read of '%s'", name);
+        TVB_CUDA(cudaMemcpyAsync(d + done, sg.buf[cur], len, cudaMemcpyHostToDevice, sg.st));
+        TVB_CUDA(cudaEventRecord(sg.ev[cur], sg.st));
+        done += len;
+        cur ^= 1;
+    }
+    TVB_CUDA(cudaStreamSynchronize(sg.st));
+    return TVB_OK;
+}
+
 }  // namespace
 
 struct tvb_cache {
@@ -310,33 +337,171 @@ tvb_status tvb_cache_read(tvb_cache* c, const char* name, void* dst, uint64_t ca
                 (unsigned long long)e->nbytes, (unsigned long long)capacity);
     if (std::fseek(c->file.f, (long)(c->hdr.data_offset + e->data_offset), SEEK_SET) != 0)
         return tvb::set_error(TVB_ERR_INVALID, "cache_read: seek failed for '%s'", name);
-    if (!on_device(dst)) {
-        if (std::fread(dst, 1, e->nbytes, c->file.f) != e->nbytes)
-            return tvb::set_error(TVB_ERR_INVALID, "cache_read: short read of '%s'", name);
-        return TVB_OK;
-    }
-    // file -> pinned chunk -> device, the upload of chunk i overlapping the read of chunk i + 1
-    Staging sg;
-    TVB_TRY(sg.init());
-    char* d = static_cast<char*>(dst);
-    size_t done = 0;
-    int cur = 0;
-    while (done < e->nbytes) {
-        const size_t len = e->nbytes - done < kChunk ? e->nbytes - done : kChunk;
-        TVB_CUDA(cudaEventSynchronize(sg.ev[cur]));   // the buffer's previous upload is done
-        if (std::fread(sg.buf[cur], 1, len, c->file.f) != len)
-            return tvb::set_error(TVB_ERR_INVALID, "cache_read: short read of '%s'", name);
-        TVB_CUDA(cudaMemcpyAsync(d + done, sg.buf[cur], len, cudaMemcpyHostToDevice, sg.st));
-        TVB_CUDA(cudaEventRecord(sg.ev[cur], sg.st));
-        done += len;
-        cur ^= 1;
-    }
-    TVB_CUDA(cudaStreamSynchronize(sg.st));
-    return TVB_OK;
+    return read_into(c->file.f, dst, e->nbytes, name);
 }
 
 tvb_status tvb_cache_close(tvb_cache* c) {
     delete c;
+    return TVB_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// GGUF ingest: the tensor table of a GGUF v3 file (gguf.cpp's
+// gguf_parse_buffer: header, metadata key/values, tensor infos, the data
+// section at general.alignment) read without loading the file, and single
+// tensors streamed from the file into device (or host) memory through the
+// same pinned staging -- instead of gguf_load's copy of the whole file into
+// host memory before anything reaches the GPU.  Byte sizes follow the
+// reference's Tensor (tensor.cpp:108-121): F32 4, F16 / BF16 2 bytes per
+// element, I2_S 32 bytes per 128 weights plus the F32 scale.
+// ---------------------------------------------------------------------------
+struct tvb_gguf {
+    File file;
+    std::string path;
+    struct Info {
+        std::string name;
+        uint32_t type;
+        std::vector<uint64_t> shape;
+        uint64_t offset, nbytes;
+    };
+    std::vector<Info> tensors;
+    uint64_t data_offset = 0;
+    uint64_t file_size = 0;
+};
+
+namespace {
+
+bool rd(FILE* f, void* p, size_t n) { return std::fread(p, 1, n, f) == n; }
+
+bool rd_string(FILE* f, std::string* out) {
+    uint64_t n = 0;
+    if (!rd(f, &n, 8) || n > (1ull << 30)) return false;
+    if (!out) return std::fseek(f, (long)n, SEEK_CUR) == 0;
+    out->resize(n);
+    return n == 0 || rd(f, &(*out)[0], n);
+}
+
+// Skip (or read, for the one key the layout needs) one metadata value of type t.
+bool skip_value(FILE* f, uint32_t t, int depth, uint64_t* u32_out) {
+    static const int sizes[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    if (t > 12 || depth > 4) return false;
+    if (t == 8) return rd_string(f, nullptr);
+    if (t == 9) {
+        uint32_t et = 0;
+        uint64_t n = 0;
+        if (!rd(f, &et, 4) || !rd(f, &n, 8) || et > 12) return false;
+        if (et != 8 && et != 9) return std::fseek(f, (long)(n * (uint64_t)sizes[et]), SEEK_CUR) == 0;
+        for (uint64_t i = 0; i < n; ++i)
+            if (!skip_value(f, et, depth + 1, nullptr)) return false;
+        return true;
+    }
+    if (u32_out && t == 4) {
+        uint32_t v = 0;
+        if (!rd(f, &v, 4)) return false;
+        *u32_out = v;
+        return true;
+    }
+    return std::fseek(f, sizes[t], SEEK_CUR) == 0;
+}
+
+bool gguf_bytes(uint32_t type, uint64_t n, uint64_t* out) {
+    switch (type) {
+        case 0: *out = n * 4; return true;                       // F32
+        case 1: case 30: *out = n * 2; return true;              // F16, BF16
+        case 36: *out = (n + 127) / 128 * 32 + 4; return true;   // I2_S: codes + F32 scale
+        default: return false;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+tvb_status tvb_gguf_open(const char* path, tvb_gguf** out) {
+    TVB_REQUIRE(path && out, "gguf_open: null argument");
+    *out = nullptr;
+    auto* g = new (std::nothrow) tvb_gguf();
+    if (!g) return tvb::set_error(TVB_ERR_OOM, "gguf_open: host allocation");
+    auto fail = [&](const char* why) {
+        delete g;
+        return tvb::set_error(TVB_ERR_INVALID, "gguf_open: %s: %s", path, why);
+    };
+    g->path = path;
+    g->file.f = std::fopen(path, "rb");
+    if (!g->file.f) return fail("cannot open");
+    FILE* f = g->file.f;
+    std::fseek(f, 0, SEEK_END);
+    g->file_size = (uint64_t)std::ftell(f);
+    std::fseek(f, 0, SEEK_SET);
+    uint32_t magic = 0, version = 0;
+    uint64_t n_tensors = 0, n_kv = 0;
+    if (!rd(f, &magic, 4) || magic != 0x46554747u) return fail("not a GGUF file");
+    if (!rd(f, &version, 4) || version != 3) return fail("GGUF version is not 3");
+    if (!rd(f, &n_tensors, 8) || !rd(f, &n_kv, 8) || n_tensors > 1000000) return fail("bad header");
+    uint64_t alignment = 32;
+    for (uint64_t i = 0; i < n_kv; ++i) {
+        std::string key;
+        uint32_t t = 0;
+        if (!rd_string(f, &key) || !rd(f, &t, 4)) return fail("truncated metadata");
+        uint64_t v = 0;
+        const bool want = key == "general.alignment";
+        if (!skip_value(f, t, 0, want ? &v : nullptr)) return fail("bad metadata value");
+        if (want && t == 4 && v > 0) alignment = v;
+    }
+    g->tensors.resize(n_tensors);
+    for (auto& ti : g->tensors) {
+        uint32_t nd = 0;
+        if (!rd_string(f, &ti.name) || !rd(f, &nd, 4) || nd > 8) return fail("bad tensor info");
+        ti.shape.resize(nd);
+        uint64_t n = 1;
+        for (auto& d : ti.shape) {
+            if (!rd(f, &d, 8)) return fail("bad tensor info");
+            n *= d;
+        }
+        if (!rd(f, &ti.type, 4) || !rd(f, &ti.offset, 8)) return fail("bad tensor info");
+        if (!gguf_bytes(ti.type, n, &ti.nbytes)) ti.nbytes = 0;   // a type this reader does not size
+    }
+    const uint64_t pos = (uint64_t)std::ftell(f);
+    g->data_offset = (pos + alignment - 1) / alignment * alignment;
+    *out = g;
+    return TVB_OK;
+}
+
+int tvb_gguf_count(const tvb_gguf* g) { return g ? (int)g->tensors.size() : 0; }
+
+tvb_status tvb_gguf_tensor(const tvb_gguf* g, int i, tvb_cache_tensor* info, uint64_t* nbytes) {
+    TVB_REQUIRE(g && info && i >= 0 && i < (int)g->tensors.size(), "gguf_tensor: bad arguments");
+    const auto& t = g->tensors[i];
+    std::memset(info, 0, sizeof(*info));
+    info->name = t.name.c_str();
+    info->ggml_type = (int)t.type;
+    info->n_dims = (int)std::min<size_t>(t.shape.size(), 4);
+    for (int d = 0; d < info->n_dims; ++d) info->shape[d] = (int64_t)t.shape[d];
+    if (nbytes) *nbytes = t.nbytes;
+    return TVB_OK;
+}
+
+tvb_status tvb_gguf_read(tvb_gguf* g, const char* name, void* dst, uint64_t capacity) {
+    TVB_REQUIRE(g && name && dst, "gguf_read: null argument");
+    const tvb_gguf::Info* t = nullptr;
+    for (const auto& x : g->tensors)
+        if (x.name == name) t = &x;
+    TVB_REQUIRE(t, "gguf_read: no tensor '%s' in %s", name, g->path.c_str());
+    TVB_REQUIRE(t->nbytes > 0, "gguf_read: '%s' has ggml type %u (F32, F16, BF16 and I2_S are read)", name,
+                t->type);
+    TVB_REQUIRE(capacity >= t->nbytes, "gguf_read: '%s' needs %llu bytes, destination has %llu", name,
+                (unsigned long long)t->nbytes, (unsigned long long)capacity);
+    TVB_REQUIRE(g->data_offset + t->offset + t->nbytes <= g->file_size, "gguf_read: '%s' runs past the file end",
+                name);
+    if (std::fseek(g->file.f, (long)(g->data_offset + t->offset), SEEK_SET) != 0)
+        return tvb::set_error(TVB_ERR_INVALID, "gguf_read: seek failed for '%s'", name);
+    return read_into(g->file.f, dst, t->nbytes, name);
+}
+
+tvb_status tvb_gguf_close(tvb_gguf* g) {
+    delete g;
     return TVB_OK;
 }
 
