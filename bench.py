@@ -422,6 +422,176 @@ def gemv_tp_sweep(be, m, cfg, stream, world, rank, hbm):
     return out
 
 
+def write_gguf_i2s(path, cfg, layers, rank, rng):
+    """A GGUF v3 file holding the I2_S projections of `layers` layers (random
+    codes, F32 scale after each) and their rank-`rank` F32 lora_a / lora_b,
+    data section at the default 32-byte alignment.  Returns its tensor names."""
+    import struct
+    from ternative_b200.model import PROJ, proj_shape
+    tensors = []
+    for li in range(layers):
+        for n in PROJ:
+            N, K = proj_shape(cfg, n)
+            codes = rng.integers(0, 256, K * N // 4, dtype=np.uint8).tobytes() + struct.pack("<f", 0.02)
+            tensors.append((f"blk.{li}.{n}.weight", 36, (K, N), codes))
+            tensors.append((f"blk.{li}.{n}.lora_a", 0, (K, rank),
+                            rng.standard_normal(rank * K, dtype=np.float32).tobytes()))
+            tensors.append((f"blk.{li}.{n}.lora_b", 0, (rank, N),
+                            rng.standard_normal(rank * N, dtype=np.float32).tobytes()))
+
+    def s(b):
+        return struct.pack("<Q", len(b)) + b
+    head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), 1) + s(b"general.architecture") \
+        + struct.pack("<I", 8) + s(b"bitnet")
+    off = 0
+    for name, t, shape, data in tensors:
+        head += s(name.encode()) + struct.pack("<I", len(shape)) + b"".join(struct.pack("<Q", d) for d in shape)
+        head += struct.pack("<IQ", t, off)
+        off += (len(data) + 31) // 32 * 32
+    with open(path, "wb") as f:
+        f.write(head + bytes((-len(head)) % 32))
+        for _, _, _, data in tensors:
+            f.write(data + bytes((-len(data)) % 32))
+    return [t[0] for t in tensors]
+
+
+def serving_rows(be, m, cfg, stream, rng, cpu_seconds):
+    """The rows either side of the decode path on the 2B model: the device
+    sampler over 8 rows, log-probabilities of a 512-token sequence, the
+    merged-weight cache (.tvcache) and GGUF ingest into device memory, each
+    beside the reference's own CPU code for the same work where that runs
+    here (oracle/_ref: sample_token, gguf_load)."""
+    import ctypes as C
+    import shutil
+    import tempfile
+    import torch
+    from ternative_b200 import cache as tc
+    from ternative_b200 import load
+    from ternative_b200._lib import SamplerConfig
+
+    def ev_time(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {}
+    lib = load()
+    # ---- sampler: 8 rows of vocab logits, temperature 0.8, top-p 0.9, top-k 40,
+    # repetition penalty 1.1 over 64 seen tokens per row
+    B, V, NS = 8, cfg.vocab_size, 64
+    with torch.cuda.stream(stream):
+        lg = torch.randn(B, V, device="cuda") * 3
+        seen = torch.from_numpy(rng.integers(0, V, (B, NS)).astype(np.int32)).cuda()
+        n_seen = torch.full((B,), NS, dtype=torch.int32, device="cuda")
+        u = torch.rand(B, device="cuda")
+        tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    sc = SamplerConfig(0.8, 0.9, 40, 1.1)
+
+    def sample():
+        st = lib.tvb_sample(lg.data_ptr(), B, V, V, C.byref(sc), seen.data_ptr(), n_seen.data_ptr(), NS,
+                            u.data_ptr(), tok.data_ptr(), be.stream)
+        if st != 0:
+            raise RuntimeError(f"tvb_sample status {st}")
+    us = ev_time(sample, 50) * 1e3
+    out["sampler"] = {"workload": f"{B} rows x {V} logits, T 0.8, top-p 0.9, top-k 40, penalty 1.1 "
+                                  f"over {NS} seen tokens", "us_per_call": us, "rows_per_s": B / (us * 1e-6),
+                      "logit_GB/s": B * V * 4 / (us * 1e-6) / 1e9}
+    try:
+        from oracle.oracle import Reference
+        ref = Reference()
+        h_lg = lg.cpu().numpy()
+        h_seen = seen.cpu().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < min(2.0, cpu_seconds):
+            for b in range(B):
+                ref.L.tvref_sample_token(h_lg[b], V, 0.8, 0.9, 40, 1.1, h_seen[b], NS)
+            n += B
+        out["sampler"]["cpu_baseline"] = {
+            "us_per_row": (time.perf_counter() - t0) / n * 1e6, "cores": 1, "kind": "reference",
+            "sample": f"{n} rows through sample_token (sampler.cpp) on host logits, no D2H copy counted"}
+    except Exception as e:
+        out["sampler"]["cpu_baseline"] = {"unavailable": repr(e)}
+
+    # ---- log-probabilities: one 512-token sequence, top 5 per position, through
+    # the C ABI (H2D tokens, D2H results)
+    T = min(512, cfg.max_prefill, cfg.max_seq_len)
+    toks = rng.integers(0, V, T).astype(np.int32)
+    ms = ev_time(lambda: be.score_logprobs(toks, k=5), 3)
+    out["logprobs"] = {"workload": f"{T}-token sequence, top 5 per position", "ms": ms,
+                       "scored_tok_s": (T - 1) / (ms * 1e-3)}
+
+    tmp = tempfile.mkdtemp(prefix="tvb_bench_")
+    try:
+        # ---- .tvcache of the first 4 layers' merged tensors (+ embedding, norm):
+        # write from device memory, then read back into device buffers; the file is in
+        # the page cache on read
+        ents = tc.model_entries(m)
+        ents = [e for e in ents if not e.name.startswith("blk.") or int(e.name.split(".")[1]) < 4]
+        path = os.path.join(tmp, "m.tvcache")
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tc.write(path, tc.make_key(), ents)
+        wsec = time.perf_counter() - t0
+        nbytes = os.path.getsize(path)
+        with tc.CacheFile(path) as f:
+            bufs = {n: torch.empty(max(1, b), dtype=torch.uint8, device="cuda") for n, (_, _, b) in f.entries.items()}
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for n, (_, _, b) in f.entries.items():
+                f.read(n, bufs[n].data_ptr(), b)
+            torch.cuda.synchronize()
+            rsec = time.perf_counter() - t0
+        del bufs
+        out["tvcache"] = {"workload": f"{len(ents)} merged tensors (embedding, output norm, layers 0-3), "
+                                      f"{nbytes / 1e9:.2f} GB file", "write_GB/s": nbytes / wsec / 1e9,
+                          "read_to_device_GB/s": nbytes / rsec / 1e9}
+        os.remove(path)
+
+        # ---- GGUF ingest: I2_S + LoRA (rank 16) of all layers into device memory
+        gpath = os.path.join(tmp, "m.gguf")
+        names = write_gguf_i2s(gpath, cfg, cfg.num_layers, 16, rng)
+        gbytes = os.path.getsize(gpath)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with tc.GGUFFile(gpath) as g:
+            total = sum(b for _, _, b in g.entries.values())
+            pool = torch.empty(total + 256 * len(names), dtype=torch.uint8, device="cuda")
+            off = 0
+            for n in names:
+                b = g.entries[n][2]
+                g.read(n, pool.data_ptr() + off, b)
+                off += (b + 255) // 256 * 256
+            torch.cuda.synchronize()
+        gsec = time.perf_counter() - t0
+        del pool
+        out["gguf_ingest"] = {"workload": f"{len(names)} tensors (I2_S projections of {cfg.num_layers} layers "
+                                          f"+ rank-16 F32 LoRA), {gbytes / 1e9:.2f} GB file in the page cache",
+                              "seconds": gsec, "GB/s_to_device": total / gsec / 1e9}
+        try:
+            t0 = time.perf_counter()
+            reference_gguf_load = ref.L.tvref_gguf_tensor
+            t = C.c_int()
+            nd = C.c_int()
+            shp = (C.c_longlong * 8)()
+            reference_gguf_load(gpath.encode(), names[0].encode(), None, C.byref(t), C.byref(nd), shp)
+            out["gguf_ingest"]["cpu_baseline"] = {
+                "seconds": time.perf_counter() - t0, "cores": 1, "kind": "reference",
+                "sample": "gguf_load (gguf.cpp) of the same file into host memory, before any upload"}
+        except Exception as e:
+            out["gguf_ingest"]["cpu_baseline"] = {"unavailable": repr(e)}
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return out
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -795,6 +965,13 @@ def run_ours(args, world, rank, local):
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                    "sample": f"unavailable: {e!r}"}
 
+    serving = None
+    if world == 1 and not args.no_serving:
+        try:
+            serving = serving_rows(be, m, cfg, stream, rng, args.cpu_seconds)
+        except Exception as e:   # reported, not fatal to the headline line
+            serving = {"unavailable": repr(e)}
+
     tp8 = None
     if not args.no_tp:
         try:
@@ -811,6 +988,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps,   # one decode_step_kernel launch per token
             "clocks": clk.report(), "merge": merge, "prefill": prefill, "mixed_offload": mixed, "tp_8b": tp8,
+            "serving_rows": serving,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -828,6 +1006,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-serving", action="store_true")
     ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill"], default=None,
                     help="profiling: run only W+K launches of one part, print nothing")
     ap.add_argument("--layers", type=int, default=0,

@@ -28,6 +28,8 @@ namespace tvb {
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampCand = 1024;
+constexpr int kSampPer = 4;                         // entries per thread in a step-7 tile
+constexpr int kSampTile = kSampThreads * kSampPer;
 constexpr int kMaxLogprobs = kMaxLogprobsHost;
 
 struct SampArgs {
@@ -77,6 +79,9 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
     __shared__ unsigned long long cand[kSampCand];
     __shared__ int s_count, s_keep, s_token;
     __shared__ unsigned hist[256];
+    __shared__ float tile_v[kSampTile];
+    __shared__ int tile_i[kSampTile];
+    __shared__ int warp_cnt[32];
 
     // 1-2. temperature, then the repetition penalty on first occurrences
     const bool temp = a.temperature > 0.0f && a.temperature != 1.0f;
@@ -118,9 +123,17 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
         for (int shift = 56; shift >= 0; shift -= 8) {
             for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0u;
             __syncthreads();
-            for (int i = tid; i < V; i += kSampThreads) {
-                const unsigned long long k = samp_key(p[i], i);
-                if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            // warp-aggregated counts: the probabilities crowd into few bins
+            for (int base = 0; base < V; base += kSampThreads) {
+                const int i = base + tid;
+                const unsigned long long k = i < V ? samp_key(p[i], i) : 0ull;
+                const bool hit = i < V && (k & mask) == prefix;
+                const unsigned act = __ballot_sync(0xffffffffu, hit);
+                if (hit) {
+                    const unsigned bin = (unsigned)(k >> shift) & 255u;
+                    const unsigned peers = __match_any_sync(act, bin);
+                    if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+                }
             }
             __syncthreads();
             if (tid == 0) {
@@ -209,25 +222,74 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
     }
     for (int i = tid; i < V; i += kSampThreads) p[i] = (float)((double)p[i] / s2);
     __syncthreads();
-    // 7. running F32 sum in index order; zeros leave it unchanged, so only the
-    //    nonzero entries (in index order) are visited when a filter ran
-    if (tid == 0) {
-        const float u = a.u[b];
-        float acc = 0.0f;
-        int tok = u <= 0.0f ? 0 : V - 1;   // u == 0: index 0 (its running sum is >= 0)
-        for (int i = 0; i < V && u > 0.0f; ++i) {
-            const float v = p[i];
-            if (v == 0.0f) continue;
-            acc += v;
-            if (u <= acc) {
-                tok = i;
-                break;
+    // 7. running F32 sum in index order, the reference's sequential loop.
+    //    Zeros leave it unchanged, so each tile of kSampTile entries is
+    //    compacted (block scan) to its nonzero entries in index order and
+    //    thread 0 continues the sum over those from shared memory.
+    const float u = a.u[b];
+    if (u <= 0.0f) {   // index 0: its running sum is >= 0
+        if (tid == 0) a.out[b] = 0;
+        return;
+    }
+    const int lane = tid & 31, warp = tid >> 5;
+    float acc = 0.0f;   // thread 0's running sum
+    int tok = V - 1;
+    if (tid == 0) s_token = -1;
+    for (int base = 0; base < V; base += kSampTile) {
+        float v[kSampPer];
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < kSampPer; ++j) {
+            const int i = base + tid * kSampPer + j;
+            v[j] = i < V ? p[i] : 0.0f;
+            c += v[j] != 0.0f;
+        }
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) warp_cnt[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const int w = warp_cnt[lane];
+            int wi = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += t;
+            }
+            warp_cnt[lane] = wi - w;
+            if (lane == 31) s_count = wi;
+        }
+        __syncthreads();
+        int at = warp_cnt[warp] + incl - c;
+#pragma unroll
+        for (int j = 0; j < kSampPer; ++j)
+            if (v[j] != 0.0f) {
+                tile_v[at] = v[j];
+                tile_i[at] = base + tid * kSampPer + j;
+                ++at;
+            }
+        __syncthreads();
+        if (tid == 0) {
+            const int n = s_count;
+            for (int m = 0; m < n; ++m) {
+                acc += tile_v[m];
+                if (u <= acc) {
+                    s_token = tile_i[m];
+                    break;
+                }
             }
         }
-        s_token = tok;
+        __syncthreads();
+        if (s_token >= 0) {
+            tok = s_token;
+            break;
+        }
     }
-    __syncthreads();
-    if (tid == 0) a.out[b] = s_token;
+    if (tid == 0) a.out[b] = tok;
 }
 
 // ---------------------------------------------------------------------------

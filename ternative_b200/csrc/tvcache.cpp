@@ -140,13 +140,13 @@ tvb_status write_tensor(FILE* f, const void* src, size_t n, Staging& sg) {
 
 // n bytes from the file's position into dst: host memory directly, device
 // memory through the staging (the upload of chunk i overlaps the read of
-// chunk i + 1).
-tvb_status read_into(FILE* f, void* dst, uint64_t n, const char* name) {
+// chunk i + 1).  The staging belongs to the open file and is pinned once, on
+// its first device read.
+tvb_status read_into(FILE* f, void* dst, uint64_t n, const char* name, Staging& sg) {
     if (!on_device(dst)) {
         if (std::fread(dst, 1, n, f) != n) return tvb::set_error(TVB_ERR_INVALID, "short read of '%s'", name);
         return TVB_OK;
     }
-    Staging sg;
     TVB_TRY(sg.init());
     char* d = static_cast<char*>(dst);
     size_t done = 0;
@@ -168,6 +168,7 @@ tvb_status read_into(FILE* f, void* dst, uint64_t n, const char* name) {
 }  // namespace
 
 struct tvb_cache {
+    Staging sg;   // destroyed after the file: declared first
     File file;
     FileHeader hdr;
     std::vector<FileTensor> table;
@@ -337,7 +338,7 @@ tvb_status tvb_cache_read(tvb_cache* c, const char* name, void* dst, uint64_t ca
                 (unsigned long long)e->nbytes, (unsigned long long)capacity);
     if (std::fseek(c->file.f, (long)(c->hdr.data_offset + e->data_offset), SEEK_SET) != 0)
         return tvb::set_error(TVB_ERR_INVALID, "cache_read: seek failed for '%s'", name);
-    return read_into(c->file.f, dst, e->nbytes, name);
+    return read_into(c->file.f, dst, e->nbytes, name, c->sg);
 }
 
 tvb_status tvb_cache_close(tvb_cache* c) {
@@ -358,6 +359,7 @@ tvb_status tvb_cache_close(tvb_cache* c) {
 // element, I2_S 32 bytes per 128 weights plus the F32 scale.
 // ---------------------------------------------------------------------------
 struct tvb_gguf {
+    Staging sg;
     File file;
     std::string path;
     struct Info {
@@ -497,7 +499,7 @@ tvb_status tvb_gguf_read(tvb_gguf* g, const char* name, void* dst, uint64_t capa
                 name);
     if (std::fseek(g->file.f, (long)(g->data_offset + t->offset), SEEK_SET) != 0)
         return tvb::set_error(TVB_ERR_INVALID, "gguf_read: seek failed for '%s'", name);
-    return read_into(g->file.f, dst, t->nbytes, name);
+    return read_into(g->file.f, dst, t->nbytes, name, g->sg);
 }
 
 tvb_status tvb_gguf_close(tvb_gguf* g) {
