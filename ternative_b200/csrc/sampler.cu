@@ -22,9 +22,13 @@
 
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "sampler.h"
 
 namespace tvb {
+
+namespace cg = cooperative_groups;
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampCand = 1024;
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
     for (int i = tid; i < V / 32 + 1; i += kSampThreads) bits[i] = 0u;
     __syncthreads();
     if (a.penalty > 1.0f) {
-        const int n = a.n_seen[b];
+        const int n = min(a.n_seen[b], a.max_seen);
         // distinct tokens only: the first thread to mark a token divides it
         for (int j = tid; j < n; j += kSampThreads) {
             const int t = a.seen[(size_t)b * a.max_seen + j];
@@ -293,6 +297,280 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
+// The same steps with one thread-block cluster of kClu CTAs per row: each CTA
+// keeps a slice of S probabilities in shared memory for every pass, and the
+// row-wide values (max, sums, the radix histograms, the top-p candidates) are
+// combined through distributed shared memory in rank order, so every CTA of
+// the cluster derives the same thresholds.  Step 7's sequential sum hands its
+// F32 running value from CTA to CTA in index order.  No work buffer; rows of
+// up to kClu * kCluMaxSlice entries (the single-CTA kernel above takes longer
+// rows).
+// ---------------------------------------------------------------------------
+constexpr int kClu = 8;
+constexpr int kCluMaxSlice = 24576;
+
+template <typename T, typename Op>
+__device__ __forceinline__ T cluster_combine(cg::cluster_group& cl, T v, T* slot, T* all, Op op) {
+    if (threadIdx.x == 0) *slot = v;
+    cl.sync();
+    if (threadIdx.x == 0) {
+        T acc = *cl.map_shared_rank(slot, 0);
+        for (int q = 1; q < kClu; ++q) acc = op(acc, *cl.map_shared_rank(slot, q));
+        *all = acc;
+    }
+    cl.sync();   // also: every remote read of `slot` is done before it is written again
+    return *all;
+}
+
+__global__ void __cluster_dims__(kClu, 1, 1) __launch_bounds__(kSampThreads)
+sample_cluster_kernel(const __grid_constant__ SampArgs a, int S) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int r = (int)cl.block_rank(), b = blockIdx.y, tid = threadIdx.x, V = a.vocab;
+    const int lo = r * S;
+    const int n = max(0, min(V, lo + S) - lo);   // this CTA's entries [lo, lo + n)
+    extern __shared__ __align__(16) unsigned char samp_smem[];
+    float* p = reinterpret_cast<float*>(samp_smem);   // [S]
+    int* ix = reinterpret_cast<int*>(p + S);           // [S] step-7 compaction
+    unsigned* bits = reinterpret_cast<unsigned*>(ix + S);   // [S / 32 + 1]
+    __shared__ double red_d[32], x_d, all_d;
+    __shared__ float red_f[32], x_f, all_f;
+    __shared__ unsigned long long red_k[32], x_k, all_k;
+    __shared__ unsigned long long loc[kSampCand], cand[kSampCand];
+    __shared__ unsigned hist[2][256], comb[256];
+    __shared__ int cnt_all[kClu], cnt_tile[32];
+    __shared__ int s_loc, s_keep, s_need, s_nz, s_done;
+    __shared__ float s_acc;
+    const float* lg = a.logits + (size_t)b * a.ld + lo;
+
+    // 1-2. temperature, then the repetition penalty on first occurrences (each
+    //      CTA marks the seen tokens of its slice)
+    const bool temp = a.temperature > 0.0f && a.temperature != 1.0f;
+    for (int i = tid; i < n; i += kSampThreads) p[i] = temp ? lg[i] / a.temperature : lg[i];
+    for (int i = tid; i < S / 32 + 1; i += kSampThreads) bits[i] = 0u;
+    if (tid == 0) {
+        s_acc = 0.0f;
+        s_done = 0;
+    }
+    __syncthreads();
+    if (a.penalty > 1.0f) {
+        const int ns = min(a.n_seen[b], a.max_seen);
+        for (int j = tid; j < ns; j += kSampThreads) {
+            const int t = a.seen[(size_t)b * a.max_seen + j] - lo;
+            if (t < 0 || t >= n) continue;
+            const unsigned m = 1u << (t & 31);
+            if (!(atomicOr(&bits[t >> 5], m) & m)) p[t] = p[t] / a.penalty;
+        }
+        __syncthreads();
+    }
+    // 3. softmax over the row
+    float mx = -FLT_MAX;
+    for (int i = tid; i < n; i += kSampThreads) mx = fmaxf(mx, p[i]);
+    mx = block_reduce(mx, [](float x, float y) { return fmaxf(x, y); }, red_f);
+    mx = cluster_combine(cl, mx, &x_f, &all_f, [](float x, float y) { return fmaxf(x, y); });
+    double sum = 0.0;
+    for (int i = tid; i < n; i += kSampThreads) {
+        const float e = expf(p[i] - mx);
+        p[i] = e;
+        sum += (double)e;
+    }
+    sum = block_reduce(sum, [](double x, double y) { return x + y; }, red_d);
+    sum = cluster_combine(cl, sum, &x_d, &all_d, [](double x, double y) { return x + y; });
+    for (int i = tid; i < n; i += kSampThreads) p[i] = (float)((double)p[i] / sum);
+    __syncthreads();
+
+    const bool topk = a.top_k > 0 && a.top_k < V;
+    const bool topp = a.top_p > 0.0f && a.top_p < 1.0f;
+    if (topk) {
+        // 4. radix select of the k-th largest key over the cluster's histograms
+        unsigned long long prefix = 0ull, mask = 0ull;
+        int need = a.top_k;
+        int par = 0;
+        for (int shift = 56; shift >= 0; shift -= 8, par ^= 1) {
+            unsigned* h = hist[par];   // rewritten two passes later, after a cluster barrier
+            for (int i = tid; i < 256; i += kSampThreads) h[i] = 0u;
+            __syncthreads();
+            for (int base = 0; base < n; base += kSampThreads) {
+                const int i = base + tid;
+                const unsigned long long k = i < n ? samp_key(p[i], lo + i) : 0ull;
+                const bool hit = i < n && (k & mask) == prefix;
+                const unsigned act = __ballot_sync(0xffffffffu, hit);
+                if (hit) {
+                    const unsigned bin = (unsigned)(k >> shift) & 255u;
+                    const unsigned peers = __match_any_sync(act, bin);
+                    if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&h[bin], (unsigned)__popc(peers));
+                }
+            }
+            cl.sync();
+            if (tid < 256) {
+                unsigned c = 0u;
+                for (int q = 0; q < kClu; ++q) c += cl.map_shared_rank(h, q)[tid];
+                comb[tid] = c;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                int d = 255;
+                for (; d > 0; --d) {
+                    if ((int)comb[d] >= need) break;
+                    need -= (int)comb[d];
+                }
+                s_keep = d;
+                s_need = need;
+            }
+            __syncthreads();
+            prefix |= (unsigned long long)s_keep << shift;
+            mask |= 255ull << shift;
+            need = s_need;
+            __syncthreads();
+        }
+        for (int i = tid; i < n; i += kSampThreads)
+            if (samp_key(p[i], lo + i) < prefix) p[i] = 0.0f;
+        __syncthreads();
+    }
+    if (topp) {
+        // 5. every CTA gathers the cluster's kept p > 0 (at most top_k <= 1024)
+        //    in rank order and sorts them
+        if (tid == 0) s_loc = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += kSampThreads)
+            if (p[i] > 0.0f) {
+                const int at = atomicAdd(&s_loc, 1);
+                if (at < kSampCand) loc[at] = samp_key(p[i], lo + i);
+            }
+        cl.sync();
+        if (tid < kClu) cnt_all[tid] = min(*cl.map_shared_rank(&s_loc, tid), kSampCand);
+        __syncthreads();
+        int total = 0;
+        for (int q = 0; q < kClu; ++q) {
+            const unsigned long long* rl = cl.map_shared_rank(loc, q);
+            for (int i = tid; i < cnt_all[q] && total + i < kSampCand; i += kSampThreads) cand[total + i] = rl[i];
+            total += cnt_all[q];
+        }
+        total = min(total, kSampCand);
+        for (int i = total + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
+        cl.sync();   // the remote reads of loc / s_loc are done
+        for (int size = 2; size <= kSampCand; size <<= 1) {
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const int i = tid, j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long x = cand[i], y = cand[j];
+                    if (desc ? (x < y) : (x > y)) {
+                        cand[i] = y;
+                        cand[j] = x;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (tid == 0) {
+            float cum = 0.0f;
+            int m = 0;
+            while (m < total) {
+                cum += __uint_as_float((unsigned)(cand[m] >> 32));
+                ++m;
+                if (cum >= a.top_p) break;
+            }
+            s_keep = m;
+        }
+        __syncthreads();
+        const int m = s_keep;
+        const unsigned long long kmin = m > 0 ? cand[m - 1] : ~0ull;
+        for (int i = tid; i < n; i += kSampThreads)
+            if (p[i] > 0.0f && samp_key(p[i], lo + i) < kmin) p[i] = 0.0f;
+        __syncthreads();
+    }
+    // 6. renormalise
+    double s2 = 0.0;
+    for (int i = tid; i < n; i += kSampThreads) s2 += (double)p[i];
+    s2 = block_reduce(s2, [](double x, double y) { return x + y; }, red_d);
+    s2 = cluster_combine(cl, s2, &x_d, &all_d, [](double x, double y) { return x + y; });
+    if (s2 <= 0.0) {
+        unsigned long long best = 0ull;
+        for (int i = tid; i < n; i += kSampThreads) {
+            const unsigned ob = __float_as_uint(lg[i]);
+            const unsigned ord = (ob & 0x80000000u) ? ~ob : (ob | 0x80000000u);
+            const unsigned long long k = ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (unsigned)(lo + i));
+            best = k > best ? k : best;
+        }
+        auto kmax = [](unsigned long long x, unsigned long long y) { return x > y ? x : y; };
+        best = block_reduce(best, kmax, red_k);
+        best = cluster_combine(cl, best, &x_k, &all_k, kmax);
+        if (r == 0 && tid == 0) a.out[b] = (int)(0xFFFFFFFFu - (unsigned)(best & 0xFFFFFFFFu));
+        return;
+    }
+    const float u = a.u[b];
+    if (u <= 0.0f) {   // index 0: its running sum is >= 0
+        if (r == 0 && tid == 0) a.out[b] = 0;
+        return;
+    }
+    // 7. this slice's nonzero p / s2 compacted in index order (in place: a tile
+    //    is read into registers before any of it is overwritten)
+    const int lane = tid & 31, warp = tid >> 5;
+    int off = 0;
+    for (int base = 0; base < n; base += kSampTile) {
+        float v[kSampPer];
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < kSampPer; ++j) {
+            const int i = base + tid * kSampPer + j;
+            v[j] = i < n ? (float)((double)p[i] / s2) : 0.0f;
+            c += v[j] != 0.0f;
+        }
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) cnt_tile[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const int w = cnt_tile[lane];
+            int wi = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += t;
+            }
+            cnt_tile[lane] = wi - w;
+            if (lane == 31) s_nz = wi;
+        }
+        __syncthreads();
+        int at = off + cnt_tile[warp] + incl - c;
+#pragma unroll
+        for (int j = 0; j < kSampPer; ++j)
+            if (v[j] != 0.0f) {
+                p[at] = v[j];
+                ix[at] = lo + base + tid * kSampPer + j;
+                ++at;
+            }
+        off += s_nz;
+        __syncthreads();
+    }
+    //    the F32 running sum, CTA by CTA in rank (= index) order
+    for (int q = 0; q < kClu; ++q) {
+        if (r == q && tid == 0) {
+            float acc = s_acc;
+            int done = s_done;
+            for (int m = 0; m < off && !done; ++m) {
+                acc += p[m];
+                if (u <= acc) {
+                    a.out[b] = ix[m];
+                    done = 1;
+                }
+            }
+            if (q + 1 < kClu) {
+                *cl.map_shared_rank(&s_acc, q + 1) = acc;
+                *cl.map_shared_rank(&s_done, q + 1) = done;
+            } else if (!done) {
+                a.out[b] = V - 1;
+            }
+        }
+        cl.sync();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Log-probabilities of scored tokens (Model::score_logprobs, model.cpp:1746-
 // 1831): per row of logits [n][V], lp = (l - max) - log(sum exp(l - max)),
 // the target token's lp and the k largest lps (descending; equal lps: the
@@ -404,9 +682,6 @@ extern "C" tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, 
     TVB_REQUIRE(!topp || (cfg->top_k >= 1 && cfg->top_k <= kSampCand),
                 "sample: top_p %g needs top_k in [1, %d] (got %d)", cfg->top_p, kSampCand, cfg->top_k);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const size_t words = (size_t)vocab / 32 + 1;
-    void* ws = nullptr;
-    TVB_CUDA(cudaMallocAsync(&ws, (size_t)B * ((size_t)vocab * 4 + words * 4), st));
     SampArgs a;
     a.logits = logits;
     a.vocab = vocab;
@@ -420,6 +695,23 @@ extern "C" tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, 
     a.max_seen = max_seen;
     a.u = u;
     a.out = out;
+    a.work = nullptr;
+    a.bits = nullptr;
+    const int S = ((vocab + kClu - 1) / kClu + 31) / 32 * 32;   // entries per CTA of a row's cluster
+    if (S <= kCluMaxSlice) {
+        const size_t smem = (size_t)S * 8 + ((size_t)S / 32 + 1) * 4;
+        static size_t smem_set = 0;
+        if (smem > smem_set) {
+            TVB_CUDA(cudaFuncSetAttribute(sample_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+            smem_set = smem;
+        }
+        sample_cluster_kernel<<<dim3(kClu, (unsigned)B), kSampThreads, smem, st>>>(a, S);
+        return check_launch("sample_cluster_kernel");
+    }
+    const size_t words = (size_t)vocab / 32 + 1;
+    void* ws = nullptr;
+    TVB_CUDA(cudaMallocAsync(&ws, (size_t)B * ((size_t)vocab * 4 + words * 4), st));
     a.work = static_cast<float*>(ws);
     a.bits = reinterpret_cast<unsigned*>(static_cast<float*>(ws) + (size_t)B * vocab);
     sample_kernel<<<B, kSampThreads, 0, st>>>(a);

@@ -2,7 +2,9 @@
 sample_token (pinned by tests/test_sampler.py) with the same uniform draws:
 the same token for every row, except where a draw lies within 1e-5 of a
 boundary of the cumulative distribution (the device's expf and tree sums may
-move a boundary by a few F32 ulps)."""
+move a boundary by a few F32 ulps).  Rows up to 196,608 entries run on one
+8-CTA cluster per row (100, 1000 and 128,256 here, the first with CTAs whose
+slice is empty); the 200,000-entry rows take the single-CTA kernel."""
 import ctypes as C
 
 import numpy as np
@@ -32,7 +34,7 @@ def run(lib, torch, logits, cfg, seen, u):
     return st, d_out.cpu().numpy()
 
 
-@pytest.mark.parametrize("V", [1000, 128256])
+@pytest.mark.parametrize("V", [100, 1000, 128256, 200000])
 @pytest.mark.parametrize("cfg", [(0.8, 0.9, 40, 1.1), (1.0, 1.0, 0, 1.0), (0.5, 0.95, 1024, 1.2),
                                  (0.0, 0.5, 1, 1.0), (1.3, 1.0, 7, 1.0)])
 def test_device_sampler_matches_restatement(V, cfg):
@@ -48,16 +50,21 @@ def test_device_sampler_matches_restatement(V, cfg):
     st, got = run(lib, torch, logits, cfg, seen, u)
     assert st == 0, lib.tvb_last_error()
     T, tp, tk, pen = cfg
-    checked = 0
+    exact = 0
     for b in range(B):
         tok, cdf = sample_token(logits[b], T, tp, tk, pen, seen[b], u=float(u[b]), return_cdf=True)
-        if cdf is not None and u[b] > 0:
-            nz = np.unique(cdf)
-            if np.min(np.abs(nz.astype(np.float64) - float(u[b]))) < 1e-5:
-                continue
-        assert got[b] == tok, (b, got[b], tok)
-        checked += 1
-    assert checked >= B - 1
+        if got[b] == tok:
+            exact += 1
+            continue
+        # a different token only where the draw is within 1e-5 of the restated
+        # cumulative distribution at the device's token (with 200k entries and
+        # no filter, neighbouring boundaries lie closer than that)
+        assert cdf is not None and u[b] > 0, (b, got[b], tok)
+        g = int(got[b])
+        above = float(cdf[g]) >= float(u[b]) - 1e-5
+        below = g == 0 or float(cdf[g - 1]) < float(u[b]) + 1e-5
+        assert above and below, (b, g, tok, float(u[b]))
+    assert exact >= B // 2
 
 
 def test_device_sampler_rejects_top_p_without_top_k():
