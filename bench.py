@@ -613,6 +613,26 @@ def run_ours(args, world, rank, local):
     if args.layers:
         # profiling only: the same shapes with fewer layers (smaller device footprint)
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
+    if args.only == "sample":
+        # profiling: W + K device samplings of 8 rows of vocabulary logits
+        # (temperature 0.8, top-p 0.9, top-k 40, penalty 1.1 over 64 seen tokens)
+        import ctypes as C
+        from ternative_b200 import load
+        from ternative_b200._lib import SamplerConfig
+        lib = load()
+        B, V = 8, cfg.vocab_size
+        lg = torch.randn(B, V, device="cuda") * 3
+        seen = torch.randint(0, V, (B, 64), dtype=torch.int32, device="cuda")
+        n_seen = torch.full((B,), 64, dtype=torch.int32, device="cuda")
+        u = torch.rand(B, device="cuda")
+        tok = torch.empty(B, dtype=torch.int32, device="cuda")
+        sc = SamplerConfig(0.8, 0.9, 40, 1.1)
+        for _ in range(args.warmup + args.steps):
+            if lib.tvb_sample(lg.data_ptr(), B, V, V, C.byref(sc), seen.data_ptr(), n_seen.data_ptr(), 64,
+                              u.data_ptr(), tok.data_ptr(), None) != 0:
+                raise RuntimeError(lib.tvb_last_error().decode())
+        torch.cuda.synchronize()
+        return
     synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0)
     be = CUDABackend()
     if args.only == "merge":
@@ -1007,7 +1027,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-serving", action="store_true")
-    ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill"], default=None,
+    ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill", "sample"], default=None,
                     help="profiling: run only W+K launches of one part, print nothing")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling with --only: use this many layers of the shape")

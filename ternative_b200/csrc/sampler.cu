@@ -1,6 +1,7 @@
 // The token sampler on the device (sample_token, src/sampler.cpp:11-148) for B
 // rows of logits, so a batched decode step need not copy 128k logits per row
-// to the host.  One CTA of 1024 threads per row runs the reference's steps in
+// to the host.  One 8-CTA cluster per row (sample_cluster_kernel; rows longer
+// than 196,608 entries: one CTA, sample_kernel) runs the reference's steps in
 // its order and arithmetic:
 //
 //   1. logits / temperature (when temperature > 0 and != 1)
@@ -72,6 +73,51 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
     return red[0];
 }
 
+// One radix-select step, run by warp 0: the bin d of the need-th largest key
+// among those counted in hist[256] -- the first bin, from 255 down, whose
+// running count reaches need (bin 0 if none does) -- and the rank left within
+// it.  Lane l owns bins 255 - 8l .. 248 - 8l; a warp scan replaces the walk
+// over the bins.
+__device__ __forceinline__ void radix_pick(const unsigned* hist, int need, int* keep, int* left) {
+    const int lane = threadIdx.x & 31;
+    unsigned c[8], tot = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+    }
+    unsigned incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const unsigned excl = incl - tot;
+    const unsigned un = (unsigned)need;
+    // bins 255 .. 1 only: bin 0 takes whatever is left
+    const unsigned last = lane == 31 ? incl - c[7] : incl;
+    const unsigned bal = __ballot_sync(0xffffffffu, excl < un && un <= last);
+    if (bal == 0u) {
+        if (lane == 31) {
+            *keep = 0;
+            *left = need - (int)(incl - c[7]);
+        }
+        return;
+    }
+    if (lane == __ffs(bal) - 1) {
+        unsigned run = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (run + c[j] >= un) {
+                *keep = 255 - 8 * lane - j;
+                *left = need - (int)run;
+                break;
+            }
+            run += c[j];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_constant__ SampArgs a) {
     const int b = blockIdx.x, tid = threadIdx.x, V = a.vocab;
     const float* lg = a.logits + (size_t)b * a.ld;
@@ -140,15 +186,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
                 }
             }
             __syncthreads();
-            if (tid == 0) {
-                int d = 255;
-                for (; d > 0; --d) {
-                    if ((int)hist[d] >= need) break;
-                    need -= (int)hist[d];
-                }
-                s_keep = d;
-                s_count = need;
-            }
+            if (tid < 32) radix_pick(hist, need, &s_keep, &s_count);
             __syncthreads();
             prefix |= (unsigned long long)s_keep << shift;
             mask |= 255ull << shift;
@@ -407,15 +445,7 @@ sample_cluster_kernel(const __grid_constant__ SampArgs a, int S) {
                 comb[tid] = c;
             }
             __syncthreads();
-            if (tid == 0) {
-                int d = 255;
-                for (; d > 0; --d) {
-                    if ((int)comb[d] >= need) break;
-                    need -= (int)comb[d];
-                }
-                s_keep = d;
-                s_need = need;
-            }
+            if (tid < 32) radix_pick(comb, need, &s_keep, &s_need);
             __syncthreads();
             prefix |= (unsigned long long)s_keep << shift;
             mask |= 255ull << shift;
@@ -613,15 +643,7 @@ logprob_kernel(const float* __restrict__ logits, int V, int ld, const int* __res
             if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
         }
         __syncthreads();
-        if (tid == 0) {
-            int d = 255;
-            for (; d > 0; --d) {
-                if ((int)hist[d] >= need) break;
-                need -= (int)hist[d];
-            }
-            s_keep = d;
-            s_count = need;
-        }
+        if (tid < 32) radix_pick(hist, need, &s_keep, &s_count);
         __syncthreads();
         prefix |= (unsigned long long)s_keep << shift;
         mask |= 255ull << shift;
