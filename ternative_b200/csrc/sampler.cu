@@ -478,10 +478,12 @@ sample_cluster_kernel(const __grid_constant__ SampArgs a, int S) {
         total = min(total, kSampCand);
         for (int i = total + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
         cl.sync();   // the remote reads of loc / s_loc are done
-        for (int size = 2; size <= kSampCand; size <<= 1) {
+        int P = 2;   // the sort covers the first P >= total entries (the rest are zero)
+        while (P < total) P <<= 1;
+        for (int size = 2; size <= P; size <<= 1) {
             for (int stride = size >> 1; stride > 0; stride >>= 1) {
                 const int i = tid, j = i ^ stride;
-                if (j > i) {
+                if (i < P && j > i) {
                     const bool desc = (i & size) == 0;
                     const unsigned long long x = cand[i], y = cand[j];
                     if (desc ? (x < y) : (x > y)) {
