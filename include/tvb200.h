@@ -243,6 +243,18 @@ tvb_status tvb_kv_download_slot(tvb_context* ctx, int layer, int pos, int n_floa
 /* sync_d (ops.h:123). */
 tvb_status tvb_context_sync(tvb_context* ctx);
 
+/* Phase trace of the fused decode step (no counterpart in the reference, whose
+ * only tracing is stdout progress lines).  Only the trace build of the library
+ * (libtvb200_trace.so, `make -C ternative_b200/csrc trace`) records: every
+ * later decode-step launch on this device writes, from thread 0 of each CTA,
+ * %globaltimer nanoseconds at 8 event slots per (phase, CTA) into `dev_buf`
+ * laid out [phase][CTA][8] as 64-bit words, for the first `n_phases` phases
+ * (the buffer holds n_phases x SMs x 8 words).  Slots: 0 phase start, 1 inputs
+ * staged, 2 weight stream done, 3 epilogue done, 6 barrier arrival, 4 next
+ * phase prepared, 5 barrier passed.  dev_buf NULL stops tracing.
+ * The product build returns TVB_ERR_UNSUPPORTED. */
+tvb_status tvb_trace_set(void* dev_buf, int n_phases);
+
 /* ------------------------------------------------------------------------ */
 /* Tensor parallelism: one process (and context) per GPU.  No counterpart in */
 /* the reference, whose GPU path is single-device.  Each rank's context is  */

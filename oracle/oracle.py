@@ -22,7 +22,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 RESTATED_SO = os.path.join(HERE, "libtvoracle.so")
 REFERENCE_SO = os.path.join(HERE, "_ref", "libtvref.so")
 DROPIN_SO = os.path.join(HERE, "_ref", "libtvref_dropin.so")
-REFERENCE_SRC = "/root/reference"
+# Where the reference sources lie (oracle/Makefile's REF); only build() reads it.
+REFERENCE_SRC = os.environ.get("TVB_REFERENCE_SRC", "/root/reference")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
@@ -38,7 +39,7 @@ def build(reference: bool = True) -> None:
     targets = ["libtvoracle.so"]
     if reference and os.path.isdir(REFERENCE_SRC):
         targets += ["ref", "dropin"]
-    subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={REFERENCE_SRC}", *targets], check=True)
 
 
 def _c(a, dtype):
@@ -187,6 +188,7 @@ class Reference:
         L.tvref_model_create.argtypes = [C.c_int] * 7 + [C.c_float, C.c_float]
         L.tvref_model_free.argtypes = [C.c_void_p]
         L.tvref_model_set.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.tvref_model_set_f32.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.tvref_forward_prefill.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
         L.tvref_forward_prefill_hidden.argtypes = [C.c_void_p, _i32p, C.c_int, _f32p]
         L.tvref_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _f32p]
@@ -343,7 +345,11 @@ class ReferenceModel:
 
         def put(which, layer, arr):
             arr = np.ascontiguousarray(arr)
-            rc = L.tvref_model_set(self.h, which, layer, arr.ctypes.data)
+            # F16 bits (uint16) are the merged weights; an F32 projection holds the
+            # exact dequantised values of a per-row INT8 layer
+            setter = L.tvref_model_set_f32 if arr.dtype == np.float32 and which not in (1, 2, 7, 8, 12) \
+                else L.tvref_model_set
+            rc = setter(self.h, which, layer, arr.ctypes.data)
             if rc != 0:
                 raise RuntimeError(f"tvref_model_set({which}, {layer}) -> {rc}")
 

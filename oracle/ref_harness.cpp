@@ -238,6 +238,32 @@ int tvref_model_set(tvref_model* h, int which, int layer, const void* data) {
     return 0;
 }
 
+// Projection `which` (3..6, 9..11 of the numbering above) as an F32 tensor
+// [out][in]: the exact dequantised values of a per-row INT8 layer (code times
+// its row scale), which no F16 tensor holds.  The reference's tensor_matmul
+// takes its all-F32 path for such a weight (tensor.cpp:575-620).
+int tvref_model_set_f32(tvref_model* h, int which, int layer, const float* data) {
+    Model& m = h->m;
+    const auto& c = m.config;
+    const int64_t H = c.hidden_size, I = c.intermediate_size;
+    const int64_t Hq = (int64_t)c.num_heads * c.head_dim;
+    const int64_t Hk = (int64_t)c.num_kv_heads * c.head_dim;
+    if (layer < 0 || layer >= c.num_layers) return -1;
+    LayerWeights& w = m.layers[layer];
+    auto f32 = [&](int64_t in, int64_t out) { return make_f32({in, out}, data); };
+    switch (which) {
+        case 3: w.wq = f32(H, Hq); break;
+        case 4: w.wk = f32(H, Hk); break;
+        case 5: w.wv = f32(H, Hk); break;
+        case 6: w.wo = f32(Hq, H); break;
+        case 9: w.w_gate = f32(H, I); break;
+        case 10: w.w_up = f32(H, I); break;
+        case 11: w.w_down = f32(I, H); break;
+        default: return -2;
+    }
+    return 0;
+}
+
 // model.cpp:1139-1234 — Model::forward_prefill; logits [S][V].
 int tvref_forward_prefill(tvref_model* h, const int* tokens, int S, float* logits) {
     std::vector<int> t(tokens, tokens + S);

@@ -147,6 +147,12 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
     __syncthreads();
     bool ok = true;
     for (int p = 0; p < n_phases && ok; ++p) {
+#ifdef TVB_PHASE_TRACE
+        if (threadIdx.x == 0)
+            s_trace_row = (g_trace_buf && p < g_trace_phases) ? g_trace_buf + ((size_t)p * G + b) * kTraceEvents
+                                                              : nullptr;
+#endif
+        trace_stamp(0);
         const Phase& ph = desc[p & 1];
         // The next phase's descriptor.  Its buffer held phase p - 1, which
         // nothing reads any more; the GEMV prologue's __syncthreads (or the
@@ -166,16 +172,20 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
             buf = ChunkBuf{};
             __syncthreads();
             if (b < ph.at.nkv * ph.at.nsplit) attn_item(ph.at, b, smem + 1024, pos);
+            trace_stamp(1);
         }
         // A row-parallel exchange is waited for even after the last phase: the
         // next launch's first exchange reuses this one's slot parity.
         if (p + 1 < n_phases || exchange) {
             grid_arrive(st);   // this phase's outputs are written (includes __syncthreads)
             if (exchange && threadIdx.x == 0) tp_count_arrive(tp);
+            trace_stamp(6);
             // input-independent work for the next phase overlaps the barrier
             if (p + 1 < n_phases) phase_prepare(next, smem, G, b, warp, pos, buf);
+            trace_stamp(4);
             ok = exchange ? tp_exchange_wait(st, tp, push0 + (unsigned)tp.index + 1u, G)
                           : grid_wait(st, (unsigned)(p + 1) * (unsigned)G);
+            trace_stamp(5);
         }
     }
     // last CTA out resets the barrier for the next launch

@@ -1095,6 +1095,20 @@ tvb_status tvb_context_sync(tvb_context* c) {
     return TVB_OK;
 }
 
+tvb_status tvb_trace_set(void* dev_buf, int n_phases) {
+#ifdef TVB_PHASE_TRACE
+    TVB_REQUIRE(n_phases >= 0, "trace_set: n_phases < 0");
+    unsigned long long* p = static_cast<unsigned long long*>(dev_buf);
+    TVB_CUDA(cudaMemcpyToSymbol(g_trace_buf, &p, sizeof(p)));
+    TVB_CUDA(cudaMemcpyToSymbol(g_trace_phases, &n_phases, sizeof(n_phases)));
+    return TVB_OK;
+#else
+    (void)dev_buf;
+    (void)n_phases;
+    return set_error(TVB_ERR_UNSUPPORTED, "trace_set: this build records no phase trace (libtvb200_trace.so does)");
+#endif
+}
+
 tvb_status tvb_set_layer(tvb_context* c, int layer, const tvb_layer_weights* lw) {
     TVB_REQUIRE(c && lw, "set_layer: null argument");
     TVB_REQUIRE(layer >= 0 && layer < c->L, "set_layer: layer %d of %d", layer, c->L);

@@ -32,6 +32,28 @@
 namespace tvb {
 
 enum GemvMode { GM_PLAIN = 0, GM_QKV = 1, GM_RESID = 2, GM_GATEUP = 3, GM_LMHEAD = 4 };
+
+// Phase trace of the decode step, compiled in only with -DTVB_PHASE_TRACE (the
+// libtvb200_trace.so build): thread 0 of every CTA writes %globaltimer (ns) at
+// fixed points of each phase into the buffer given to tvb_trace_set, laid out
+// [phase][CTA][kTraceEvents].  Events: 0 phase start, 1 inputs staged (GEMV
+// prologue done / attention item done), 2 weight stream done, 3 epilogue done,
+// 6 barrier arrival made, 4 next phase prepared, 5 barrier passed.
+constexpr int kTraceEvents = 8;
+#ifdef TVB_PHASE_TRACE
+static __device__ unsigned long long* g_trace_buf;
+static __device__ int g_trace_phases;
+static __shared__ unsigned long long* s_trace_row;   // this CTA's row of the running phase
+__device__ __forceinline__ void trace_stamp(int ev) {
+    if (threadIdx.x == 0 && s_trace_row) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        s_trace_row[ev] = t;
+    }
+}
+#else
+__device__ __forceinline__ void trace_stamp(int) {}
+#endif
 enum WType { WT_F16 = 0, WT_I8 = 1 };
 
 constexpr int kGemvThreads = 512;
@@ -528,6 +550,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
         if (lane == 0) red_ss[warp] = ss;
     }
     __syncthreads();
+    trace_stamp(1);
 
     // ---- main loop: kDepth chunks in flight per warp ---------------------------------
     const int hsel = (lane >> 2) & 1;   // bank-conflict-free order for the F16 x loads
@@ -573,6 +596,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
         }
     }
     __syncthreads();
+    trace_stamp(2);
 
     // tensor.cpp:675-676: rms = sqrt(ss/n + eps); inv = 1/rms
     float inv = 1.0f, ss_local = 0.f;
@@ -649,6 +673,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
             }
         }
     }
+    trace_stamp(3);
 }
 
 // LM-head completion: CTA-wide argmax, global max, and -- in the last CTA to
@@ -707,6 +732,9 @@ template <int MODE, int WT, int R, bool TP = false>
 __global__ void __launch_bounds__(kGemvThreads, 1)
 stream_gemv_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
+#ifdef TVB_PHASE_TRACE
+    if (threadIdx.x == 0) s_trace_row = nullptr;   // stand-alone launches are not traced
+#endif
     ChunkBuf buf;
     gemv_prefetch<MODE, WT, R>(a, gridDim.x, blockIdx.x, threadIdx.x >> 5, buf);
     pdl_launch_dependents();

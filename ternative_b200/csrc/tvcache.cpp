@@ -293,7 +293,9 @@ tvb_status tvb_cache_open(const char* path, tvb_cache** out) {
         return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: truncated tensor table in %s", path));
     for (auto& e : c->table) {
         e.name[sizeof(e.name) - 1] = 0;
-        if (e.n_dims > 4 || c->hdr.data_offset + e.data_offset + e.nbytes > c->hdr.total_size)
+        // bounds written so that no file-supplied sum can wrap around
+        const uint64_t size = c->hdr.total_size, base = c->hdr.data_offset;
+        if (e.n_dims > 4 || base > size || e.data_offset > size - base || e.nbytes > size - base - e.data_offset)
             return fail(tvb::set_error(TVB_ERR_INVALID, "cache_open: entry '%s' out of range", e.name));
     }
     *out = c;
@@ -408,11 +410,13 @@ bool skip_value(FILE* f, uint32_t t, int depth, uint64_t* u32_out) {
     return std::fseek(f, sizes[t], SEEK_CUR) == 0;
 }
 
+// Byte size of n elements of a ggml type; false for a type this reader does
+// not size, or for a count whose size does not fit 64 bits.
 bool gguf_bytes(uint32_t type, uint64_t n, uint64_t* out) {
     switch (type) {
-        case 0: *out = n * 4; return true;                       // F32
-        case 1: case 30: *out = n * 2; return true;              // F16, BF16
-        case 36: *out = (n + 127) / 128 * 32 + 4; return true;   // I2_S: codes + F32 scale
+        case 0: if (n > UINT64_MAX / 4) return false; *out = n * 4; return true;              // F32
+        case 1: case 30: if (n > UINT64_MAX / 2) return false; *out = n * 2; return true;     // F16, BF16
+        case 36: *out = (n / 128 + (n % 128 != 0)) * 32 + 4; return n <= UINT64_MAX / 2;     // I2_S + F32 scale
         default: return false;
     }
 }
@@ -450,16 +454,23 @@ tvb_status tvb_gguf_open(const char* path, tvb_gguf** out) {
         uint64_t v = 0;
         const bool want = key == "general.alignment";
         if (!skip_value(f, t, 0, want ? &v : nullptr)) return fail("bad metadata value");
-        if (want && t == 4 && v > 0) alignment = v;
+        if (want && t == 4 && v > 0) {
+            // the reference rounds with any alignment (gguf.cpp:299-304); a cap of
+            // 1 MiB keeps the rounding from wrapping
+            if (v > (1u << 20)) return fail("general.alignment above 1 MiB");
+            alignment = v;
+        }
     }
     g->tensors.resize(n_tensors);
     for (auto& ti : g->tensors) {
         uint32_t nd = 0;
+        // up to 8 dimensions, the reference parser's cap (gguf.cpp:286-287)
         if (!rd_string(f, &ti.name) || !rd(f, &nd, 4) || nd > 8) return fail("bad tensor info");
         ti.shape.resize(nd);
         uint64_t n = 1;
         for (auto& d : ti.shape) {
             if (!rd(f, &d, 8)) return fail("bad tensor info");
+            if (d != 0 && n > UINT64_MAX / d) return fail("tensor element count overflows");
             n *= d;
         }
         if (!rd(f, &ti.type, 4) || !rd(f, &ti.offset, 8)) return fail("bad tensor info");
@@ -479,7 +490,10 @@ tvb_status tvb_gguf_tensor(const tvb_gguf* g, int i, tvb_cache_tensor* info, uin
     std::memset(info, 0, sizeof(*info));
     info->name = t.name.c_str();
     info->ggml_type = (int)t.type;
-    info->n_dims = (int)std::min<size_t>(t.shape.size(), 4);
+    if (t.shape.size() > 4)
+        return tvb::set_error(TVB_ERR_UNSUPPORTED, "gguf_tensor: '%s' has %d dimensions (tvb_cache_tensor holds 4)",
+                              t.name.c_str(), (int)t.shape.size());
+    info->n_dims = (int)t.shape.size();
     for (int d = 0; d < info->n_dims; ++d) info->shape[d] = (int64_t)t.shape[d];
     if (nbytes) *nbytes = t.nbytes;
     return TVB_OK;
@@ -495,8 +509,9 @@ tvb_status tvb_gguf_read(tvb_gguf* g, const char* name, void* dst, uint64_t capa
                 t->type);
     TVB_REQUIRE(capacity >= t->nbytes, "gguf_read: '%s' needs %llu bytes, destination has %llu", name,
                 (unsigned long long)t->nbytes, (unsigned long long)capacity);
-    TVB_REQUIRE(g->data_offset + t->offset + t->nbytes <= g->file_size, "gguf_read: '%s' runs past the file end",
-                name);
+    TVB_REQUIRE(g->data_offset <= g->file_size && t->offset <= g->file_size - g->data_offset &&
+                    t->nbytes <= g->file_size - g->data_offset - t->offset,
+                "gguf_read: '%s' runs past the file end", name);
     if (std::fseek(g->file.f, (long)(g->data_offset + t->offset), SEEK_SET) != 0)
         return tvb::set_error(TVB_ERR_INVALID, "gguf_read: seek failed for '%s'", name);
     return read_into(g->file.f, dst, t->nbytes, name, g->sg);

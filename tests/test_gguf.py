@@ -49,3 +49,34 @@ def test_malformed_files_are_rejected(tmp_path):
     cut.write_bytes(data[:40])
     with pytest.raises(TvbError):
         GGUFFile(str(cut))
+
+
+def test_file_sizes_that_would_wrap_are_rejected(tmp_path):
+    """Sizes from the file are checked before any arithmetic on them can wrap:
+    an element count past 64 bits, an alignment past 1 MiB, a tensor offset
+    near 2^64 (whose end would wrap back into the file), more than 4 dims."""
+    huge = tmp_path / "huge.gguf"
+    write_gguf(str(huge), [("x", GGML_F32, (1 << 40, 1 << 40), b"")])
+    with pytest.raises(TvbError, match="overflows"):
+        GGUFFile(str(huge))
+    align = tmp_path / "align.gguf"
+    write_gguf(str(align), [("x", GGML_F32, (8,), np.zeros(8, np.float32).tobytes())], alignment=1 << 21)
+    with pytest.raises(TvbError, match="alignment"):
+        GGUFFile(str(align))
+    # a tensor whose offset is 2^64 - 16: its end wraps to a small number
+    wrap = tmp_path / "wrap.gguf"
+    write_gguf(str(wrap), [("x", GGML_F32, (8,), np.zeros(8, np.float32).tobytes())])
+    blob = bytearray(wrap.read_bytes())
+    at = blob.find(b"\x01\x00\x00\x00\x00\x00\x00\x00x")   # name length 1, then "x"
+    assert at > 0
+    off_at = at + 9 + 4 + 8 + 4                             # name, n_dims, dim 0, type -> offset
+    blob[off_at:off_at + 8] = ((1 << 64) - 16).to_bytes(8, "little")
+    wrap.write_bytes(bytes(blob))
+    with GGUFFile(str(wrap)) as g:
+        out = np.empty(32, np.uint8)
+        with pytest.raises(TvbError, match="past the file end"):
+            g.read("x", out.ctypes.data, out.size)
+    five = tmp_path / "five.gguf"
+    write_gguf(str(five), [("x", GGML_F32, (2, 1, 1, 1, 2), np.zeros(4, np.float32).tobytes())])
+    with pytest.raises(TvbError, match="dimensions"):
+        GGUFFile(str(five))
