@@ -67,7 +67,7 @@ def test_file_sizes_that_would_wrap_are_rejected(tmp_path):
     wrap = tmp_path / "wrap.gguf"
     write_gguf(str(wrap), [("x", GGML_F32, (8,), np.zeros(8, np.float32).tobytes())])
     blob = bytearray(wrap.read_bytes())
-    at = blob.find(b"\x01\x00\x00\x00\x00\x00\x00\x00x")   # name length 1, then "x"
+    at = blob.rfind(b"\x01\x00\x00\x00\x00\x00\x00\x00x")   # the tensor info: name length 1, "x"
     assert at > 0
     off_at = at + 9 + 4 + 8 + 4                             # name, n_dims, dim 0, type -> offset
     blob[off_at:off_at + 8] = ((1 << 64) - 16).to_bytes(8, "little")
