@@ -273,7 +273,12 @@ tvb_status tvb_trace_set(void* dev_buf, int n_phases);
 /* tvb_tp_set_peers.  Every rank must then run the same sequence of decode  */
 /* and prefill calls; logits returned are this rank's vocabulary slice       */
 /* (vocab_size / world floats, rows [rank * vocab_size / world, ...)).      */
-/* After a device-side error every rank must be re-initialised.             */
+/* When a step's device-side wait gives up (TVB_ERR_TIMEOUT, e.g. a rank    */
+/* skipped the step), the ranks' exchange counters no longer agree: that    */
+/* rank then refuses steps (TVB_ERR_STATE) until tvb_tp_recover.  Recover   */
+/* every rank (each call zeroes that rank's exchange buffer and step        */
+/* counters after its stream is idle), and let no rank start a step before  */
+/* all ranks have returned from tvb_tp_recover (a host-side barrier).       */
 /* Close imported buffers (tvb_ipc_close) after destroying the context.     */
 /* ------------------------------------------------------------------------ */
 typedef struct {
@@ -282,6 +287,7 @@ typedef struct {
 
 tvb_status tvb_tp_init(tvb_context* ctx, int rank, int world, void** exchange);
 tvb_status tvb_tp_set_peers(tvb_context* ctx, void* const* exchanges);
+tvb_status tvb_tp_recover(tvb_context* ctx);
 tvb_status tvb_ipc_export(const void* dev_ptr, tvb_ipc_handle* out);
 tvb_status tvb_ipc_import(const tvb_ipc_handle* handle, void** dev_ptr);
 tvb_status tvb_ipc_close(void* dev_ptr);

@@ -126,6 +126,7 @@ _SIGS = {
     "tvb_kv_download_slot": [_P, _I, _I, _I, _P],
     "tvb_context_sync": [_P],
     "tvb_trace_set": [_P, _I],
+    "tvb_tp_recover": [_P],
     "tvb_set_layer": [_P, _I, C.POINTER(LayerWeights)],
     "tvb_set_output": [_P, _P, _P],
     "tvb_decode_step": [_P, _I, _I, _P, _P],

@@ -254,6 +254,12 @@ class CUDABackend:
         arr = (C.c_void_p * len(buffers))(*buffers)
         call("tvb_tp_set_peers", self.ctx, arr)
 
+    def tp_recover(self) -> None:
+        """After a tensor-parallel step failed on any rank: zero this rank's
+        exchange buffer and step counters.  Every rank calls it; no rank may
+        start a step before all ranks have returned (a host-side barrier)."""
+        call("tvb_tp_recover", self.ctx)
+
     @staticmethod
     def ipc_export(dev_ptr: int) -> bytes:
         h = IpcHandle()

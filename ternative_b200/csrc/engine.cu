@@ -183,6 +183,10 @@ struct tvb_context {
     float* tp_xchg = nullptr;
     float* tp_peer[kMaxTp] = {};
     bool tp_ready = false;
+    // a device-side wait of a tensor-parallel step gave up: the exchange
+    // counters of the ranks no longer agree, so steps are refused until every
+    // rank has called tvb_tp_recover
+    bool tp_failed = false;
     float* e_x2 = nullptr;
     int n_push = 0;   // row-parallel exchanges per launch (both graphs)
     size_t tp_pf_off = 0;   // float offset of the prefill region in every rank's exchange buffer
@@ -443,8 +447,20 @@ tvb_status check_status(tvb_context* c) {
     // clear counters, flags and the abort latch so the next call starts clean
     cudaMemsetAsync(c->st, 0, sizeof(StepState), c->stream);
     cudaStreamSynchronize(c->stream);
+    // Under tensor parallelism the ranks' exchange buffers still hold arrival
+    // counts and flags of the abandoned step, which the restarted counters
+    // would compare against: no step may run until every rank recovers.
+    if (c->tp_world > 1) c->tp_failed = true;
     if (s & kStatusTimeout) return set_error(TVB_ERR_TIMEOUT, "a device-side wait exceeded its limit");
     return set_error(TVB_ERR_CUDA, "device status 0x%x", s);
+}
+
+// Entry guard of every call that runs a (possibly tensor-parallel) step.
+tvb_status tp_guard(const tvb_context* c, const char* what) {
+    if (c->tp_world > 1 && c->tp_failed)
+        return set_error(TVB_ERR_STATE,
+                         "%s: a tensor-parallel step failed on this rank; call tvb_tp_recover on every rank first", what);
+    return TVB_OK;
 }
 
 // ---- batched prefill (Model::forward_prefill, model.cpp:1139-1234) -----------------
@@ -999,6 +1015,17 @@ tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
     return TVB_OK;
 }
 
+tvb_status tvb_tp_recover(tvb_context* c) {
+    TVB_REQUIRE(c, "tp_recover: null context");
+    TVB_REQUIRE(c->tp_xchg, "tp_recover: call tvb_tp_init first");
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    TVB_CUDA(cudaMemsetAsync(c->tp_xchg, 0, (c->tp_key_off + 2 * kMaxBatch) * 4, c->stream));
+    TVB_CUDA(cudaMemsetAsync(c->st, 0, sizeof(StepState), c->stream));
+    TVB_CUDA(cudaStreamSynchronize(c->stream));
+    c->tp_failed = false;
+    return TVB_OK;
+}
+
 tvb_status tvb_tp_set_peers(tvb_context* c, void* const* exchanges) {
     TVB_REQUIRE(c && exchanges, "tp_set_peers: null argument");
     TVB_REQUIRE(c->tp_xchg, "tp_set_peers: call tvb_tp_init first");
@@ -1143,6 +1170,7 @@ tvb_status tvb_set_output(tvb_context* c, const void* tok_embd, const float* out
 
 tvb_status tvb_decode_step(tvb_context* c, int token, int pos, float* logits_host, int* argmax_host) {
     TVB_REQUIRE(c, "decode_step: null context");
+    TVB_TRY(tp_guard(c, "decode_step"));
     TVB_REQUIRE(token >= 0 && token < c->V, "decode_step: token %d outside vocab %d", token, c->V);
     TVB_REQUIRE(pos >= 0 && pos < c->cfg.max_seq_len, "decode_step: pos %d outside KV capacity %d", pos,
                 c->cfg.max_seq_len);
@@ -1164,6 +1192,7 @@ tvb_status tvb_decode_step(tvb_context* c, int token, int pos, float* logits_hos
 
 tvb_status tvb_generate_greedy(tvb_context* c, int token, int pos, int n_steps, int* tokens_host) {
     TVB_REQUIRE(c && tokens_host, "generate_greedy: null argument");
+    TVB_TRY(tp_guard(c, "generate_greedy"));
     TVB_REQUIRE(token >= 0 && token < c->V, "generate_greedy: token %d", token);
     TVB_REQUIRE(pos >= 0 && n_steps >= 0 && pos + n_steps <= c->cfg.max_seq_len,
                 "generate_greedy: positions [%d, %d) exceed KV capacity %d", pos, pos + n_steps,
@@ -1187,6 +1216,7 @@ tvb_status tvb_generate_greedy(tvb_context* c, int token, int pos, int n_steps, 
 
 tvb_status tvb_decode_enqueue(tvb_context* c, int token, int pos, int n_steps) {
     TVB_REQUIRE(c, "decode_enqueue: null context");
+    TVB_TRY(tp_guard(c, "decode_enqueue"));
     TVB_REQUIRE(token >= 0 && token < c->V, "decode_enqueue: token %d", token);
     TVB_REQUIRE(pos >= 0 && n_steps >= 0 && pos + n_steps <= c->cfg.max_seq_len,
                 "decode_enqueue: positions [%d, %d) exceed KV capacity %d", pos, pos + n_steps,
@@ -1206,6 +1236,7 @@ tvb_status tvb_prefill(tvb_context* c, const int* tokens, int S, float* last_log
 tvb_status tvb_prefill_slot(tvb_context* c, int slot, const int* tokens, int S, float* last_logits,
                             int* argmax_host) {
     TVB_REQUIRE(c && tokens, "prefill: null argument");
+    TVB_TRY(tp_guard(c, "prefill"));
     TVB_REQUIRE(slot >= 0 && slot < c->slots, "prefill: slot %d of %d", slot, c->slots);
     TVB_REQUIRE(S > 0 && S <= c->cfg.max_seq_len, "prefill: S=%d outside (0, %d]", S, c->cfg.max_seq_len);
     for (int i = 0; i < S; ++i)
@@ -1241,6 +1272,7 @@ tvb_status tvb_prefill_slot(tvb_context* c, int slot, const int* tokens, int S, 
 tvb_status tvb_score_logprobs(tvb_context* c, const int* tokens, int T, int start_pos, int k, float* logprobs,
                               int* top_ids, float* top_logprobs) {
     TVB_REQUIRE(c && tokens && logprobs, "score_logprobs: null argument");
+    TVB_TRY(tp_guard(c, "score_logprobs"));
     TVB_REQUIRE(T > 0 && T <= c->cfg.max_seq_len, "score_logprobs: T=%d outside (0, %d]", T, c->cfg.max_seq_len);
     TVB_REQUIRE(k >= 0 && k <= kMaxLogprobsHost && (k == 0 || (top_ids && top_logprobs)),
                 "score_logprobs: k=%d (0 .. %d, with output arrays)", k, kMaxLogprobsHost);
@@ -1286,6 +1318,7 @@ tvb_status tvb_score_logprobs(tvb_context* c, const int* tokens, int T, int star
 tvb_status tvb_decode_batch(tvb_context* c, const int* tokens, const int* positions, int B, float* logits,
                             int* next_tokens) {
     TVB_REQUIRE(c && tokens && positions && next_tokens, "decode_batch: null argument");
+    TVB_TRY(tp_guard(c, "decode_batch"));
     TVB_REQUIRE(B >= 1 && B <= c->slots && B <= kMaxBatch && 3 * B <= 2 * c->cfg.max_seq_len,
                 "decode_batch: B=%d (context slots %d, at most %d)", B, c->slots, kMaxBatch);
     for (int b = 0; b < B; ++b) {

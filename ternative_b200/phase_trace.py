@@ -100,7 +100,7 @@ def main(argv=None):
     m = Model.load(synth)
     be = m.backend
     G = torch.cuda.get_device_properties(0).multi_processor_count
-    n_phases = 5 * cfg.num_layers + 1
+    n_phases = len(KINDS) * cfg.num_layers + 1
     buf = torch.zeros(n_phases * G * EVENTS, dtype=torch.int64, device="cuda")
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
     be.clear_kv_d()

@@ -154,6 +154,13 @@ class TPModel:
                 bufs.append(p)
         be.tp_set_peers(bufs)
 
+    def recover(self, barrier: Callable[[], None]) -> None:
+        """Re-align the ranks after a step failed (TVB_ERR_TIMEOUT on some
+        rank): every rank zeroes its exchange buffer and counters, then the
+        ranks meet at `barrier` before any of them runs another step."""
+        self.backend.tp_recover()
+        barrier()
+
     def close(self):
         self.backend.close()
         for p in self._imported:

@@ -194,3 +194,157 @@ def test_tp_batch_decode_matches_single_gpu():
     for r in range(2):
         assert res[r]["toks"] == res[0]["toks"]
     assert max(res[0]["errs"]) < RTOL, res[0]["errs"]
+
+
+def _tp_setup(rank, world, port, cfg, seed=4, norm=1.0):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    from ternative_b200.model import SyntheticModel
+    from ternative_b200.tp import TPModel
+
+    def all_gather(obj):
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
+    synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=seed, norm_value=norm)
+    return dist, all_gather, synth, TPModel(synth, world, rank, all_gather)
+
+
+# Norm weights of the reference comparison: with every norm weight 1.0 at
+# hidden 1024 the q.k/sqrt(128) products have a standard deviation of ~450, so
+# softmaxes are near-hard maxima whose ties amplify F32 summation-order noise
+# (the reference's own F32 and float64 forwards part by more than 2e-3);
+# 1/16 (exact in binary) brings it to ~1.7.
+REF_NORM = 1.0 / 16
+
+
+def _child_ref(rank, world, port, cfg, prompt, n_new, q):
+    """Tensor-parallel prefill + greedy decode; rank 0 checks the assembled
+    logits against the reference's own Model::forward_prefill (oracle/_ref)
+    run teacher-forced over the generated tokens on the whole merged model."""
+    dist = None
+    try:
+        dist, all_gather, synth, m = _tp_setup(rank, world, port, cfg, norm=REF_NORM)
+        be = m.backend
+        be.clear_kv_d()
+        last, am = be.prefill(prompt)
+        toks = [int(t) for t in prompt] + [am]
+        logits = [last]
+        for _ in range(n_new - 1):
+            lg, am = be.decode_step(toks[-1], len(toks) - 1)
+            logits.append(lg)
+            toks.append(am)
+        parts = all_gather(np.stack(logits))
+        res = {"rank": rank, "toks": toks}
+        if rank == 0:
+            from oracle.oracle import ModelShape, Reference, ReferenceModel
+            from ternative_b200.model import Model
+            whole = Model.load(synth)
+            shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                               cfg.num_kv_heads, cfg.intermediate_size, cfg.max_seq_len, cfg.rope_theta,
+                               cfg.rms_norm_eps)
+            rm = ReferenceModel(Reference(), shape, whole.host_weights())
+            whole.backend.close()
+            res["full"] = np.concatenate(parts, axis=1)
+            res["ref"] = rm.forward_prefill(np.asarray(toks[:-1], np.int32))[len(prompt) - 1:]
+            rm.close()
+        dist.barrier()
+        m.close()
+        q.put(res)
+    except Exception as e:   # report, do not hang the parent
+        q.put({"rank": rank, "error": repr(e)})
+        raise
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_matches_reference(world, reference):
+    """8 query / 8 KV heads (whole heads per rank at 8 ranks), FFN 2048: the
+    ranks agree on every token and their logits, put together, lie within 2e-3
+    of the reference's forward_prefill over the same tokens, whose argmax they
+    follow."""
+    from ternative_b200.backend import Config
+    cfg = Config(vocab_size=4096, hidden_size=1024, num_layers=3, num_heads=8, num_kv_heads=8,
+                 head_dim=128, intermediate_size=2048, max_seq_len=256, max_prefill=256)
+    prompt = np.random.default_rng(100 + world).integers(0, cfg.vocab_size, 11).astype(np.int32)
+    res = _run(world, cfg, prompt, 10, child=_child_ref)
+    toks = res[0]["toks"]
+    for r in range(world):
+        assert res[r]["toks"] == toks
+    full, ref = res[0]["full"], res[0]["ref"]
+    assert full.shape == ref.shape
+    for i in range(len(ref)):
+        err = float(np.abs(full[i].astype(np.float64) - ref[i]).max() / np.abs(ref[i]).max())
+        assert err < RTOL, (i, err)
+        top2 = np.sort(ref[i])[-2:]
+        assert int(np.argmax(ref[i])) == toks[len(prompt) + i], f"step {i}: margin {top2[1] - top2[0]:.3g}"
+
+
+def _child_fault(rank, world, port, cfg, prompt, q):
+    """Rank 1 skips one decode step (it waits at a host barrier, no kernel in
+    flight); rank 0's bounded exchange wait gives up inside that step."""
+    import os
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist = None
+    try:
+        from ternative_b200 import TvbError
+        dist, all_gather, synth, m = _tp_setup(rank, world, port, cfg)
+        be = m.backend
+        be.clear_kv_d()
+        _, am = be.prefill(prompt)
+        _, am = be.decode_step(am, len(prompt))   # one step on every rank
+        dist.barrier()
+        res = {"rank": rank}
+        if rank == 0:
+            t0 = time.time()
+            for key in ("first", "second"):
+                try:
+                    be.decode_step(am, len(prompt) + 1)
+                    res[key] = "ok"
+                except TvbError as e:
+                    res[key] = e.status
+            res["wait_s"] = time.time() - t0
+        dist.barrier()
+        m.recover(dist.barrier)
+        be.clear_kv_d()
+        _, am = be.prefill(prompt)
+        toks = [am]
+        for i in range(4):
+            _, am = be.decode_step(toks[-1], len(prompt) + i)
+            toks.append(am)
+        res["toks"] = toks
+        dist.barrier()
+        m.close()
+        q.put(res)
+    except Exception as e:
+        q.put({"rank": rank, "error": repr(e)})
+        raise
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+def test_tp_skipped_step_times_out_then_recovers():
+    """A rank that skips a step: the peer gets TVB_ERR_TIMEOUT after about a
+    second (its bounded wait), then TVB_ERR_STATE until every rank calls
+    tvb_tp_recover; after recovery both ranks decode the same tokens again as
+    the undisturbed path does."""
+    from ternative_b200._lib import STATUS_NAMES
+    from ternative_b200.backend import Config
+    cfg = Config(vocab_size=4096, hidden_size=512, num_layers=2, num_heads=8, num_kv_heads=4,
+                 head_dim=128, intermediate_size=2048, max_seq_len=128, max_prefill=128)
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab_size, 7).astype(np.int32)
+    res = _run(2, cfg, None, None, child=_child_fault, args=(prompt,))
+    names = {v: k for k, v in STATUS_NAMES.items()}
+    assert res[0]["first"] == names["TVB_ERR_TIMEOUT"], res[0]
+    assert res[0]["second"] == names["TVB_ERR_STATE"], res[0]
+    assert res[0]["wait_s"] < 30
+    assert res[0]["toks"] == res[1]["toks"]
+    clean = _run(2, cfg, prompt, 5)   # the undisturbed prefill + decode
+    assert res[0]["toks"] == clean[0]["toks"][len(prompt):]
