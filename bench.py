@@ -33,7 +33,10 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
-os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+# The CPU legs (the reference's OpenMP loops) use every host core: a launcher
+# such as torchrun sets OMP_NUM_THREADS=1, which would time them on one core.
+HOST_CORES = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+os.environ["OMP_NUM_THREADS"] = str(HOST_CORES)
 
 import numpy as np  # noqa: E402
 
@@ -184,7 +187,8 @@ def run_reference(args, world, rank):
     shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
                        cfg.num_kv_heads, cfg.intermediate_size, 512)
     rm = reference_model_random(shape)
-    threads = rm.ref.L.tvref_omp_threads() if hasattr(rm.ref.L, "tvref_omp_threads") else None
+    rm.ref.L.tvref_set_threads(HOST_CORES)
+    threads = rm.ref.L.tvref_omp_threads()
     for _ in range(max(0, min(args.warmup, 2))):
         rm.time_decode(1, 32, 1)
     sec, n = time_reference_decode(rm, args.steps, pos0=40, budget_s=args.cpu_seconds * 3)
@@ -196,7 +200,9 @@ def run_reference(args, world, rank):
         "data": "synthetic", "config": config_block(args, cfg),
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
                          "sample": f"{n} decode tokens at positions 41..{40 + n} (Model::forward, "
-                                   f"prefill=false) of the 2B shape, random F16 weights"},
+                                   f"prefill=false) of the 2B shape, random F16 weights; the GPU arm "
+                                   f"times 128 steps from position 40 (KV reads differ by < 1% of "
+                                   f"the bytes per token)"},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     rm.close()
@@ -204,6 +210,62 @@ def run_reference(args, world, rank):
 
 
 METRIC = "batch-1 decode tok/s (BitNet-2B ternary+LoRA, F16-merged)"
+
+
+def reference_cpu_baselines(rm, hw, cfg, synth, cores, budget_s):
+    """The reference's --no-gpu code beside the other measured rows, on this
+    host (oracle/_ref built from the reference sources):
+      prefill -- Model::forward_prefill of a 128-token prompt (OpenMP);
+      gemv    -- tensor_matmul with one activation row on each sweep shape (OpenMP);
+      merge   -- apply_lora (I2_S dequant + rank-64 matmul_lora + F16 cast,
+                 single-threaded as in the reference) of one 2560x2560 tensor,
+                 scaled to the 210 tensors of the 2B model by weight count."""
+    import torch
+    from ternative_b200.model import PROJ, proj_shape
+    L = rm.ref.L
+    out = {}
+    toks = np.random.default_rng(5).integers(0, cfg.vocab_size, 128).astype(np.int32)
+    t0 = time.perf_counter()
+    rm.forward_prefill(toks)
+    sec = time.perf_counter() - t0
+    out["prefill"] = {"tok_s": 128 / sec, "ms": sec * 1e3, "cores": cores, "kind": "reference",
+                      "sample": "Model::forward_prefill of a 128-token prompt (logits of every row), same merged model"}
+    gemv = {}
+    x = np.random.default_rng(6).standard_normal(cfg.intermediate_size).astype(np.float32)
+    for name, w in [("wk", hw["layers"][0]["wk"]), ("wq", hw["layers"][0]["wq"]), ("w_gate", hw["layers"][0]["w_gate"]),
+                    ("w_down", hw["layers"][0]["w_down"]), ("lm_head", hw["tok_embd"])]:
+        N, K = w.shape
+        y = np.empty(N, np.float32)
+        xk = np.ascontiguousarray(x[:K]) if K <= x.size else np.random.default_rng(7).standard_normal(K).astype(np.float32)
+        w = np.ascontiguousarray(w)
+        L.tvref_matmul_f16(xk, 1, K, w, N, y)   # warm
+        reps = 0
+        t0 = time.perf_counter()
+        while reps < 3 or (time.perf_counter() - t0 < 0.5 and reps < 50):
+            L.tvref_matmul_f16(xk, 1, K, w, N, y)
+            reps += 1
+        us = (time.perf_counter() - t0) / reps * 1e6
+        gemv[f"{N}x{K}_f16"] = {"us": us, "GB/s": (2 * N * K + 4 * K + 4 * N) / (us * 1e-6) / 1e9}
+    out["gemv"] = {"shapes": gemv, "cores": cores, "kind": "reference",
+                   "sample": "tensor_matmul (tensor.cpp:375-486, one activation row) on layer 0's merged weights "
+                             "and the tied lm_head, host memory"}
+    # merge: one q-shaped tensor at rank 64 (alpha 128), the merge microbench's configuration
+    t = synth.layers[0]["wq"]
+    codes = t.i2s.cpu().numpy()
+    Kq, Nq = t.K, t.N
+    g = torch.Generator(device="cpu").manual_seed(64)
+    A = (torch.randn(64, Kq, generator=g) / np.sqrt(Kq)).numpy()
+    B = (torch.randn(Nq, 64, generator=g) * 1e-3).numpy()
+    dst = np.empty(Nq * Kq, np.uint16)
+    t0 = time.perf_counter()
+    L.tvref_apply_lora_f16(codes, np.float32(t.scale), Kq, Nq, A, B, 64, 128.0, dst)
+    sec = time.perf_counter() - t0
+    n_all = sum(proj_shape(cfg, n)[0] * proj_shape(cfg, n)[1] for n in PROJ) * cfg.num_layers
+    total = sec * n_all / (Nq * Kq)
+    out["merge"] = {"r64_f16_seconds_all_210": total, "seconds_per_sample": sec, "cores": 1, "kind": "reference",
+                    "sample": f"apply_lora of one {Nq}x{Kq} I2_S tensor, rank 64 alpha 128, scaled by weight "
+                              f"count to the 210 projections ({n_all / 1e9:.2f} G weights)"}
+    return out
 
 
 def config_block(args, cfg):
@@ -284,6 +346,9 @@ def run_tp_8b(args, world, rank):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    # every rank must have decoded the same greedy tokens: 8 more steps, compared
+    check = be.generate_greedy(0, pos + args.steps, 8)
+    tokens_agree = all(np.array_equal(t, check) for t in all_gather(check))
     local = shard_config(cfg, world)
     n_w = sum(2 * a * b for a, b in [(local.num_heads * 128, 4096), (2 * local.num_kv_heads * 128, 4096),
                                      (4096, local.num_heads * 128), (2 * local.intermediate_size, 4096),
@@ -294,7 +359,8 @@ def run_tp_8b(args, world, rank):
     per_gpu = (n_w + kv) / (ms / args.steps * 1e-3) / 1e9
     res = {"workload": f"8B-shaped batch-1 greedy decode, tensor-parallel over {world} GPU(s), "
                        f"after a {args.tp_prompt}-token prompt",
-           "n_gpus": world, "tok_s": args.steps / (ms * 1e-3), "ms_per_token": ms / args.steps,
+           "n_gpus": world, "tokens_agree_all_ranks": bool(tokens_agree),
+           "tok_s": args.steps / (ms * 1e-3), "ms_per_token": ms / args.steps,
            "per_gpu_bytes_per_token": n_w + kv, "per_gpu_GB/s": per_gpu, "frac_of_hbm": per_gpu / hbm,
            "peak_kind": kind, "prefill_ms": prefill_ms,
            "prefill_tok_s": args.tp_prompt / (prefill_ms * 1e-3),
@@ -309,6 +375,51 @@ def run_tp_8b(args, world, rank):
 
 
 TP_BATCH = 8
+
+
+def tp_parity_check(world, rank, all_gather):
+    """Tensor-parallel correctness on this job's ranks: a 3-layer model with 8
+    query / 8 KV heads (hidden 1024, FFN 2048, vocabulary 4096; I2_S + rank-16
+    LoRA merged to F16, norm weights 1/16 so the attention is not a hard
+    maximum) prefills 11 tokens and decodes 10 greedy tokens split over the
+    ranks; rank 0 compares the assembled logits with the reference's own
+    Model::forward_prefill (oracle/_ref) over the same tokens."""
+    from ternative_b200.backend import Config
+    from ternative_b200.model import Model, SyntheticModel
+    from ternative_b200.tp import TPModel
+    cfg = Config(vocab_size=4096, hidden_size=1024, num_layers=3, num_heads=8, num_kv_heads=8,
+                 head_dim=128, intermediate_size=2048, max_seq_len=256, max_prefill=256)
+    synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=4, norm_value=1.0 / 16)
+    m = TPModel(synth, world, rank, all_gather)
+    be = m.backend
+    prompt = np.random.default_rng(100 + world).integers(0, cfg.vocab_size, 11).astype(np.int32)
+    be.clear_kv_d()
+    last, am = be.prefill(prompt)
+    toks, logits = [int(t) for t in prompt] + [am], [last]
+    for _ in range(9):
+        lg, am = be.decode_step(toks[-1], len(toks) - 1)
+        logits.append(lg)
+        toks.append(am)
+    parts = all_gather((toks, np.stack(logits)))
+    m.close()
+    if rank != 0:
+        return None
+    agree = all(p[0] == toks for p in parts)
+    full = np.concatenate([p[1] for p in parts], axis=1)
+    from oracle.oracle import ModelShape, Reference, ReferenceModel
+    whole = Model.load(synth)
+    rm = ReferenceModel(Reference(), ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                                                cfg.num_kv_heads, cfg.intermediate_size, cfg.max_seq_len,
+                                                cfg.rope_theta, cfg.rms_norm_eps), whole.host_weights())
+    whole.backend.close()
+    ref = rm.forward_prefill(np.asarray(toks[:-1], np.int32))[len(prompt) - 1:]
+    rm.close()
+    errs = [float(np.abs(full[i].astype(np.float64) - ref[i]).max() / np.abs(ref[i]).max()) for i in range(len(ref))]
+    follows = all(int(np.argmax(ref[i])) == toks[len(prompt) + i] for i in range(len(ref)))
+    return {"ranks": world, "tokens_agree_all_ranks": bool(agree), "max_rel_err_vs_reference": max(errs),
+            "tokens_follow_reference_argmax": bool(follows), "ok": bool(agree and follows and max(errs) < 2e-3),
+            "note": "hidden 1024, 8/8 heads, FFN 2048, 3 layers; prefill 11 + 10 greedy steps; "
+                    "reference = oracle/_ref forward_prefill, teacher-forced; tolerance 2e-3"}
 
 
 def tp_batch_decode(args, be, cfg, world, stream, n_w, hbm):
@@ -601,15 +712,45 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    def all_gather(obj):
+        if world == 1:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
+    tp_parity = None
+    if world > 1 and args.only is None:
+        try:
+            tp_parity = tp_parity_check(world, rank, all_gather)
+        except Exception as e:   # reported; the same on every rank
+            tp_parity = {"ok": False, "error": repr(e)}
     if args.only_tp:
         res = run_tp_8b(args, world, rank)
         if rank == 0:
-            print(json.dumps({"tp_8b": res}), flush=True)
+            print(json.dumps({"tp_8b": res, "tp_parity": tp_parity}), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
         return
     cfg = SHAPES[args.config]
+    if args.only == "batch8":
+        # profiling: W + K batched greedy steps of 8 sequences on the 8B shape
+        # (--layers of its 32; 64-token prompts), one GPU
+        cfg = dataclasses.replace(SHAPES["8b"], num_layers=args.layers or 32, max_batch=TP_BATCH,
+                                  max_seq_len=64 + args.warmup + args.steps + 8)
+        m = Model.load(SyntheticModel.generate(cfg, rank=32, alpha=64.0, seed=0))
+        rng = np.random.default_rng(7)
+        cur = np.empty(TP_BATCH, np.int32)
+        for b in range(TP_BATCH):
+            _, cur[b] = m.backend.prefill_slot(b, rng.integers(0, cfg.vocab_size, 64).astype(np.int32),
+                                               want_logits=False)
+        pos = np.full(TP_BATCH, 64, np.int32)
+        for _ in range(args.warmup + args.steps):
+            _, cur = m.backend.decode_batch(cur, pos, want_logits=False)
+            pos += 1
+        m.backend.sync_d()
+        return
     if args.layers:
         # profiling only: the same shapes with fewer layers (smaller device footprint)
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
@@ -967,20 +1108,29 @@ def run_ours(args, world, rank, local):
         be2.close()
         del m2
 
-    # ---- CPU baseline: the reference's own decode on this host --------------------
+    # ---- CPU baselines: the reference's own code on this host (rank 0, all host
+    # cores for its OpenMP loops; the merge is single-threaded, as the reference's is)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         try:
             from oracle.oracle import ModelShape, Reference, ReferenceModel
             shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
                                cfg.num_kv_heads, cfg.intermediate_size, 512)
-            rm = ReferenceModel(Reference(), shape, m.host_weights())
+            hw = m.host_weights()
+            rm = ReferenceModel(Reference(), shape, hw)
+            rm.ref.L.tvref_set_threads(HOST_CORES)
+            cores = rm.ref.L.tvref_omp_threads()
             sec, n = time_reference_decode(rm, 64, pos0=40, budget_s=args.cpu_seconds)
-            cpu = {"value": 1.0 / sec, "unit": "tok/s", "cores": rm.ref.L.tvref_omp_threads(),
+            cpu = {"value": 1.0 / sec, "unit": "tok/s", "cores": cores,
                    "kind": "reference",
                    "sample": f"{n} decode tokens (Model::forward, prefill=false) of the same merged "
                              "2B model, oracle/_ref built from the reference sources"}
+            cpu_extra = reference_cpu_baselines(rm, hw, cfg, synth, cores, args.cpu_seconds)
             rm.close()
+            del hw
+            prefill["cpu_baseline"] = cpu_extra["prefill"]
+            gemv["cpu_baseline"] = cpu_extra["gemv"]
+            merge["cpu_baseline"] = cpu_extra["merge"]
         except Exception as e:
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                    "sample": f"unavailable: {e!r}"}
@@ -1008,7 +1158,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps,   # one decode_step_kernel launch per token
             "clocks": clk.report(), "merge": merge, "prefill": prefill, "mixed_offload": mixed, "tp_8b": tp8,
-            "serving_rows": serving,
+            "tp_parity": tp_parity, "serving_rows": serving,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1027,7 +1177,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-serving", action="store_true")
-    ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill", "sample"], default=None,
+    ap.add_argument("--only", choices=["decode", "gemv", "merge", "prefill", "sample", "batch8"], default=None,
                     help="profiling: run only W+K launches of one part, print nothing")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling with --only: use this many layers of the shape")

@@ -196,6 +196,7 @@ class Reference:
         L.tvref_kv_set_seq_len.argtypes = [C.c_void_p, C.c_int]
         L.tvref_omp_threads.restype = C.c_int
         L.tvref_omp_threads.argtypes = []
+        L.tvref_set_threads.argtypes = [C.c_int]
         L.tvref_cache_save.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_float, C.c_int]
         L.tvref_cache_load.argtypes = [C.c_void_p, C.c_char_p]
         L.tvref_model_get.restype = C.c_longlong

@@ -424,4 +424,14 @@ int tvref_omp_threads() {
 #endif
 }
 
+// OpenMP threads of the reference's parallel loops (a launcher such as
+// torchrun may have set OMP_NUM_THREADS=1 in the environment).
+void tvref_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 }  // extern "C"

@@ -76,13 +76,14 @@ __device__ __forceinline__ bool grid_wait(StepState* st, unsigned target) {
     return s_ok != 0;
 }
 
-// End of a row-parallel phase under tensor parallelism: every CTA of every
-// rank counts its arrival on every rank (after its partial rows), then waits
-// until its own rank has counted all of them for exchange number n.
+// End of a row-parallel phase under tensor parallelism (exchange n): every CTA
+// of every rank has set its flag slot on this rank (warp 0 watches them).
 __device__ __forceinline__ bool tp_exchange_wait(StepState* st, const TpArgs& t, unsigned n, int G) {
     __shared__ int s_tp_ok;
-    if (threadIdx.x == 0)
-        s_tp_ok = tp_count_wait(t, n * (unsigned)t.world * (unsigned)G, &st->abort, &st->status) ? 1 : 0;
+    if (threadIdx.x < 32) {
+        const bool ok = tp_flag_wait(t, n, G, &st->abort, &st->status);
+        if (threadIdx.x == 0) s_tp_ok = ok ? 1 : 0;
+    }
     __syncthreads();
     return s_tp_ok != 0;
 }
@@ -184,7 +185,7 @@ decode_step_kernel(const Phase* __restrict__ phases, int n_phases, StepState* st
         // next launch's first exchange reuses this one's slot parity.
         if (p + 1 < n_phases || exchange) {
             grid_arrive(st);   // this phase's outputs are written (includes __syncthreads)
-            if (exchange && threadIdx.x == 0) tp_count_arrive(tp);
+            if (exchange && threadIdx.x == 0) tp_flag_arrive(tp, push0 + (unsigned)tp.index + 1u);
             trace_stamp(6);
             // input-independent work for the next phase overlaps the barrier
             if (p + 1 < n_phases) phase_prepare(next, smem, G, b, warp, pos, buf);

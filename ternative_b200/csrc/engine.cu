@@ -189,6 +189,7 @@ struct tvb_context {
     bool tp_failed = false;
     float* e_x2 = nullptr;
     int n_push = 0;   // row-parallel exchanges per launch (both graphs)
+    size_t tp_xf_off = 0;   // float offset of the decode step's row-exchange flags
     size_t tp_pf_off = 0;   // float offset of the prefill region in every rank's exchange buffer
     size_t tp_key_off = 0;  // float offset of the batched step's argmax keys
     // batched decode / split-K workspace (pf_workspace)
@@ -224,6 +225,7 @@ std::vector<Phase> build_phases(tvb_context* c) {
         tpb.world = c->tp_world;
         tpb.rank = c->tp_rank;
         tpb.ld = c->H + 4;
+        tpb.xf_off = (int)c->tp_xf_off;
         for (int r = 0; r < c->tp_world; ++r) tpb.peer[r] = c->tp_peer[r];
         tpb.index = -1;
         tpb.fold = -1;
@@ -996,9 +998,12 @@ tvb_status tvb_tp_init(tvb_context* c, int rank, int world, void** exchange) {
                 "tp_init: rank %d of %d (at most %d ranks)", rank, world, kMaxTp);
     TVB_REQUIRE(c->V % world == 0, "tp_init: vocabulary %d not divisible by %d ranks", c->V, world);
     TVB_REQUIRE(!c->tp_xchg, "tp_init: already initialised");
+    TVB_REQUIRE(num_sms() <= kTpMaxGrid, "tp_init: %d SMs, the exchange flags hold %d CTAs", num_sms(), kTpMaxGrid);
     // decode exchange area, then the batched-prefill region (partial rows and
     // row sums of squares of up to max_prefill rows)
-    const size_t decode_floats = (size_t)kTpSlots + 2ull * world * (c->H + 4);
+    const size_t slots_end = (size_t)kTpSlots + 2ull * world * (c->H + 4);
+    c->tp_xf_off = (slots_end + 63) / 64 * 64;   // row-exchange flags, [world][kTpMaxGrid]
+    const size_t decode_floats = c->tp_xf_off + (size_t)world * kTpMaxGrid;
     c->tp_pf_off = (decode_floats + 63) / 64 * 64;
     const int pf_rows = std::min(c->cfg.max_prefill, c->cfg.max_seq_len);
     c->tp_key_off = c->tp_pf_off + 2 * tp_prefill_region_floats(pf_rows, c->H);

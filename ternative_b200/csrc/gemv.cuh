@@ -82,14 +82,16 @@ struct StepState {
 // that its peers write over NVLink (peer pointers from CUDA IPC):
 //   [0, 8)      flags: flags[src] = number of the last argmax exchange rank src
 //               signalled
-//   [32]        arrivals: CTAs (of all ranks) that finished a row-parallel
-//               exchange; exchange n is complete at n * world * grid
 //   [64, 80)    argmax keys of the lm_head slices (64-bit, keys[src])
 //   [128, ...)  two slots (exchange number parity) of world x ld floats:
 //               slot[src] holds rank src's partial output rows and, at [H],
 //               its partial sum of squares of the sub-norm input
+//   [xf_off, +world * kTpMaxGrid)  row-exchange flags, one per (rank, CTA):
+//               xflags[src][cta] = number of the last row-parallel exchange
+//               whose partial rows CTA cta of rank src has written here
 constexpr int kMaxTp = 8;
-constexpr int kTpFlags = 0, kTpCount = 32, kTpKeys = 64, kTpSlots = 128;
+constexpr int kTpFlags = 0, kTpKeys = 64, kTpSlots = 128;
+constexpr int kTpMaxGrid = 256;   // flag slots per rank (CTAs of the decode step)
 
 // A zero-initialised TpArgs (world 0) means no tensor parallelism.
 struct TpArgs {
@@ -102,6 +104,7 @@ struct TpArgs {
     int norm_n;           // fold: full length of the sub-norm whose partials arrive
     float* x_out;         // fold: where the folded residual is stored (CTA-partitioned)
     int vocab0;           // lm_head: first vocabulary row of this rank's slice
+    int xf_off;           // float offset of the row-exchange flags in every buffer
 };
 
 __device__ __forceinline__ float* tp_slot(float* buf, const TpArgs& t, unsigned epoch) {
@@ -117,33 +120,49 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Row-parallel exchange, arrival (thread 0 after the CTA's __syncthreads): the
-// CTA's partial rows are ordered before the count at system scope (fence +
-// relaxed adds, a release pattern), and every rank's arrival count grows by 1.
-__device__ __forceinline__ void tp_count_arrive(const TpArgs& t) {
+// Row-parallel exchange n, arrival (thread 0, after the CTA's pushes and a
+// __syncthreads): the CTA's writes are ordered at system scope, then its flag
+// slot on every rank is set to n.  One writer per slot: where every CTA of
+// every rank added 1 to one counter per rank, world x grid atomics met on one
+// address per exchange; these flag stores do not queue behind each other.
+__device__ __forceinline__ void tp_flag_arrive(const TpArgs& t, unsigned n) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int r = 0; r < t.world; ++r)
-        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(
-                         reinterpret_cast<unsigned*>(t.peer[r] + kTpCount))
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(
+                         reinterpret_cast<unsigned*>(t.peer[r] + t.xf_off) + t.rank * kTpMaxGrid + blockIdx.x),
+                     "r"(n)
                      : "memory");
 }
 
-// Row-parallel exchange, wait (thread 0): until this rank's arrival count
-// reaches `target` (bounded like every wait; on a timeout the abort latch and
-// the timeout bit are raised).
-__device__ __forceinline__ bool tp_count_wait(const TpArgs& t, unsigned target, unsigned* abort_flag,
-                                              unsigned* status) {
-    const unsigned* cnt = reinterpret_cast<const unsigned*>(t.peer[t.rank] + kTpCount);
+// Row-parallel exchange n, wait (warp 0 of every CTA): until every CTA of every
+// rank has set its flag slot here to n; each lane watches every 32nd slot.
+// Bounded like every wait (on a timeout the abort latch and the timeout bit
+// are raised); returns the same answer on every lane.
+__device__ __forceinline__ bool tp_flag_wait(const TpArgs& t, unsigned n, int G, unsigned* abort_flag,
+                                             unsigned* status) {
+    const int lane = threadIdx.x & 31;
+    const unsigned* f = reinterpret_cast<const unsigned*>(t.peer[t.rank] + t.xf_off);
     const long long t0 = clock64();
-    while ((int)(ld_acquire_sys(cnt) - target) < 0) {
-        if (*reinterpret_cast<volatile unsigned*>(abort_flag)) return false;
-        if (clock64() - t0 > kSpinLimitCycles) {
-            atomicOr(abort_flag, 1u);
-            atomicOr(status, kStatusTimeout);
-            return false;
+    bool ok = true;
+    unsigned it = 0;
+    for (int r = 0; r < t.world && ok; ++r) {
+        for (int c = lane; c < G && ok; c += 32) {
+            while ((int)(ld_acquire_sys(f + r * kTpMaxGrid + c) - n) < 0) {
+                if ((++it & 31u) != 0) continue;
+                if (*reinterpret_cast<volatile unsigned*>(abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (clock64() - t0 > kSpinLimitCycles) {
+                    atomicOr(abort_flag, 1u);
+                    atomicOr(status, kStatusTimeout);
+                    ok = false;
+                    break;
+                }
+            }
         }
     }
-    return true;
+    return __all_sync(0xffffffffu, ok);
 }
 
 // Tell every rank that this rank's writes for argmax exchange `epoch` are done
@@ -299,6 +318,14 @@ __device__ __forceinline__ float2 dot4_i8(uint32_t u, const float4& x, float2 ac
 //   [.., ..)        epilogue operands: row scale and residual per local row
 //                   (2 * rows_cap floats), RoPE cos/sin at this position
 constexpr int kChunkBytes = 2048;   // one item: 4 x 512 B warp requests
+// An item covers kChunkCols columns: one F16 row (2 KB), or two INT8 rows
+// (1 KB each) multiplied with the same activations, so that every 16 bytes of
+// INT8 weights cost the same 32 bytes of shared-memory activation reads as 16
+// bytes of F16 weights (one INT8 row per item read 64: the shared-memory pipe,
+// not HBM, bounded the INT8 rows).
+constexpr int kChunkCols = 1024;
+template <int WT>
+__host__ __device__ constexpr int rows_per_item() { return WT == WT_F16 ? 1 : 2; }
 constexpr int kDepth = 3;           // items in flight per warp
 
 struct GemvSmem {
@@ -307,7 +334,8 @@ struct GemvSmem {
 constexpr int kMaxRopeHalf = 128;
 __host__ __device__ inline GemvSmem gemv_smem_layout(int K, int esz, int rows_cap) {
     GemvSmem s;
-    const int nc = (K * esz + kChunkBytes - 1) / kChunkBytes;
+    (void)esz;
+    const int nc = (K + kChunkCols - 1) / kChunkCols;
     s.x_off = 1024;
     s.nw_off = s.x_off + ((K * 4 + 127) / 128) * 128;
     s.part_off = s.nw_off + ((K * 4 + 127) / 128) * 128;
@@ -320,9 +348,10 @@ __host__ __device__ inline int gemv_rows_cap(int n_units, int grid, int R) {
 }
 
 // Geometry of one GEMV phase for this CTA/warp: the CTA's units [U0, U1)
-// become local rows [0, nrows); items t = lrow * nc + c (row-major, so a
-// warp's items are one contiguous span of the weight matrix) are split evenly
-// over the warps, this warp owning [t0, t0 + mine).
+// become local rows [0, nrows); items t = lgrp * nc + c, lgrp a group of
+// rows_per_item local rows (row-major, so a warp's items are one contiguous
+// span of the weight matrix for F16) are split evenly over the warps, this
+// warp owning [t0, t0 + mine).
 struct GemvGeo {
     int U0, U1, nrows, t0, mine, nc, rows_cap;
 };
@@ -332,12 +361,14 @@ __device__ __forceinline__ GemvGeo gemv_geo(const GemvArgs& a, int G, int b, int
     GemvGeo g;
     const int esz = (WT == WT_F16) ? 2 : 1;
     const int n_units = gemv_units<MODE>(a, R);
-    g.nc = (a.K * esz + kChunkBytes - 1) / kChunkBytes;
+    (void)esz;
+    g.nc = (a.K + kChunkCols - 1) / kChunkCols;
     g.rows_cap = gemv_rows_cap(n_units, G, R);
     g.U0 = (int)((long long)n_units * b / G);
     g.U1 = (int)((long long)n_units * (b + 1) / G);
     g.nrows = (g.U1 - g.U0) * R;
-    const int items = g.nrows * g.nc;
+    constexpr int rpi = rows_per_item<WT>();
+    const int items = ((g.nrows + rpi - 1) / rpi) * g.nc;
     g.t0 = (int)((long long)items * warp / kGemvWarps);
     g.mine = (int)((long long)items * (warp + 1) / kGemvWarps) - g.t0;
     return g;
@@ -349,27 +380,35 @@ struct ChunkBuf {
 };
 
 // Request item k of this warp into slot j (all lanes; out-of-range -> zeros).
+// F16: the item's 2 KB of one row as 4 x 512 B.  INT8: 1 KB of each of the
+// item's two rows, [0, 2) the first row and [2, 4) the second.
 template <int MODE, int WT, int R>
 __device__ __forceinline__ void gemv_load(const GemvArgs& a, const GemvGeo& g, int k, uint4 (&dst)[4]) {
     const int esz = (WT == WT_F16) ? 2 : 1;
+    constexpr int rpi = rows_per_item<WT>();
     const int row_bytes = a.K * esz;
     const int lane = threadIdx.x & 31;
-    int bytes = 0;
-    const unsigned char* src = nullptr;
+    int bytes[rpi] = {};
+    const unsigned char* src[rpi] = {};
     if (k < g.mine) {
         const int t = g.t0 + k;
-        const int lrow = t / g.nc, c = t - lrow * g.nc;
-        int m, row;
-        if (group_row<MODE, R>(a, g.U0 + lrow / R, lrow % R, m, row)) {
-            const int off = c * kChunkBytes;
-            bytes = min(kChunkBytes, row_bytes - off);
-            src = static_cast<const unsigned char*>(a.w[m]) + (size_t)row * row_bytes + off;
+        const int lg = t / g.nc, c = t - lg * g.nc;
+#pragma unroll
+        for (int q = 0; q < rpi; ++q) {
+            const int lrow = lg * rpi + q;
+            int m, row;
+            if (lrow < g.nrows && group_row<MODE, R>(a, g.U0 + lrow / R, lrow % R, m, row)) {
+                const int off = c * kChunkCols * esz;
+                bytes[q] = min(kChunkCols * esz, row_bytes - off);
+                src[q] = static_cast<const unsigned char*>(a.w[m]) + (size_t)row * row_bytes + off;
+            }
         }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int o = 512 * i + lane * 16;
-        dst[i] = (o < bytes) ? ld_stream16(src + o) : make_uint4(0u, 0u, 0u, 0u);
+        const int q = (rpi == 1) ? 0 : (i >> 1);
+        const int o = 512 * (rpi == 1 ? i : (i & 1)) + lane * 16;
+        dst[i] = (o < bytes[q]) ? ld_stream16(src[q] + o) : make_uint4(0u, 0u, 0u, 0u);
     }
 }
 
@@ -561,9 +600,10 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
             const int k = k0 + j;
             if (k >= g.mine) break;
             const int t = g.t0 + k;
-            const int lrow = t / g.nc, c = t - lrow * g.nc;
-            const int e0 = c * (kChunkBytes / esz);   // first column of the chunk
+            const int lg = t / g.nc, c = t - lg * g.nc;
+            const int e0 = c * kChunkCols;   // first column of the chunk
             float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+            float2 accB0 = acc0, accB1 = acc0;   // INT8: the item's second row
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 if (WT == WT_F16) {
@@ -575,24 +615,37 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
                         if (i & 1) acc1 = dot8_h(buf.v[j][i], hsel ? p1 : p0, hsel ? p0 : p1, acc1);
                         else acc0 = dot8_h(buf.v[j][i], hsel ? p1 : p0, hsel ? p0 : p1, acc0);
                     }
-                } else {
+                } else if (i < 2) {
                     const int e = e0 + 512 * i + lane * 16;
                     if (e < K) {
                         // the lane's 16 activations as 4 float4, read in a rotated
-                        // order (quad (q + lane / 2) % 4): conflict-free shared memory
+                        // order (quad (q + lane / 2) % 4): conflict-free shared memory;
+                        // each is used by both rows of the item
                         const float4* xp = reinterpret_cast<const float4*>(xs + e);
+                        const float4 x0 = xp[qrot], x1 = xp[(qrot + 1) & 3], x2 = xp[(qrot + 2) & 3],
+                                     x3 = xp[(qrot + 3) & 3];
                         const uint4 w = rot_words(buf.v[j][i], qrot);
-                        acc0 = dot4_i8(w.x, xp[qrot], acc0);
-                        acc1 = dot4_i8(w.y, xp[(qrot + 1) & 3], acc1);
-                        acc0 = dot4_i8(w.z, xp[(qrot + 2) & 3], acc0);
-                        acc1 = dot4_i8(w.w, xp[(qrot + 3) & 3], acc1);
+                        acc0 = dot4_i8(w.x, x0, acc0);
+                        acc1 = dot4_i8(w.y, x1, acc1);
+                        acc0 = dot4_i8(w.z, x2, acc0);
+                        acc1 = dot4_i8(w.w, x3, acc1);
+                        const uint4 u = rot_words(buf.v[j][i + 2], qrot);
+                        accB0 = dot4_i8(u.x, x0, accB0);
+                        accB1 = dot4_i8(u.y, x1, accB1);
+                        accB0 = dot4_i8(u.z, x2, accB0);
+                        accB1 = dot4_i8(u.w, x3, accB1);
                     }
                 }
             }
             // refill this slot with the item kDepth ahead
             gemv_load<MODE, WT, R>(a, g, k + kDepth, buf.v[j]);
             const float v = warp_sum((acc0.x + acc0.y) + (acc1.x + acc1.y));
-            if (lane == 0) part[c * g.rows_cap + lrow] = v;
+            constexpr int rpi = rows_per_item<WT>();
+            if (lane == 0) part[c * g.rows_cap + lg * rpi] = v;
+            if (rpi == 2) {
+                const float vb = warp_sum((accB0.x + accB0.y) + (accB1.x + accB1.y));
+                if (lane == 0 && lg * rpi + 1 < g.nrows) part[c * g.rows_cap + lg * rpi + 1] = vb;
+            }
         }
     }
     __syncthreads();
@@ -662,7 +715,7 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
                 if (MODE == GM_PLAIN) a.y[rows[r]] = y[r];
                 else if (MODE == GM_RESID) {
                     if (push) {
-                        for (int q = 0; q < a.tp.world; ++q) a.tp.peer[q][tp_off + rows[r]] = y[r];
+                        pre_res[lu * R + r] = y[r];   // pushed below, 16 bytes at a time
                     } else {
                         a.y[rows[r]] = __fadd_rn(pre_res[lu * R + r], y[r]);
                     }
@@ -670,6 +723,28 @@ __device__ __forceinline__ void gemv_run(const GemvArgs& a, unsigned char* smem,
                     a.y[rows[r]] = y[r];
                     if (y[r] > best.v) { best.v = y[r]; best.i = rows[r] + a.tp.vocab0; }
                 }
+            }
+        }
+    }
+    if (push) {
+        // The CTA's rows [U0, U1) (R == 1: one row per unit) to every rank's
+        // slot: 16-byte stores for the aligned middle, single floats at the edges
+        // (slot offsets and ld are multiples of 4 floats).
+        __syncthreads();
+        const int r0 = g.U0, r1 = g.U1;
+        const int a0 = min(r1, (r0 + 3) & ~3), a1 = max(a0, r1 & ~3);
+        const int nv = (a1 - a0) >> 2, ne = (a0 - r0) + (r1 - a1);
+        for (int i = tid; i < a.tp.world * (nv + ne); i += kGemvThreads) {
+            const int q = i / (nv + ne), j = i - q * (nv + ne);
+            float* dst = a.tp.peer[q] + tp_off;
+            if (j < nv) {
+                const int row = a0 + 4 * j;
+                const float* v = pre_res + (row - r0);
+                *reinterpret_cast<float4*>(dst + row) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                const int e = j - nv;
+                const int row = e < a0 - r0 ? r0 + e : a1 + (e - (a0 - r0));
+                dst[row] = pre_res[row - r0];
             }
         }
     }

@@ -12,9 +12,15 @@
 // summation order and IEEE-rounded, never-contracted multiplies and adds
 // (__fmul_rn/__fadd_rn).  Packed mul/add.rn.f32x2 would halve the issue count,
 // but ptxas contracts those pairs into fused multiply-adds, which changes the
-// low bit of the delta.  Each CTA owns ROWS output rows of one tensor;
-// its 8 warps stride across the 128-column I2_S blocks of those rows.  One
-// launch covers many tensors through a by-value descriptor table.
+// low bit of the delta.  Each CTA owns a 64-row x 128-column tile of one
+// tensor (the 128 columns are one I2_S block of each row) and stages A and B
+// through shared memory 32 rank-columns at a time; each thread accumulates a
+// 4-row x 8-column register tile over j in order.  A CTA of whole rows re-read
+// all of A per 8 rows (32 bytes of L2 traffic per output at rank 64); the tile
+// reads 6.  One launch covers many tensors through a by-value descriptor table.
+// Per-row INT8 needs each row's largest magnitude before any code: the tiles
+// write the exact F16 values into a workspace and fold their rows' maxima into
+// per-row words, and a second kernel writes the codes and scales.
 #include "common.cuh"
 
 #include <algorithm>
@@ -23,18 +29,19 @@
 namespace tvb {
 
 constexpr int kMergeThreads = 256;
-constexpr int kMergeWarps = kMergeThreads / 32;
 constexpr int kMaxDescs = 192;
 constexpr int kMaxRank = 256;
+constexpr int kTileRows = 64, kTileCols = 128, kJChunk = 32;
+constexpr int kBsLd = kTileRows + 4;   // Bs row stride: 16-byte rows, 4-way store conflicts at most
 
-enum MergeMode { kOutF32 = 0, kOutF16 = 1, kOutI8Row = 2 };
+enum MergeMode { kOutF32 = 0, kOutF16 = 1, kOutF16Stage = 2 };
 
 struct MergeDescDev {
     const uint8_t* i2s;
     const float* A;
     const float* B;
-    void* dst;
-    float* row_scales;
+    void* dst;           // output; kOutF16Stage: the F16 workspace of this tensor
+    unsigned* rowmax;    // kOutF16Stage: per-row largest |F16| (as float bits)
     float scale;
     float sf;       // alpha / r, rounded once as the reference does (model.cpp:226)
     int K, N, r;
@@ -47,148 +54,165 @@ struct MergeBatch {
     int n;
 };
 
-__device__ __forceinline__ float code_value(uint32_t word, int byte, int shift, float scale) {
-    // map2bit = {-1, 0, +1, 0} (tensor.cpp:1020); value = scale * map[c].
-    uint32_t c = (word >> (8 * byte + shift)) & 3u;
-    float m = (c == 0u) ? -1.0f : (c == 2u ? 1.0f : 0.0f);
-    return __fmul_rn(scale, m);
+__device__ __forceinline__ int find_desc(const MergeBatch& b, int cta) {
+    int lo = 0, hi = b.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (b.cta_start[mid] <= cta) lo = mid; else hi = mid - 1;
+    }
+    return lo;
 }
 
-template <int ROWS, int MODE>
+template <int MODE>
 __global__ void __launch_bounds__(kMergeThreads)
-merge_kernel(const __grid_constant__ MergeBatch batch) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int cta = blockIdx.x;
-    // Locate this CTA's tensor (cta_start is ascending).
-    int lo = 0, hi = batch.n - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (batch.cta_start[mid] <= cta) lo = mid; else hi = mid - 1;
-    }
-    const MergeDescDev& D = batch.d[lo];
+merge_tile_kernel(const __grid_constant__ MergeBatch batch) {
+    __shared__ __align__(16) float As[kJChunk][kTileCols];   // As[jj][c] = A[j0 + jj][col0 + c]
+    __shared__ __align__(16) float Bs[kJChunk][kBsLd];       // Bs[jj][i] = B[row0 + i][j0 + jj]
+    const int di = find_desc(batch, blockIdx.x);
+    const MergeDescDev& D = batch.d[di];
     const int K = D.K, N = D.N, r = D.r;
-    const int row0 = (cta - batch.cta_start[lo]) * ROWS;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ctiles = K / kTileCols;
+    const int t = blockIdx.x - batch.cta_start[di];
+    const int rt = t / ctiles, ct = t - rt * ctiles;
+    const int row0 = rt * kTileRows, col0 = ct * kTileCols;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
 
-    // B rows of this CTA, transposed: Bs[j][i] = B[row0+i][j].
-    float* Bs = reinterpret_cast<float*>(smem);
-    for (int idx = tid; idx < ROWS * r; idx += kMergeThreads) {
-        int i = idx / r, j = idx - i * r;
-        Bs[j * ROWS + i] = (row0 + i < N) ? D.B[(int64_t)(row0 + i) * r + j] : 0.0f;
-    }
-    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + sizeof(float) * ROWS * kMaxRank);
-    __shared__ float wmax[kMergeWarps][ROWS];
-    float rmax[ROWS];
+    float acc[4][8];
 #pragma unroll
-    for (int i = 0; i < ROWS; ++i) rmax[i] = 0.0f;
-    __syncthreads();
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
 
-    const int nchunks = K >> 7;
-    const int src_blocks = D.ld >> 7, blk0 = D.k0 >> 7;   // I2_S blocks per source row, first block
-    const int byte_off = (lane & 7) * 4;
-    const int shift = 6 - 2 * (lane >> 3);
-    for (int c = warp; c < nchunks; c += kMergeWarps) {
-        const int col = c * 128 + lane * 4;
-        float2 acc[ROWS][2];
-#pragma unroll
-        for (int i = 0; i < ROWS; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
-        const float* Ap = D.A + D.k0 + col;
-#pragma unroll 4
-        for (int j = 0; j < r; ++j) {
-            float4 a = __ldg(reinterpret_cast<const float4*>(Ap + (int64_t)j * D.ld));
-            float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
-            float bj[ROWS];
-#pragma unroll
-            for (int i4 = 0; i4 < ROWS; i4 += 4) {
-                float4 t = *reinterpret_cast<const float4*>(Bs + j * ROWS + i4);
-                bj[i4] = t.x; bj[i4 + 1] = t.y; bj[i4 + 2] = t.z; bj[i4 + 3] = t.w;
-            }
-#pragma unroll
-            for (int i = 0; i < ROWS; ++i) {
-                // __fmul_rn/__fadd_rn are never contracted into an FMA.
-                acc[i][0].x = __fadd_rn(acc[i][0].x, __fmul_rn(a01.x, bj[i]));
-                acc[i][0].y = __fadd_rn(acc[i][0].y, __fmul_rn(a01.y, bj[i]));
-                acc[i][1].x = __fadd_rn(acc[i][1].x, __fmul_rn(a23.x, bj[i]));
-                acc[i][1].y = __fadd_rn(acc[i][1].y, __fmul_rn(a23.y, bj[i]));
-            }
+    for (int j0 = 0; j0 < r; j0 += kJChunk) {
+        const int jn = min(kJChunk, r - j0);
+        __syncthreads();   // the previous chunk is consumed
+        for (int idx = tid; idx < kJChunk * (kTileCols / 4); idx += kMergeThreads) {
+            const int jj = idx >> 5, c4 = idx & 31;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (jj < jn)
+                v = __ldg(reinterpret_cast<const float4*>(D.A + (int64_t)(j0 + jj) * D.ld + D.k0 + col0) + c4);
+            *reinterpret_cast<float4*>(&As[jj][c4 * 4]) = v;
         }
-        const float2 sf2 = make_float2(D.sf, D.sf);
+        for (int idx = tid; idx < kTileRows * kJChunk; idx += kMergeThreads) {
+            const int i = idx >> 5, jj = idx & 31;
+            Bs[jj][i] = (jj < jn && row0 + i < N) ? __ldg(D.B + (int64_t)(row0 + i) * r + j0 + jj) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 2
+        for (int jj = 0; jj < jn; ++jj) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[jj][tx * 8]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[jj][tx * 8 + 4]);
+            const float4 bv = *reinterpret_cast<const float4*>(&Bs[jj][ty * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-        for (int i = 0; i < ROWS; ++i) {
-            const int row = row0 + i;
-            if (row >= N) break;
-            const int64_t blk = (int64_t)row * src_blocks + blk0 + c;
-            uint32_t word = *reinterpret_cast<const uint32_t*>(D.i2s + blk * 32 + byte_off);
-            float2 d01 = make_float2(__fmul_rn(acc[i][0].x, sf2.x), __fmul_rn(acc[i][0].y, sf2.y));
-            float2 d23 = make_float2(__fmul_rn(acc[i][1].x, sf2.x), __fmul_rn(acc[i][1].y, sf2.y));
-            float2 b01 = make_float2(code_value(word, 0, shift, D.scale),
-                                     code_value(word, 1, shift, D.scale));
-            float2 b23 = make_float2(code_value(word, 2, shift, D.scale),
-                                     code_value(word, 3, shift, D.scale));
-            float2 v01 = make_float2(__fadd_rn(b01.x, d01.x), __fadd_rn(b01.y, d01.y));
-            float2 v23 = make_float2(__fadd_rn(b23.x, d23.x), __fadd_rn(b23.y, d23.y));
-            const int64_t off = (int64_t)row * K + col;
-            if (MODE == kOutF32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(D.dst) + off) =
-                    make_float4(v01.x, v01.y, v23.x, v23.y);
-            } else {
-                uint32_t h0 = f32_to_f16_trunc_fast(v01.x) | ((uint32_t)f32_to_f16_trunc_fast(v01.y) << 16);
-                uint32_t h1 = f32_to_f16_trunc_fast(v23.x) | ((uint32_t)f32_to_f16_trunc_fast(v23.y) << 16);
-                if (MODE == kOutF16) {
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(D.dst) + off) = make_uint2(h0, h1);
-                } else {
-                    *reinterpret_cast<uint2*>(stage + i * K + col) = make_uint2(h0, h1);
-                    // |F16 value| compares like its magnitude bits.
-                    uint32_t m = max(max(h0 & 0x7FFFu, (h0 >> 16) & 0x7FFFu),
-                                     max(h1 & 0x7FFFu, (h1 >> 16) & 0x7FFFu));
-                    rmax[i] = fmaxf(rmax[i], __half2float(__ushort_as_half((uint16_t)m)));
-                }
-            }
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[i][q] = __fadd_rn(acc[i][q], __fmul_rn(a[q], b[i]));
         }
     }
 
-    if (MODE == kOutI8Row) {
+    // epilogue: the I2_S codes of this thread's 8 columns sit in bytes
+    // (8 tx) % 32 .. + 7 of the row's 128-column block, at one bit position
+    const int src_blocks = D.ld >> 7, blk0 = D.k0 >> 7;
+    const int cb = (tx * 8) & 31, shift = 6 - 2 * ((tx * 8) >> 5);
+    __shared__ unsigned smax[kTileRows];
+    if (MODE == kOutF16Stage) {
+        for (int i = tid; i < kTileRows; i += kMergeThreads) smax[i] = 0u;
+        __syncthreads();
+    }
 #pragma unroll
-        for (int i = 0; i < ROWS; ++i) {
-            float m = warp_max(rmax[i]);
-            if (lane == 0) wmax[warp][i] = m;
+    for (int i = 0; i < 4; ++i) {
+        const int row = row0 + ty * 4 + i;
+        if (row >= N) continue;
+        const uint8_t* blk = D.i2s + ((int64_t)row * src_blocks + blk0 + ct) * 32 + cb;
+        const uint32_t words[2] = {*reinterpret_cast<const uint32_t*>(blk),
+                                   *reinterpret_cast<const uint32_t*>(blk + 4)};
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            // map2bit = {-1, 0, +1, 0} (tensor.cpp:1020); value = scale * map[c]
+            const uint32_t c = (words[q >> 2] >> (8 * (q & 3) + shift)) & 3u;
+            const float m = (c == 0u) ? -1.0f : (c == 2u ? 1.0f : 0.0f);
+            v[q] = __fadd_rn(__fmul_rn(D.scale, m), __fmul_rn(acc[i][q], D.sf));
         }
-        __syncthreads();
-        __shared__ float sscale[ROWS];
-        if (tid < ROWS) {
-            float m = 0.0f;
-            for (int w = 0; w < kMergeWarps; ++w) m = fmaxf(m, wmax[w][tid]);
-            if (m == 0.0f) m = 1.0f;
-            float s = __fdiv_rn(m, 127.0f);
-            sscale[tid] = s;
-            if (row0 + tid < N) D.row_scales[row0 + tid] = s;
-        }
-        __syncthreads();
-        const int nrows = min(ROWS, N - row0);
-        int8_t* out = static_cast<int8_t*>(D.dst) + (int64_t)row0 * K;
-        // 16 codes per thread per step, coalesced 16-byte stores.
-        for (int e = tid * 16; e < nrows * K; e += kMergeThreads * 16) {
-            const int i = e / K;
-            const float s = sscale[i];
-            const uint4 hv = *reinterpret_cast<const uint4*>(stage + e);
-            const uint4 hw = *reinterpret_cast<const uint4*>(stage + e + 8);
-            const uint32_t hs[8] = {hv.x, hv.y, hv.z, hv.w, hw.x, hw.y, hw.z, hw.w};
-            uint32_t words[4];
+        const int64_t off = (int64_t)row * K + col0 + tx * 8;
+        if (MODE == kOutF32) {
+            float4* o = reinterpret_cast<float4*>(static_cast<float*>(D.dst) + off);
+            o[0] = make_float4(v[0], v[1], v[2], v[3]);
+            o[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+            uint32_t h[4];
+            uint32_t mbits = 0;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                uint32_t acc = 0;
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    uint32_t h2 = hs[2 * q + t];
-                    float lo_v = __half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFFu)));
-                    float hi_v = __half2float(__ushort_as_half((uint16_t)(h2 >> 16)));
-                    acc |= ((uint32_t)(uint8_t)int8_code(lo_v, s)) << (16 * t);
-                    acc |= ((uint32_t)(uint8_t)int8_code(hi_v, s)) << (16 * t + 8);
-                }
-                words[q] = acc;
+                const uint32_t lo = f32_to_f16_trunc_fast(v[2 * q]), hi = f32_to_f16_trunc_fast(v[2 * q + 1]);
+                h[q] = lo | (hi << 16);
+                mbits = max(mbits, max(lo & 0x7FFFu, hi & 0x7FFFu));   // |F16| compares like its bits
             }
-            *reinterpret_cast<uint4*>(out + e) = make_uint4(words[0], words[1], words[2], words[3]);
+            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(D.dst) + off) = make_uint4(h[0], h[1], h[2], h[3]);
+            if (MODE == kOutF16Stage)
+                atomicMax(&smax[ty * 4 + i],
+                          __float_as_uint(__half2float(__ushort_as_half((uint16_t)mbits))));   // >= 0
         }
+    }
+    if (MODE == kOutF16Stage) {
+        __syncthreads();
+        for (int i = tid; i < kTileRows; i += kMergeThreads)
+            if (row0 + i < N && smax[i]) atomicMax(D.rowmax + row0 + i, smax[i]);
+    }
+}
+
+// Per-row INT8, second pass: one warp per row reads the row's exact F16
+// values and writes the codes and the row's scale (model.cpp:381-401 per row).
+struct CodeDescDev {
+    const uint16_t* f16;
+    const unsigned* rowmax;
+    int8_t* q;
+    float* row_scales;
+    int K;
+};
+struct CodeBatch {
+    CodeDescDev d[kMaxDescs];
+    int row_start[kMaxDescs + 1];
+    int n;
+};
+
+__global__ void __launch_bounds__(256) merge_codes_kernel(const __grid_constant__ CodeBatch batch, int total_rows) {
+    const int grow = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (grow >= total_rows) return;
+    int lo = 0, hi = batch.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (batch.row_start[mid] <= grow) lo = mid; else hi = mid - 1;
+    }
+    const CodeDescDev& D = batch.d[lo];
+    const int row = grow - batch.row_start[lo];
+    float mx = __uint_as_float(D.rowmax[row]);
+    if (mx == 0.0f) mx = 1.0f;
+    const float s = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) D.row_scales[row] = s;
+    const uint16_t* src = D.f16 + (int64_t)row * D.K;
+    int8_t* out = D.q + (int64_t)row * D.K;
+    for (int e = lane * 16; e < D.K; e += 32 * 16) {   // K % 128 == 0: whole 16-element groups
+        const uint4 hv = *reinterpret_cast<const uint4*>(src + e);
+        const uint4 hw = *reinterpret_cast<const uint4*>(src + e + 8);
+        const uint32_t hs[8] = {hv.x, hv.y, hv.z, hv.w, hw.x, hw.y, hw.z, hw.w};
+        uint32_t words[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t acc = 0;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const uint32_t h2 = hs[2 * q + t];
+                const float lo_v = __half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFFu)));
+                const float hi_v = __half2float(__ushort_as_half((uint16_t)(h2 >> 16)));
+                acc |= ((uint32_t)(uint8_t)int8_code(lo_v, s)) << (16 * t);
+                acc |= ((uint32_t)(uint8_t)int8_code(hi_v, s)) << (16 * t + 8);
+            }
+            words[q] = acc;
+        }
+        *reinterpret_cast<uint4*>(out + e) = make_uint4(words[0], words[1], words[2], words[3]);
     }
 }
 
@@ -254,21 +278,6 @@ __global__ void tensor_scale_kernel(float* scales) {
 // ---------------------------------------------------------------------------
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-static size_t merge_smem(int rows, int mode, int K) {
-    size_t s = sizeof(float) * rows * kMaxRank;
-    if (mode == kOutI8Row) s += (size_t)rows * K * sizeof(uint16_t);
-    return s;
-}
-
-template <int ROWS, int MODE>
-static tvb_status launch_merge(MergeBatch& b, int total_ctas, int maxK, cudaStream_t st) {
-    size_t smem = merge_smem(ROWS, MODE, maxK);
-    auto kern = merge_kernel<ROWS, MODE>;
-    TVB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<total_ctas, kMergeThreads, smem, st>>>(b);
-    return check_launch("merge_kernel");
-}
-
 static tvb_status validate(const tvb_merge_desc& d, tvb_dtype out) {
     TVB_REQUIRE(d.i2s && d.dst, "merge: null i2s/dst");
     TVB_REQUIRE(d.K > 0 && d.N > 0 && d.K % 128 == 0, "merge: K=%d must be a positive multiple of 128", d.K);
@@ -284,6 +293,10 @@ static tvb_status validate(const tvb_merge_desc& d, tvb_dtype out) {
     return TVB_OK;
 }
 
+// Per-row INT8 goes through an F16 workspace in groups of tensors of at most
+// this many bytes.
+constexpr size_t kI8WorkspaceBytes = 512ull << 20;
+
 static tvb_status merge_run(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st) {
     if (n <= 0) return TVB_OK;
     TVB_REQUIRE(descs, "merge: descs is NULL");
@@ -296,46 +309,89 @@ static tvb_status merge_run(const tvb_merge_desc* descs, int n, tvb_dtype out, c
         tvb_status s = validate(descs[i], out);
         if (s != TVB_OK) return s;
     }
-    // I8 rows stage ROWS*K F16 values in shared memory: 8 rows up to K=13312.
-    int maxK = 0;
-    for (int i = 0; i < n; ++i) maxK = std::max(maxK, descs[i].K);
-    const bool narrow = (out == TVB_I8_ROW) && merge_smem(8, kOutI8Row, maxK) > 220 * 1024;
-    if (narrow && merge_smem(4, kOutI8Row, maxK) > 220 * 1024)
-        return set_error(TVB_ERR_UNSUPPORTED, "merge: K=%d too large for per-row INT8", maxK);
-    const int rows = narrow ? 4 : 8;
-
     static thread_local MergeBatch b;
-    for (int base = 0; base < n; base += kMaxDescs) {
-        const int cnt = std::min(kMaxDescs, n - base);
-        int ctas = 0;
-        for (int i = 0; i < cnt; ++i) {
-            const tvb_merge_desc& s = descs[base + i];
-            MergeDescDev& d = b.d[i];
-            d.i2s = s.i2s;
-            d.A = s.r ? s.A : nullptr;
-            d.B = s.r ? s.B : nullptr;
-            d.dst = s.dst;
-            d.row_scales = s.row_scales;
-            d.scale = s.scale;
-            d.r = s.r;
-            d.sf = s.r ? s.alpha / (float)s.r : 0.0f;
-            d.K = s.K;
-            d.N = s.N;
-            d.k0 = s.k0;
-            d.ld = s.ld ? s.ld : s.K;
-            b.cta_start[i] = ctas;
-            ctas += (s.N + rows - 1) / rows;
+    static thread_local CodeBatch cb;
+    auto fill = [&](MergeDescDev& d, const tvb_merge_desc& s) {
+        d.i2s = s.i2s;
+        d.A = s.r ? s.A : nullptr;
+        d.B = s.r ? s.B : nullptr;
+        d.dst = s.dst;
+        d.rowmax = nullptr;
+        d.scale = s.scale;
+        d.r = s.r;
+        d.sf = s.r ? s.alpha / (float)s.r : 0.0f;
+        d.K = s.K;
+        d.N = s.N;
+        d.k0 = s.k0;
+        d.ld = s.ld ? s.ld : s.K;
+    };
+    auto tiles = [](const tvb_merge_desc& s) { return ((s.N + kTileRows - 1) / kTileRows) * (s.K / kTileCols); };
+    if (out != TVB_I8_ROW) {
+        for (int base = 0; base < n; base += kMaxDescs) {
+            const int cnt = std::min(kMaxDescs, n - base);
+            int ctas = 0;
+            for (int i = 0; i < cnt; ++i) {
+                fill(b.d[i], descs[base + i]);
+                b.cta_start[i] = ctas;
+                ctas += tiles(descs[base + i]);
+            }
+            b.cta_start[cnt] = ctas;
+            b.n = cnt;
+            if (out == TVB_F32) merge_tile_kernel<kOutF32><<<ctas, kMergeThreads, 0, st>>>(b);
+            else merge_tile_kernel<kOutF16><<<ctas, kMergeThreads, 0, st>>>(b);
+            TVB_TRY(check_launch("merge_tile_kernel"));
+        }
+        return TVB_OK;
+    }
+    // Per-row INT8: groups of tensors whose F16 images and row maxima fit the workspace.
+    size_t need = 0;
+    for (int i = 0; i < n; ++i)
+        need = std::max(need, (size_t)descs[i].N * descs[i].K * 2 + (size_t)descs[i].N * 4 + 256);
+    const size_t ws_bytes = std::max(need, std::min(kI8WorkspaceBytes, [&] {
+        size_t t = 0;
+        for (int i = 0; i < n; ++i) t += (size_t)descs[i].N * descs[i].K * 2 + (size_t)descs[i].N * 4 + 256;
+        return t;
+    }()));
+    void* ws = nullptr;
+    TVB_CUDA(cudaMallocAsync(&ws, ws_bytes, st));
+    tvb_status result = TVB_OK;
+    int i = 0;
+    while (i < n && result == TVB_OK) {
+        size_t used = 0;
+        int cnt = 0, ctas = 0, rows = 0;
+        unsigned char* p = static_cast<unsigned char*>(ws);
+        while (i + cnt < n && cnt < kMaxDescs) {
+            const tvb_merge_desc& s = descs[i + cnt];
+            const size_t f16 = ((size_t)s.N * s.K * 2 + 255) / 256 * 256, mx = ((size_t)s.N * 4 + 255) / 256 * 256;
+            if (cnt > 0 && used + f16 + mx > ws_bytes) break;
+            MergeDescDev& d = b.d[cnt];
+            fill(d, s);
+            d.dst = p + used;
+            d.rowmax = reinterpret_cast<unsigned*>(p + used + f16);
+            cb.d[cnt] = CodeDescDev{static_cast<const uint16_t*>(d.dst), d.rowmax, static_cast<int8_t*>(s.dst),
+                                    s.row_scales, s.K};
+            b.cta_start[cnt] = ctas;
+            cb.row_start[cnt] = rows;
+            ctas += tiles(s);
+            rows += s.N;
+            used += f16 + mx;
+            ++cnt;
         }
         b.cta_start[cnt] = ctas;
-        b.n = cnt;
-        tvb_status st_ = TVB_OK;
-        if (out == TVB_F32) st_ = launch_merge<8, kOutF32>(b, ctas, maxK, st);
-        else if (out == TVB_F16) st_ = launch_merge<8, kOutF16>(b, ctas, maxK, st);
-        else if (!narrow) st_ = launch_merge<8, kOutI8Row>(b, ctas, maxK, st);
-        else st_ = launch_merge<4, kOutI8Row>(b, ctas, maxK, st);
-        if (st_ != TVB_OK) return st_;
+        cb.row_start[cnt] = rows;
+        b.n = cb.n = cnt;
+        cudaError_t e = cudaMemsetAsync(ws, 0, used, st);   // row maxima start at 0 (workspace images too)
+        if (e != cudaSuccess) { result = cuda_error(e, "cudaMemsetAsync"); break; }
+        merge_tile_kernel<kOutF16Stage><<<ctas, kMergeThreads, 0, st>>>(b);
+        result = check_launch("merge_tile_kernel");
+        if (result != TVB_OK) break;
+        merge_codes_kernel<<<(rows + 7) / 8, 256, 0, st>>>(cb, rows);
+        result = check_launch("merge_codes_kernel");
+        i += cnt;
     }
-    return TVB_OK;
+    cudaError_t e = cudaFreeAsync(ws, st);
+    if (result == TVB_OK && e != cudaSuccess) result = cuda_error(e, "cudaFreeAsync");
+    return result;
 }
 
 tvb_status merge_exact(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st) {
