@@ -407,7 +407,7 @@ def tp_parity_check(world, rank, all_gather):
     agree = all(p[0] == toks for p in parts)
     full = np.concatenate([p[1] for p in parts], axis=1)
     from oracle.oracle import ModelShape, Reference, ReferenceModel
-    whole = Model.load(synth)
+    whole = Model.load(synth, exact_merge=True)   # the ranks merge exactly
     rm = ReferenceModel(Reference(), ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
                                                 cfg.num_kv_heads, cfg.intermediate_size, cfg.max_seq_len,
                                                 cfg.rope_theta, cfg.rms_norm_eps), whole.host_weights())

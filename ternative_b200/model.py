@@ -147,9 +147,12 @@ class Model:
 
     @staticmethod
     def load(synth: SyntheticModel, int8_layers=(), per_row: bool = True,
-             backend: Optional[CUDABackend] = None) -> "Model":
+             backend: Optional[CUDABackend] = None, exact_merge: bool = False) -> "Model":
         """Merge every projection on the device (F16, or INT8 for the layers in
-        ``int8_layers``) and register the result with the fused step."""
+        ``int8_layers``) and register the result with the fused step.  F16 layers
+        take the tensor-core merge (within one F16 unit in the last place of the
+        reference's apply_lora, usually identical) unless ``exact_merge``, which
+        takes the bit-exact CUDA-core merge; INT8 codes are always exact."""
         import torch
         cfg = synth.cfg
         be = backend or CUDABackend()
@@ -171,7 +174,8 @@ class Model:
             i8_scales.append(so)
         f16_layers = [li for li in range(cfg.num_layers) if f16_out[li]]
         if f16_layers:
-            be.merge_batch(synth.merge_descs(f16_out, layers=f16_layers), TVB_F16)
+            merge = be.merge_batch if exact_merge else be.merge_batch_tc
+            merge(synth.merge_descs(f16_out, layers=f16_layers), TVB_F16)
         if int8_layers and per_row:
             be.merge_batch(synth.merge_descs(i8_out, i8_scales, layers=sorted(int8_layers)),
                            TVB_I8_ROW)

@@ -84,6 +84,7 @@ def main(argv=None):
     ap.add_argument("--json", default=None, help="also write the summary here")
     ap.add_argument("--lib", default=TRACE_LIB, help="a trace build of the library")
     ap.add_argument("--norm", type=float, default=1.0, help="every norm weight of the synthetic model")
+    ap.add_argument("--int8", action="store_true", help="every layer per-row INT8 instead of F16")
     args = ap.parse_args(argv)
 
     from . import _lib
@@ -97,7 +98,7 @@ def main(argv=None):
     if args.layers:
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
     synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=0, norm_value=args.norm)
-    m = Model.load(synth)
+    m = Model.load(synth, int8_layers=range(cfg.num_layers) if args.int8 else ())
     be = m.backend
     G = torch.cuda.get_device_properties(0).multi_processor_count
     n_phases = len(KINDS) * cfg.num_layers + 1
@@ -133,7 +134,8 @@ def main(argv=None):
     }
     hdr = ["phases", "step_us", "inputs_us", "inputs_max_us", "stream_us", "stream_max_us", "epi_us",
            "arrive_us", "prep_us", "last_arrive_us", "bar_us", "exit_spread_us"]
-    print(f"{args.config}, {cfg.num_layers} layers, {G} CTAs, kv_len {pos + 2}: step {step_us:.1f} us "
+    print(f"{args.config}{' INT8' if args.int8 else ''}, {cfg.num_layers} layers, {G} CTAs, kv_len {pos + 2}: "
+          f"step {step_us:.1f} us "
           f"(CUDA events), traced span {summary['traced_span_us']:.1f} us, timer resolution "
           f"{summary['timer_resolution_ns']} ns")
     print("kind    " + " ".join(f"{h.replace('_us', ''):>11}" for h in hdr))

@@ -55,7 +55,7 @@ def _child(rank, world, port, cfg, prompt, n_new, q):
         res = {"rank": rank, "toks": toks}
         if rank == 0:
             res["full"] = np.concatenate(parts, axis=1)
-            ref = Model.load(synth)
+            ref = Model.load(synth, exact_merge=True)   # the ranks merge exactly too
             ref.backend.clear_kv_d()
             rl, _ = ref.backend.prefill(np.asarray(toks[:len(prompt)], np.int32))
             refs = [rl]
@@ -113,7 +113,7 @@ def _child_batch(rank, world, port, cfg, prompts, steps, q):
         if rank == 0:
             full = np.concatenate(parts, axis=2)         # [steps][B][V]
             ref = Model.load(SyntheticModel.generate(dataclasses.replace(cfg, max_batch=1), rank=16,
-                                                     alpha=32.0, seed=4))
+                                                     alpha=32.0, seed=4), exact_merge=True)
             errs = []
             for b, p in enumerate(prompts):
                 ref.backend.clear_kv_d()
@@ -242,7 +242,7 @@ def _child_ref(rank, world, port, cfg, prompt, n_new, q):
         if rank == 0:
             from oracle.oracle import ModelShape, Reference, ReferenceModel
             from ternative_b200.model import Model
-            whole = Model.load(synth)
+            whole = Model.load(synth, exact_merge=True)
             shape = ModelShape(cfg.vocab_size, cfg.hidden_size, cfg.num_layers, cfg.num_heads,
                                cfg.num_kv_heads, cfg.intermediate_size, cfg.max_seq_len, cfg.rope_theta,
                                cfg.rms_norm_eps)
