@@ -193,7 +193,8 @@ struct tvb_context {
     size_t tp_pf_off = 0;   // float offset of the prefill region in every rank's exchange buffer
     size_t tp_key_off = 0;  // float offset of the batched step's argmax keys
     // batched decode / split-K workspace (pf_workspace)
-    float* pf_part = nullptr;   // split-K partial sums
+    float* pf_part = nullptr;   // split-K partial sums / stream-K pieces
+    unsigned* pf_flags = nullptr;   // stream-K piece flags [SMs][4]
     size_t pf_part_floats = 0;
     float* bd_attn_part = nullptr;   // [max_batch][nh][splits][hd + 4]
     float* bd_logits = nullptr;      // [max_batch][V]
@@ -489,6 +490,8 @@ tvb_status pf_workspace(tvb_context* c) {
         {(void**)&c->bd_keys, (size_t)kMaxBatch * 8},
     };
     for (auto& a : allocs) TVB_TRY(alloc_dev(a.p, a.b));
+    TVB_TRY(alloc_dev((void**)&c->pf_flags, (size_t)num_sms() * 4 * sizeof(unsigned)));
+    TVB_CUDA(cudaMemset(c->pf_flags, 0, (size_t)num_sms() * 4 * sizeof(unsigned)));
     c->pf_part_floats = (size_t)kPfPartRows * num_sms() * 256;
     if (pf_attention_tc_supported(c->cfg.num_heads, c->cfg.num_kv_heads, c->cfg.head_dim))
         TVB_TRY(alloc_dev(&c->pf_planes, pf_attn_planes_bytes(cap, c->cfg.max_seq_len, c->cfg.num_heads,
@@ -604,6 +607,7 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot, c
             size_t off = 0;
             PfGemm g;
             g.part = c->pf_part;
+            g.flags = c->pf_flags;
             g.part_floats = c->pf_part_floats;
             g.S = n;
             g.xh = c->pf_xh;
@@ -682,6 +686,7 @@ tvb_status prefill_batched(tvb_context* c, const int* tokens, int S, int slot, c
                 lg.row_exp = c->pf_exp;
                 lg.status = &c->st->status;
                 lg.part = c->pf_part;
+                lg.flags = c->pf_flags;
                 lg.part_floats = c->pf_part_floats;
                 lg.m[0].w = static_cast<const uint16_t*>(c->tok_embd);
                 lg.m[0].rows = c->V;
@@ -778,6 +783,7 @@ tvb_status decode_batch(tvb_context* c, int B) {
         g.row_exp = c->pf_exp;
         g.status = &c->st->status;
         g.part = c->pf_part;
+        g.flags = c->pf_flags;
         g.part_floats = c->pf_part_floats;
         g.pdl = pdl;
         // attn_norm -> q, k, v -> RoPE at each row's position -> KV slot rows
@@ -847,6 +853,7 @@ tvb_status decode_batch(tvb_context* c, int B) {
     g.row_exp = c->pf_exp;
     g.status = &c->st->status;
     g.part = c->pf_part;
+    g.flags = c->pf_flags;
     g.part_floats = c->pf_part_floats;
     g.pdl = pdl;
     g.m[0].w = static_cast<const uint16_t*>(c->tok_embd) + (size_t)c->tp_rank * vs * H;
@@ -978,7 +985,7 @@ tvb_status tvb_context_destroy(tvb_context* c) {
                    c->e_attn, c->e_h, c->e_logits, c->attn_part, c->kcache, c->vcache,
                    c->rope_cos, c->rope_sin, c->st, c->hist, c->d_phases,
                    c->pf_x, c->pf_q, c->pf_attn, c->pf_h, c->pf_xh, c->pf_xl, c->pf_exp, c->pf_tok,
-                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes, c->pf_inv, c->pf_part, c->bd_attn_part,
+                   c->pf_w16, c->e_x2, c->tp_xchg, c->pf_planes, c->pf_inv, c->pf_part, c->pf_flags, c->bd_attn_part,
                    c->bd_logits, c->bd_io, c->bd_keys};
     for (void* p : dev)
         if (p) cudaFree(p);

@@ -163,13 +163,22 @@ tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* 
         const size_t plane = (size_t)M * K;
         const size_t wide = wt ? (size_t)N * K : 0;
         unsigned char* buf = nullptr;
-        const size_t bytes = (2 * plane + wide) * 2 + (size_t)M * 4 + 256;
+        // then the split-K / stream-K workspace: SMs x 128 x 256 partial sums
+        // and SMs x 4 zeroed piece flags
+        const size_t part_floats = (size_t)num_sms() * 128 * 256;
+        const size_t head = ((2 * plane + wide) * 2 + (size_t)M * 4 + 255) & ~(size_t)255;
+        const size_t bytes = head + part_floats * 4 + (size_t)num_sms() * 16;
         TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&buf), bytes, st));
         uint16_t* xh = reinterpret_cast<uint16_t*>(buf);
         uint16_t* xl = xh + plane;
         uint16_t* w16 = xl + plane;
         int* ex = reinterpret_cast<int*>(w16 + wide);
-        tvb_status s = pf_norm_split(x, nullptr, M, K, 0.f, xh, xl, ex, st);
+        float* part = reinterpret_cast<float*>(buf + head);
+        unsigned* flags = reinterpret_cast<unsigned*>(part + part_floats);
+        tvb_status s = TVB_OK;
+        const cudaError_t me = cudaMemsetAsync(flags, 0, (size_t)num_sms() * 16, st);
+        if (me != cudaSuccess) s = cuda_error(me, "cudaMemsetAsync");
+        if (s == TVB_OK) s = pf_norm_split(x, nullptr, M, K, 0.f, xh, xl, ex, st);
         if (s == TVB_OK && wt) s = pf_i8_to_f16(static_cast<const int8_t*>(w->w), wide, w16, st);
         if (s == TVB_OK) {
             PfGemm g;
@@ -185,6 +194,9 @@ tvb_status tvb_matmul(float* y, const float* x, int M, int K, const tvb_weight* 
             g.m[0].scale = ts;
             g.y = y;
             g.ldy = N;
+            g.part = part;
+            g.part_floats = part_floats;
+            g.flags = flags;
             s = pf_gemm(g, st);
         }
         cudaFreeAsync(buf, st);

@@ -44,10 +44,21 @@ constexpr int kPfHalf = 128 * kPfBK * 2;           // 16 KB weight half-tile per
 // NH = 128-row weight halves per tile (2: 256 rows, the default; 1: 128 rows
 // for projections with too few 256-row tiles to cover the SMs)
 __host__ __device__ constexpr int pf_stage_bytes(int nh) { return 2 * kPfPlane + nh * kPfHalf; }
-__host__ __device__ constexpr int pf_smem_bytes(int nh) { return kPfStages * pf_stage_bytes(nh) + 1024 + 256; }
+// after the stage ring: 1 KB of barriers, then two 4 KB output stages (32 x 32
+// floats, 1024-byte aligned for the 128-byte swizzle) per epilogue warp
+constexpr int kPfBarBytes = 1024;
+constexpr int kPfOutStage = 32 * 32 * 4;
+constexpr int kPfOutBytes = 4 * 2 * kPfOutStage;
+__host__ __device__ constexpr int pf_smem_bytes(int nh) {
+    return kPfStages * pf_stage_bytes(nh) + 1024 + kPfBarBytes + kPfOutBytes;
+}
 
 struct PfMaps {
     CUtensorMap xh, xl, w[3];
+    // epilogue outputs (PfArgs::tma_out): STORE / RESID / GATEUP: out[0] over
+    // y [S][rows0]; QKV: out[0..2] over q_out [S][nh * hd] and this layer's K / V
+    // cache rows [pos0 + S][nkv * hd].  F32, 32 x 32 boxes, 128-byte swizzle.
+    CUtensorMap out[3];
 };
 
 struct PfArgs {
@@ -70,6 +81,12 @@ struct PfArgs {
     float* part;             // split-K: raw partials [ksplit][S][width]
     int ksplit, width;       // width = tiles * 128 * NH
     int w_static;            // no earlier kernel of the stream writes the weights
+    // persistent stream-K kernel (pf_gemm_sk_kernel)
+    int sk_total;            // k-block iterations of all tiles: units x nk
+    int sk_mtiles;           // token tiles per weight tile (unit u: weight tile u / sk_mtiles)
+    unsigned sk_epoch;       // value this launch writes into the flags of finished partial sums
+    unsigned* sk_flags;      // [gridDim.x][4]: one per epilogue warp
+    int tma_out;             // outputs leave through TMA stores (maps.out), else per-thread stores
 };
 
 // Position of activation row s, and the offset of its KV cache slot.
@@ -129,6 +146,192 @@ __device__ __forceinline__ void pf_store32(float* dst, const float (&v)[32], int
 __device__ __forceinline__ void pf_fail(const PfArgs& a, volatile int* abort_flag) {
     *abort_flag = 1;
     if (a.status) atomicOr(a.status, kStatusTimeout);
+}
+
+// While the MMAs of a tile run, its epilogue warp asks L2 for the RoPE rows of
+// its 32 positions (QKV), which later weight traffic has usually evicted.
+template <int NH>
+__device__ __forceinline__ void pf_epilogue_prefetch(const PfArgs& a, int s_base, int lane) {
+    const int nrows = min(32, a.S - s_base);
+    if (a.mode != PF_QKV || nrows <= 0) return;
+    const int half = a.hd >> 1;
+    for (int i = lane; i < 32 * 2; i += 32) {
+        const int r = i >> 1;
+        if (r >= nrows) continue;
+        const size_t o = (size_t)pf_pos(a, s_base + r) * half + (i & 1) * 32;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.rope_cos + o));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.rope_sin + o));
+    }
+}
+
+// This lane's row scale 2^row_exp (1 past the rows).
+__device__ __forceinline__ float pf_e2(const PfArgs& a, int s) {
+    return (s < a.S && a.row_exp) ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
+}
+
+// TMA stores of a 32 x 32 F32 box from shared memory (bulk async-groups).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+// y[box] += box (F32 add, one rounding per element)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most one group of this thread still reading shared memory
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every group of this thread complete (its writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Where the finished 32-column chunks of one warp's 32 token rows go.  TMA
+// mode: the warp's rows are written into one of its two 128-byte-swizzled
+// shared-memory boxes and lane 0 issues a tensor store (or reduce-add) of the
+// 32 x 32 box; the tensor map clips rows past S and columns past the matrix.
+// Otherwise: per-thread stores of the row (lanes past S store nothing).
+struct PfEmit {
+    const PfMaps* maps;
+    uint32_t box[2];   // this warp's two stages (shared addresses)
+    int nb;            // stage of the next box
+    int lane;
+    bool tma;
+    bool srow;         // this lane's row exists
+
+    // which: tensor map index; (x, y): box origin (column, row of the warp's
+    // first row); dst / count / add: the per-thread fallback for this lane's row
+    __device__ __forceinline__ void put(int which, int x, int y, bool add, float* dst, int count,
+                                        const float (&v)[32]) {
+        if (!tma) {
+            if (srow) pf_store32(dst, v, count, add);
+            return;
+        }
+        if (lane == 0) bulk_wait_read1();   // the box used two puts ago has been read
+        __syncwarp();
+        const uint32_t b = box[nb];
+        nb ^= 1;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(b + sw128_offset(lane, c)), "f"(v[4 * c]),
+                         "f"(v[4 * c + 1]), "f"(v[4 * c + 2]), "f"(v[4 * c + 3])
+                         : "memory");
+        fence_proxy_async_smem_cta();
+        __syncwarp();
+        if (lane == 0) {
+            if (add) tma_reduce_add_2d(&maps->out[which], x, y, b);
+            else tma_store_2d(&maps->out[which], x, y, b);
+            bulk_commit();
+        }
+    }
+    // before the stages are used otherwise, or the results are needed
+    __device__ __forceinline__ void drain_reads() {
+        if (tma && lane == 0) bulk_wait_read0();
+        __syncwarp();
+    }
+    __device__ __forceinline__ void finish() {
+        if (tma && lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+};
+
+// Epilogue of one 128-token x (128 * NH)-row tile for this thread's token row
+// s (warp rows s_base .. s_base + 31): get(col, v) yields the row's sums of
+// accumulator columns [col, col + 32) already scaled by the row's 2^row_exp
+// (warp-collective: every lane calls it, in the same order); every finished
+// 32-column chunk leaves through `out`.
+template <int NH, class Get>
+__device__ __forceinline__ void pf_tile_epilogue(const PfArgs& a, int s_base, int lane, const int (&mi)[2],
+                                                 const int (&row)[2], const bool (&hv)[2], Get&& get, PfEmit& out) {
+    const int s = s_base + lane;
+    float v0[32], v1[32];
+    if (a.mode == PF_GATEUP) {
+        // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
+        for (int c = 0; c < 4; ++c) {
+            __syncwarp();
+            get(c * 32, v0);
+            get(128 + c * 32, v1);
+            const int n0 = row[0] + c * 32;
+            if (!(hv[0] && hv[1]) || n0 >= a.rows[0]) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int n = min(n0 + j, a.rows[0] - 1);
+                const float g = __fmul_rn(v0[j], pf_row_scale(a, 0, n));
+                const float u = __fmul_rn(v1[j], pf_row_scale(a, 1, n));
+                const float gr = fmaxf(g, 0.0f);
+                v0[j] = __fmul_rn(__fmul_rn(gr, gr), u);
+            }
+            out.put(0, n0, s_base, false, a.y + (size_t)s * a.ldy + n0, a.rows[0] - n0, v0);
+        }
+    } else if (a.mode == PF_QKV) {
+        const int half = a.hd >> 1;   // 64
+        const int pos = s < a.S ? pf_pos(a, s) : 0;
+        for (int h = 0; h < NH; ++h) {
+            const int head = row[h] / a.hd;
+            for (int c = 0; c < 2; ++c) {
+                __syncwarp();
+                // RoPE factors of this row's position (2 x 128 contiguous bytes)
+                float4 cs4[8], sn4[8];
+                const bool rope = hv[h] && mi[h] < 2;
+                if (rope) {
+                    const float4* cp = reinterpret_cast<const float4*>(a.rope_cos + (size_t)pos * half + c * 32);
+                    const float4* sp = reinterpret_cast<const float4*>(a.rope_sin + (size_t)pos * half + c * 32);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        cs4[t] = __ldg(cp + t);
+                        sn4[t] = __ldg(sp + t);
+                    }
+                }
+                get(h * 128 + c * 32, v0);
+                get(h * 128 + half + c * 32, v1);
+                if (!hv[h]) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int d = c * 32 + j;
+                    float y0 = __fmul_rn(v0[j], pf_row_scale(a, mi[h], row[h] + d));
+                    float y1 = __fmul_rn(v1[j], pf_row_scale(a, mi[h], row[h] + d + half));
+                    if (rope) {
+                        // NeoX pair (d, d + hd/2), tensor.cpp:918-925
+                        const float4 c4 = cs4[j >> 2], s4 = sn4[j >> 2];
+                        const float cs = (j & 3) == 0 ? c4.x : (j & 3) == 1 ? c4.y : (j & 3) == 2 ? c4.z : c4.w;
+                        const float sn = (j & 3) == 0 ? s4.x : (j & 3) == 1 ? s4.y : (j & 3) == 2 ? s4.z : s4.w;
+                        const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
+                        const float t1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
+                        y0 = t0;
+                        y1 = t1;
+                    }
+                    v0[j] = y0;
+                    v1[j] = y1;
+                }
+                float* dst;
+                if (mi[h] == 0) dst = a.q_out + (size_t)s * a.nh * a.hd + head * a.hd;
+                else
+                    dst = (mi[h] == 1 ? a.kcache : a.vcache) + pf_slot(a, s) + (size_t)pos * a.nkv * a.hd +
+                          head * a.hd;
+                // q rows are token rows; K/V rows are positions pos0 + s
+                const int y = mi[h] == 0 ? s_base : a.pos0 + s_base;
+                out.put(mi[h], head * a.hd + c * 32, y, false, dst + c * 32, 32, v0);
+                out.put(mi[h], head * a.hd + half + c * 32, y, false, dst + half + c * 32, 32, v1);
+            }
+        }
+    } else {
+        const bool add = a.mode == PF_RESID;
+        for (int h = 0; h < NH; ++h) {
+            for (int c = 0; c < 4; ++c) {
+                __syncwarp();
+                get(h * 128 + c * 32, v0);
+                const int n0 = row[h] + c * 32;
+                if (!hv[h] || n0 >= a.rows[0]) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v0[j] = __fmul_rn(v0[j], pf_row_scale(a, 0, min(n0 + j, a.rows[0] - 1)));
+                out.put(0, n0, s_base, add, a.y + (size_t)s * a.ldy + n0, a.rows[0] - n0, v0);
+            }
+        }
+    }
 }
 
 template <int NH>
@@ -233,6 +436,7 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         const int q = warp & 3;
         const int s = s0 + 32 * q + lane;
         const bool srow = s < a.S;
+        if (gridDim.z == 1) pf_epilogue_prefetch<NH>(a, s0 + 32 * q, lane);
         const bool ok = mbar_wait_bounded(done, 0u);
         tc_fence_after();
         if (!ok) pf_fail(a, abort_flag);
@@ -243,9 +447,8 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
             tmem_wait_ld();
         };
         if (ok && !*abort_flag) {
-            const float e2 = (srow && a.row_exp) ? ldexpf(1.0f, a.row_exp[s]) : 1.0f;
-            uint32_t r0[32], r1[32];
-            float v0[32], v1[32];
+            uint32_t r0[32];
+            float v0[32];
             if (gridDim.z > 1) {
                 // split-K: raw sums of this k range; pf_splitk_epilogue finishes
                 float* dst = a.part + ((size_t)blockIdx.z * a.S + s) * a.width + (size_t)tile * 128 * NH;
@@ -257,78 +460,16 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
                     for (int j = 0; j < 32; ++j) v0[j] = __uint_as_float(r0[j]);
                     pf_store32(dst + c * 32, v0, 32, false);
                 }
-            } else if (a.mode == PF_GATEUP) {
-                // relu2_d then mul_d (ops_cuda.cu:123-130, 116-121)
-                for (int c = 0; c < 4; ++c) {
-                    __syncwarp();
-                    fetch(c * 32, r0);
-                    fetch(128 + c * 32, r1);
-                    const int n0 = row[0] + c * 32;
-                    if (srow && hv[0] && hv[1] && n0 < a.rows[0]) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = min(n0 + j, a.rows[0] - 1);
-                            const float g = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, 0, n));
-                            const float u = __fmul_rn(__uint_as_float(r1[j]) * e2, pf_row_scale(a, 1, n));
-                            const float gr = fmaxf(g, 0.0f);
-                            v0[j] = __fmul_rn(__fmul_rn(gr, gr), u);
-                        }
-                        pf_store32(a.y + (size_t)s * a.ldy + n0, v0, a.rows[0] - n0, false);
-                    }
-                }
-            } else if (a.mode == PF_QKV) {
-                const int half = a.hd >> 1;   // 64
-                for (int h = 0; h < NH; ++h) {
-                    const int head = row[h] / a.hd;
-                    for (int c = 0; c < 2; ++c) {
-                        __syncwarp();
-                        fetch(h * 128 + c * 32, r0);
-                        fetch(h * 128 + half + c * 32, r1);
-                        if (!(srow && hv[h])) continue;
-                        const int pos = pf_pos(a, s);
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int d = c * 32 + j;
-                            float y0 = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, mi[h], row[h] + d));
-                            float y1 = __fmul_rn(__uint_as_float(r1[j]) * e2,
-                                                 pf_row_scale(a, mi[h], row[h] + d + half));
-                            if (mi[h] < 2) {
-                                // NeoX pair (d, d + hd/2), tensor.cpp:918-925
-                                const float cs = __ldg(a.rope_cos + (size_t)pos * half + d);
-                                const float sn = __ldg(a.rope_sin + (size_t)pos * half + d);
-                                const float t0 = __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
-                                const float t1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, cs));
-                                y0 = t0;
-                                y1 = t1;
-                            }
-                            v0[j] = y0;
-                            v1[j] = y1;
-                        }
-                        float* dst;
-                        if (mi[h] == 0) dst = a.q_out + (size_t)s * a.nh * a.hd + head * a.hd;
-                        else
-                            dst = (mi[h] == 1 ? a.kcache : a.vcache) + pf_slot(a, s) + (size_t)pos * a.nkv * a.hd +
-                                  head * a.hd;
-                        pf_store32(dst + c * 32, v0, 32, false);
-                        pf_store32(dst + half + c * 32, v1, 32, false);
-                    }
-                }
             } else {
-                const bool add = a.mode == PF_RESID;
-                for (int h = 0; h < NH; ++h) {
-                    for (int c = 0; c < 4; ++c) {
-                        __syncwarp();
-                        fetch(h * 128 + c * 32, r0);
-                        const int n0 = row[h] + c * 32;
-                        if (!(srow && hv[h]) || n0 >= a.rows[0]) continue;
+                const uint32_t ob = base + (uint32_t)(kPfStages * kPfStage + kPfBarBytes + q * 2 * kPfOutStage);
+                PfEmit out{&maps, {ob, ob + (uint32_t)kPfOutStage}, 0, lane, a.tma_out != 0, srow};
+                const float e2 = pf_e2(a, s);
+                pf_tile_epilogue<NH>(a, s0 + 32 * q, lane, mi, row, hv, [&](int col, float (&v)[32]) {
+                    fetch(col, r0);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = min(n0 + j, a.rows[0] - 1);
-                            v0[j] = __fmul_rn(__uint_as_float(r0[j]) * e2, pf_row_scale(a, 0, n));
-                        }
-                        pf_store32(a.y + (size_t)s * a.ldy + n0, v0, a.rows[0] - n0, add);
-                    }
-                }
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]) * e2;
+                }, out);
+                out.finish();
             }
         }
         tc_fence_before();
@@ -344,6 +485,301 @@ pf_gemm_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfAr
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols)
                      : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent stream-K GEMM.  The U = weight tiles x token tiles output tiles
+// ("units", unit u: weight tile u / mtiles, token tile u % mtiles), each nk
+// k-blocks long, are laid end to end and CTA c of G takes the iterations
+// [T c / G, T (c + 1) / G) of the T = U nk, so every SM gets the same number of
+// k-blocks whatever U is.  A CTA's range is a run of segments (the part of one
+// unit inside the range); the TMA producer and the MMA warp run through them
+// without draining the stage ring, and the accumulator is double-buffered in
+// TMEM (2 x 128 * NH columns), so the epilogue of one segment overlaps the
+// MMAs of the next.  A unit cut by range boundaries is finished by its owner,
+// the CTA holding its first k-block (always the last segment of the owner's
+// range): every later CTA that holds a piece of it (its first segment) stores
+// the piece's raw sums in its workspace slot part[c] ([128 tokens][128 * NH])
+// and sets its flags (one per epilogue warp) to this launch's epoch; the owner
+// waits for those flags, adds the pieces in k order to its own sums and runs
+// the epilogue.  Pieces are computed first and owners wait last, so no CTA
+// waits on one that is waiting; with at most one CTA per SM and G <= SMs all
+// CTAs are resident together.  Every wait is bounded.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int sk_begin(const PfArgs& a, int c) {
+    return (int)((long long)a.sk_total * c / gridDim.x);
+}
+
+struct PfSeg {
+    int u, kb0, nkb;
+    bool piece;   // starts inside its unit: raw sums go to this CTA's workspace slot
+    int helpers;  // owner of a unit that later CTAs finish: how many hold pieces of it
+};
+
+__device__ __forceinline__ PfSeg pf_seg(const PfArgs& a, int it, int it1) {
+    PfSeg g;
+    g.u = it / a.nk;
+    g.kb0 = it - g.u * a.nk;
+    const int uend = (g.u + 1) * a.nk;
+    const int end = min(it1, uend);
+    g.nkb = end - it;
+    g.piece = g.kb0 > 0;
+    g.helpers = 0;
+    if (!g.piece && end < uend)
+        for (int c = blockIdx.x + 1; c < (int)gridDim.x && sk_begin(a, c) < uend; ++c) ++g.helpers;
+    return g;
+}
+
+// Stream-K piece workspace: slot c (one per CTA) holds, per epilogue warp q and
+// 32-column chunk, 8 float4 slices of the warp's 32 rows, lane-minor, so that
+// writer (the piece's CTA) and reader (the owner) both move 512 contiguous
+// bytes per instruction.  Float4 index of (slot, q, chunk, slice 0, lane).
+__device__ __forceinline__ size_t pf_piece_idx(int slot, int q, int chunk, int W, int lane) {
+    return ((((size_t)slot * 4 + q) * (W / 32) + chunk) * 8) * 32 + lane;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int NH>
+__global__ void __launch_bounds__(kPfThreads, 1)
+pf_gemm_sk_kernel(const __grid_constant__ PfMaps maps, const __grid_constant__ PfArgs a) {
+    constexpr int kPfStage = pf_stage_bytes(NH);
+    constexpr int W = 128 * NH;                 // accumulator columns of one tile
+    constexpr uint32_t kCols = 2 * W;           // two accumulators
+    extern __shared__ unsigned char pf_smem_raw[];
+    const uint32_t raw = smem_u32(pf_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* smem = pf_smem_raw + (base - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPfStages * kPfStage);
+    uint64_t* empty = full + kPfStages;
+    uint64_t* acc_full = empty + kPfStages;     // [2] MMA -> epilogue
+    uint64_t* acc_empty = acc_full + 2;         // [2] epilogue (4 warps) -> MMA
+    uint64_t* drain = acc_empty + 2;            // every MMA issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued = const_cast<int*>(abort_flag) + 1;
+    int* consumed = issued + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int it0 = sk_begin(a, blockIdx.x), it1 = sk_begin(a, blockIdx.x + 1);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPfStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *issued = 0;
+        *consumed = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) tmem_alloc(tmem_slot, kCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // (programmatic launch) the activations come from the previous kernel
+    pdl_launch_dependents();
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer: one TMA ring through all segments -----------------------------
+        prefetch_tmap(&maps.xh);
+        if (a.use_lo) prefetch_tmap(&maps.xl);
+        int i = 0;
+        bool ok = true;
+        for (int it = it0; it < it1 && ok;) {
+            const PfSeg g = pf_seg(a, it, it1);
+            it += g.nkb;
+            const int tile = g.u / a.sk_mtiles, s0 = (g.u - tile * a.sk_mtiles) * kPfBM;
+            int mi[2] = {0, 0}, row[2] = {0, 0};
+            bool hv[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) hv[h] = h < NH && pf_half(a, NH, tile, h, mi[h], row[h]);
+            const uint32_t bytes =
+                (uint32_t)(kPfPlane * (a.use_lo ? 2 : 1) + (hv[0] ? kPfHalf : 0) + (hv[1] ? kPfHalf : 0));
+            for (int k = 0; k < g.nkb; ++k, ++i) {
+                const int s = i % kPfStages, r = i / kPfStages, kx = (g.kb0 + k) * kPfBK;
+                if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) {
+                    pf_fail(a, abort_flag);
+                    ok = false;
+                    break;
+                }
+                if (*abort_flag) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t st = base + (uint32_t)(s * kPfStage);
+                mbar_expect_tx(&full[s], bytes);
+                tma_load_2d(st, &maps.xh, kx, s0, &full[s]);
+                if (a.use_lo) tma_load_2d(st + kPfPlane, &maps.xl, kx, s0, &full[s]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    if (hv[h]) tma_load_2d(st + 2 * kPfPlane + h * kPfHalf, &maps.w[mi[h]], kx, row[h], &full[s]);
+            }
+        }
+        *issued = i;
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer: accumulator j & 1 for segment j -----------------------------
+        constexpr uint32_t idesc = umma_idesc_f16(kPfBM, W);
+        int i = 0, j = 0;
+        bool ok = true;
+        for (int it = it0; it < it1 && ok; ++j) {
+            const PfSeg g = pf_seg(a, it, it1);
+            it += g.nkb;
+            const int buf = j & 1;
+            if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], (uint32_t)(((j >> 1) - 1) & 1))) {
+                pf_fail(a, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(buf * W);
+            for (int k = 0; k < g.nkb; ++k) {
+                const int s = i % kPfStages, r = i / kPfStages;
+                if (!mbar_wait_bounded(&full[s], (uint32_t)(r & 1))) {
+                    pf_fail(a, abort_flag);
+                    ok = false;
+                    break;
+                }
+                ++i;
+                tc_fence_after();
+                const uint32_t st = base + (uint32_t)(s * kPfStage);
+#pragma unroll
+                for (int kk = 0; kk < kPfBK / 16; ++kk) {
+                    const uint64_t bdesc = sw128_desc(st + 2 * kPfPlane + kk * 32);
+                    tc_mma(d, sw128_desc(st + kk * 32), bdesc, idesc, (k | kk) != 0 ? 1u : 0u);
+                    if (a.use_lo) tc_mma(d, sw128_desc(st + kPfPlane + kk * 32), bdesc, idesc, 1u);
+                }
+                tc_commit(&empty[s]);   // stage s is free once these MMAs have read it
+            }
+            tc_commit(&acc_full[buf]);  // (also after a failure: the epilogue sees the abort flag)
+        }
+        *consumed = i;
+        tc_commit(drain);
+        if (!mbar_wait_bounded(drain, 0u)) pf_fail(a, abort_flag);
+    } else if (warp >= 4) {
+        // ---- epilogue: warp q owns TMEM lanes (token rows) 32q .. 32q + 31 -----------
+        const int q = warp & 3;
+        const uint32_t ob = base + (uint32_t)(kPfStages * kPfStage + kPfBarBytes + q * 2 * kPfOutStage);
+        PfEmit out{&maps, {ob, ob + (uint32_t)kPfOutStage}, 0, lane, a.tma_out != 0, true};
+        int j = 0;
+        for (int it = it0; it < it1; ++j) {
+            const PfSeg g = pf_seg(a, it, it1);
+            it += g.nkb;
+            const int buf = j & 1;
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            const int tile = g.u / a.sk_mtiles, s_base = (g.u - tile * a.sk_mtiles) * kPfBM + 32 * q;
+            int mi[2] = {0, 0}, row[2] = {0, 0};
+            bool hv[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) hv[h] = h < NH && pf_half(a, NH, tile, h, mi[h], row[h]);
+            if (!g.piece) pf_epilogue_prefetch<NH>(a, s_base, lane);
+            const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[buf], (uint32_t)((j >> 1) & 1)));
+            tc_fence_after();
+            if (!got) {
+                if (lane == 0) pf_fail(a, abort_flag);
+                break;
+            }
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;   // the sums may be incomplete
+            const uint32_t trow = tmem + (uint32_t)(buf * W) + ((uint32_t)(32 * q) << 16);
+            const float e2 = pf_e2(a, s_base + lane);
+            // this lane's row of accumulator columns [col, col + 32), times 2^row_exp
+            auto tm = [&](int col, float (&v)[32]) {
+                uint32_t r0[32];
+                tmem_ld32(trow + col, r0);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(r0[t]) * e2;
+            };
+            if (g.piece) {
+                // the warp's 32 rows (scaled): each 32-column chunk as 8
+                // float4 slices of 32 lanes, so every store is 512 contiguous bytes
+                float4* dst = reinterpret_cast<float4*>(a.part) + pf_piece_idx(blockIdx.x, q, 0, W, lane);
+                float v[32];
+                for (int c = 0; c < W / 32; ++c) {
+                    tm(c * 32, v);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        dst[(c * 8 + t) * 32] = make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+                }
+                // the warp's rows are stored: publish them (release orders the
+                // whole warp's stores, which __syncwarp makes this lane's)
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence();
+                    st_release_gpu(a.sk_flags + (size_t)blockIdx.x * 4 + q, a.sk_epoch);
+                }
+            } else {
+                bool fine = true;
+                for (int h = 1; h <= g.helpers && fine; ++h) {
+                    const unsigned* f = a.sk_flags + (size_t)(blockIdx.x + h) * 4 + q;
+                    const long long t0 = clock64();
+                    while (ld_acquire_u32_gpu(f) != a.sk_epoch) {
+                        if (*abort_flag || clock64() - t0 > kSpinLimitCycles) {
+                            fine = false;
+                            break;
+                        }
+                    }
+                }
+                if (!__all_sync(0xffffffffu, fine)) {
+                    if (lane == 0) pf_fail(a, abort_flag);
+                    break;
+                }
+                out.srow = s_base + lane < a.S;
+                // the later pieces of this unit (slots blockIdx.x + 1 .., this
+                // lane's row, stored scaled), added in k order
+                const int helpers = g.helpers;
+                pf_tile_epilogue<NH>(a, s_base, lane, mi, row, hv, [&](int col, float (&v)[32]) {
+                    tm(col, v);
+                    for (int h = 0; h < helpers; ++h) {
+                        const float4* p4 = reinterpret_cast<const float4*>(a.part) +
+                                           pf_piece_idx(blockIdx.x + 1 + h, q, col / 32, W, lane);
+                        float4 x[8];
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) x[t] = __ldcg(p4 + t * 32);
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            v[4 * t] = __fadd_rn(v[4 * t], x[t].x);
+                            v[4 * t + 1] = __fadd_rn(v[4 * t + 1], x[t].y);
+                            v[4 * t + 2] = __fadd_rn(v[4 * t + 2], x[t].z);
+                            v[4 * t + 3] = __fadd_rn(v[4 * t + 3], x[t].w);
+                        }
+                    }
+                }, out);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+        out.finish();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort_flag) {
+        // leave no TMA write in flight into this CTA's shared memory
+        for (int kb = *consumed; kb < *issued; ++kb)
+            mbar_wait_bounded(&full[kb % kPfStages], (uint32_t)((kb / kPfStages) & 1));
+    }
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kCols);
     }
 }
 
@@ -704,6 +1140,30 @@ static tvb_status encode_f16(CUtensorMap* m, const void* p, int rows, int K, int
     return TVB_OK;
 }
 
+// F32 output matrix [rows][cols] (row pitch stride_bytes) for the epilogue's
+// TMA stores: 32 x 32 boxes, 128-byte swizzle (matching PfEmit's shared boxes).
+static tvb_status encode_f32_out(CUtensorMap* m, const float* p, int cols, int rows, size_t stride_bytes) {
+    tvb_status st;
+    auto fn = encode_fn(&st);
+    if (!fn) return st;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride_bytes};
+    const cuuint32_t box[2] = {32u, 32u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(TVB_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+    return TVB_OK;
+}
+
+// The epilogue writes through TMA when every output matrix has a 16-byte
+// aligned base and row pitch (and the K/V rows of a QKV tile are consecutive
+// positions); otherwise through per-thread stores.
+static bool pf_out_aligned(const void* p, size_t pitch_bytes) {
+    return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && pitch_bytes % 16 == 0;
+}
+
 static tvb_status pf_prepare() {
     static std::once_flag once;
     static cudaError_t err = cudaSuccess;
@@ -711,6 +1171,12 @@ static tvb_status pf_prepare() {
         err = cudaFuncSetAttribute(pf_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem_bytes(2));
         if (err == cudaSuccess)
             err = cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       pf_smem_bytes(1));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(pf_gemm_sk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       pf_smem_bytes(2));
+        if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(pf_gemm_sk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        pf_smem_bytes(1));
         if (err == cudaSuccess)
             err = cudaFuncSetAttribute(pf_gemm_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -779,6 +1245,50 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
         halves = (g.m[0].rows + 127) / 128;
     }
     const int mtiles = (g.S + kPfBM - 1) / kPfBM;
+    if (!small) {
+        if (g.mode == PF_QKV) {
+            const size_t qp = (size_t)g.nh * g.hd * 4, kp = (size_t)g.nkv * g.hd * 4;
+            a.tma_out = !g.row_pos && pf_out_aligned(g.q_out, qp) && pf_out_aligned(g.kcache, kp) &&
+                        pf_out_aligned(g.vcache, kp);
+            if (a.tma_out) {
+                TVB_TRY(encode_f32_out(&maps.out[0], g.q_out, g.nh * g.hd, g.S, qp));
+                TVB_TRY(encode_f32_out(&maps.out[1], g.kcache, g.nkv * g.hd, g.pos0 + g.S, kp));
+                TVB_TRY(encode_f32_out(&maps.out[2], g.vcache, g.nkv * g.hd, g.pos0 + g.S, kp));
+            }
+        } else {
+            a.tma_out = pf_out_aligned(g.y, (size_t)g.ldy * 4);
+            if (a.tma_out) TVB_TRY(encode_f32_out(&maps.out[0], g.y, g.m[0].rows, g.S, (size_t)g.ldy * 4));
+        }
+    }
+    if (!small && g.part && g.flags) {
+        // Long reductions whose tiles leave SMs idle but are cut into at most
+        // four pieces (the down projection of a 512- or 1024-token chunk): the
+        // persistent stream-K kernel, 256-row weight tiles (128 when the
+        // matrices have a single 128-row half).  Measured at 1024 tokens of the
+        // 2B shape, down 78.6 -> 69.6 us; q/k/v (40 k-blocks, 120 tiles) was
+        // 45.5 us data-parallel against 54.9 us, o_proj and gate/up even.
+        const int nh_sk = (g.mode == PF_GATEUP || halves > 1) ? 2 : 1;
+        const int tiles_sk = g.mode == PF_GATEUP ? (g.m[0].rows + 127) / 128 : (halves + nh_sk - 1) / nh_sk;
+        const long long units = (long long)tiles_sk * mtiles;
+        const long long total = units * a.nk;
+        const int G = (int)std::min<long long>(num_sms(), total);
+        if (a.nk >= 64 && units < num_sms() && 4 * units >= G && total < (1LL << 31) &&
+            (size_t)G * kPfBM * 128 * nh_sk <= g.part_floats) {
+            static unsigned epoch = 0;   // flags of an earlier launch never match this one's
+            if (++epoch == 0) epoch = 1;
+            a.sk_total = (int)total;
+            a.sk_mtiles = mtiles;
+            a.sk_epoch = epoch;
+            a.sk_flags = g.flags;
+            a.part = g.part;
+            const dim3 grid((unsigned)G), block(kPfThreads);
+            const cudaError_t e = nh_sk == 2
+                ? launch_maybe_pdl(pf_gemm_sk_kernel<2>, grid, block, pf_smem_bytes(2), stream, g.pdl, maps, a)
+                : launch_maybe_pdl(pf_gemm_sk_kernel<1>, grid, block, pf_smem_bytes(1), stream, g.pdl, maps, a);
+            if (e != cudaSuccess) return cuda_error(e, "launch pf_gemm_sk_kernel");
+            return check_launch("pf_gemm_sk_kernel");
+        }
+    }
     // 256-row tiles, or 128-row tiles when those keep more of the SMs busy over
     // the grid's waves (gate/up tiles always pair a gate half with an up half)
     int nh = 2, tiles;

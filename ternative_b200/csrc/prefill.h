@@ -58,6 +58,10 @@ struct PfGemm {
     // epilogue; nullptr or too small: no split
     float* part = nullptr;
     size_t part_floats = 0;
+    // With many output tiles the persistent stream-K kernel runs instead: it
+    // needs one flag word per epilogue warp of every CTA (SMs x 4, zeroed once
+    // at allocation) besides the workspace (SMs x 128 x 256 floats)
+    unsigned* flags = nullptr;
     bool pdl = false;   // programmatic dependent launch after the kernel that writes x
 };
 

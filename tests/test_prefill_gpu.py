@@ -48,7 +48,15 @@ def matmul(lib, torch, x, w, dtype, row_scales=None, tensor_scale=1.0):
     return y.cpu().numpy()
 
 
-@pytest.mark.parametrize("M,K,N", [(200, 2560, 640), (37, 512, 1000), (130, 1024, 1002), (8, 6912, 256)])
+# (1024, 6912, 2560), (512, 6912, 2560), (1024, 4096, 4096) and (900, 8192, 2304)
+# take the persistent stream-K kernel (at least 64 k-blocks, fewer output tiles
+# than SMs, each cut into at most four pieces finished by their owner); the
+# other large ones the data-parallel tile kernel with TMA-stored outputs
+# (1002 columns: a row pitch TMA cannot take, per-thread stores)
+@pytest.mark.parametrize("M,K,N", [(200, 2560, 640), (37, 512, 1000), (130, 1024, 1002), (8, 6912, 256),
+                                   (1024, 6912, 2560), (512, 6912, 2560), (1024, 4096, 4096),
+                                   (900, 8192, 2304), (640, 2560, 3840), (1000, 512, 6912),
+                                   (300, 1024, 16000), (129, 2560, 10240)])
 def test_tensor_core_matmul_f16(cuda, M, K, N):
     import torch
     from ternative_b200 import TVB_F16, load
@@ -59,6 +67,24 @@ def test_tensor_core_matmul_f16(cuda, M, K, N):
     got = matmul(lib, torch, x, w, TVB_F16)
     ref = x.double().cpu().numpy() @ w.double().cpu().numpy().T
     assert rel_err(got, ref) < GEMM_RTOL, rel_err(got, ref)
+    worst = max(rel_err(got[r], ref[r]) for r in range(M))
+    assert worst < GEMM_RTOL, worst
+
+
+def test_tensor_core_matmul_int8_rows_stream_k(cuda):
+    """Per-row INT8 weights through the stream-K kernel (the down shape)."""
+    import torch
+    from ternative_b200 import TVB_I8_ROW, load
+    lib = load()
+    g = torch.Generator().manual_seed(6)
+    M, K, N = 1024, 6912, 2560
+    x = torch.randn(M, K, generator=g).cuda()
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).cuda()
+    s = (torch.rand(N, generator=g) * 1e-3 + 1e-4).cuda()
+    got = matmul(lib, torch, x, q, TVB_I8_ROW, row_scales=s)
+    ref = (x.double().cpu().numpy() @ q.double().cpu().numpy().T) * s.double().cpu().numpy()[None, :]
+    worst = max(rel_err(got[r], ref[r]) for r in range(M))
+    assert worst < GEMM_RTOL, worst
 
 
 def test_tensor_core_matmul_int8_row_and_tensor(cuda):
@@ -109,6 +135,30 @@ def _load(synth, **cfg_changes):
         synth = dataclasses.replace(synth, cfg=dataclasses.replace(synth.cfg, **cfg_changes))
     m = Model.load(synth)
     return m, m.host_weights()
+
+
+def test_prefill_2b_dims_stream_k_matches_oracle(restated):
+    """The projections of the 2B shape (hidden 2560, 20/5 heads, FFN 6912) at
+    640 and 1024 tokens -- every GEMM on the persistent stream-K kernel -- in a
+    2-layer model with a 4096-token vocabulary, against the numpy restatement;
+    then one decode step over the KV rows the prefill wrote."""
+    from ternative_b200.model import SHAPES, Model, SyntheticModel
+    cfg = dataclasses.replace(SHAPES["bitnet-2b"], vocab_size=4096, num_layers=2, max_seq_len=1152,
+                              max_prefill=1024)
+    synth = SyntheticModel.generate(cfg, rank=16, alpha=32.0, seed=5, norm_value=1.0 / 32)
+    m = Model.load(synth)
+    hw = m.host_weights()
+    for S in (640, 1024):
+        prompt = np.random.default_rng(S).integers(0, cfg.vocab_size, S).astype(np.int32)
+        m.backend.clear_kv_d()
+        last, am = m.backend.prefill(prompt)
+        lg, _ = m.backend.decode_step(am, S)
+        # causal: row S - 1 of the S + 1 tokens is the prompt's last row
+        ref = forward_prefill(oracle_shape(cfg), hw, list(prompt) + [am], restated.f16_to_f32)
+        assert rel_err(last, ref[-2]) < RTOL, (S, rel_err(last, ref[-2]))
+        assert am == int(np.argmax(last))
+        assert rel_err(lg, ref[-1]) < RTOL, (S, rel_err(lg, ref[-1]))
+    m.backend.close()
 
 
 @pytest.mark.parametrize("S,max_prefill", [(200, 512), (150, 64), (1, 512), (129, 512)])
