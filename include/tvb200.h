@@ -113,10 +113,13 @@ tvb_status tvb_merge_batch(const tvb_merge_desc* descs, int n, tvb_dtype out, vo
 /* The same merge with the rank-r delta as a tensor-core contraction
  * (tcgen05.mma on F16 hi + lo splits of A and B, F32 accumulation): TVB_F16
  * output within one unit in the last place of tvb_merge_batch's (which is
- * bit-identical to apply_lora), for ranks up to 64.  Other outputs (F32,
- * TVB_I8_ROW, whose codes must be bit-exact) and larger ranks take the
- * tvb_merge_batch path.  Uses a stream-ordered workspace of about
- * 260 B x (N + K) per tensor for the duration of the call. */
+ * bit-identical to apply_lora), for ranks up to 64.  TVB_I8_ROW: these F16
+ * rows quantised per row exactly as the reference quantises F16 weights
+ * (codes within one of tvb_merge_batch's, scales within one F16 unit of the
+ * row maximum), through an F16 workspace of at most 512 MB per group of
+ * tensors.  F32 output and larger ranks take the tvb_merge_batch path.  Uses
+ * a stream-ordered workspace of about 260 B x (N + K) per tensor for the
+ * duration of the call. */
 tvb_status tvb_merge_batch_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, void* stream);
 
 /* tensor.cpp:1006-1050: I2_S codes -> F32 (n % 128 == 0). */

@@ -18,6 +18,7 @@
 // (I2_S unpack, scale, F16 cast, 128-bit stores) reads the other half of a
 // 512-column TMEM accumulator.
 #include "common.cuh"
+#include "prefill.h"
 #include "tcgen05.cuh"
 
 #include <algorithm>
@@ -33,7 +34,11 @@ constexpr int kMtAop = kMtRows * 128;         // bytes per plane of the stripe's
 constexpr int kMtBop = kMtCols * 128;         // bytes per plane of an A^T tile
 // the column exponents rotate over 3 tiles: tile t + 1 is staged while the
 // epilogue of tile t - 1 still reads its own
-constexpr int kMtSmem = 2 * kMtAop + 4 * kMtBop + 3 * kMtCols * 4 + kMtRows * 4 + 64 + 1024;
+// then one output box per warp: 32 rows x 32 F16 columns (64 bytes, 64-byte
+// swizzle) written by the warp and stored by TMA
+constexpr int kMtBox = 32 * 32 * 2;
+constexpr int kMtOutOff = ((2 * kMtAop + 4 * kMtBop + 3 * kMtCols * 4 + kMtRows * 4 + 64 + 1023) / 1024) * 1024;
+constexpr int kMtSmem = kMtOutOff + (kMtThreads / 32) * kMtBox + 1024;
 
 struct MtDesc {
     const uint8_t* i2s;      // whole tensor's codes (row pitch ld / 4 bytes)
@@ -53,6 +58,7 @@ struct MtDesc {
 
 struct MtBatch {
     MtDesc d[kMtMaxDescs];
+    const CUtensorMap* omaps;   // [n] output maps (device memory): dst [N][K] F16, 32 x 32 boxes
     int cta_start[kMtMaxDescs + 1];   // merge CTAs (128-row stripes)
     int row_start[kMtMaxDescs + 1];   // prep warps (rows of B)
     int col_start[kMtMaxDescs + 1];   // prep threads (columns of A)
@@ -195,6 +201,11 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
 
     const int ntiles = (d.K + kMtCols - 1) / kMtCols;
     const int q = warp & 3, cq = warp >> 2;          // TMEM lane quarter, column quarter (64)
+    const uint32_t obox = base + (uint32_t)(kMtOutOff + warp * kMtBox);
+    // the output map was written into device memory by a copy before this
+    // launch: acquire it for the tensor-map proxy before the first store
+    if (lane == 0)
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(b.omaps + di) : "memory");
     const int rloc = 32 * q + lane, n = row0 + rloc;
     const int src_blocks = d.ld >> 7, blk0 = d.k0 >> 7;
     // A^T tile t (256 columns, hi and lo) into buffer `buf`: asynchronous
@@ -266,7 +277,7 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
         if (t > 0) {
             const int u = t - 1, ubuf = u & 1;
             const int colh = u * kMtCols + cq * 64;      // first of this thread's 64 columns
-            const bool rowok = ok && n < d.N && colh < d.K;
+            const bool rowok = ok && colh < d.K;   // (uniform over the warp)
             // their I2_S codes (half of one 128-column block, 32 bytes) were
             // requested during the previous tile; request the next tile's now
             const uint32_t words[8] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w};
@@ -311,18 +322,92 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
                         packed[2 * j4 + (i >> 1)] = h2;
                     }
                 }
-                uint4* out = reinterpret_cast<uint4*>(d.dst + (size_t)n * d.K + colh + c * 32);
+                // the warp's 32 rows x these 32 columns as one box: lane = row,
+                // 64 bytes in 16-byte chunks at their 64-byte-swizzled places
+                // (conflict-free per 8-lane phase); then one TMA store, which
+                // clips rows past N
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
 #pragma unroll
                 for (int v = 0; v < 4; ++v)
-                    out[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                     obox + (uint32_t)(lane * 64 + ((v ^ ((lane >> 1) & 3)) * 16))),
+                                 "r"(packed[4 * v]), "r"(packed[4 * v + 1]), "r"(packed[4 * v + 2]),
+                                 "r"(packed[4 * v + 3])
+                                 : "memory");
+                fence_proxy_async_smem_cta();
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                                     reinterpret_cast<uint64_t>(b.omaps + di)),
+                                 "r"(colh + c * 32), "r"(row0 + 32 * q), "r"(obox)
+                                 : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
             }
             tc_fence_before();
         }
         __syncthreads();
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // every output box written
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
+    }
+}
+
+// Per-row INT8 of merged F16 rows (the reference's quantisation of the F16
+// weights, tensor.cpp absmax per row): one warp per row, a max pass then a
+// code pass, 16 elements per lane step (K % 128 == 0).
+struct MtQuant {
+    const uint16_t* f16[kMtMaxDescs];
+    int8_t* q[kMtMaxDescs];
+    float* scales[kMtMaxDescs];
+    int K[kMtMaxDescs];
+    int row_start[kMtMaxDescs + 1];
+    int n;
+};
+
+__global__ void __launch_bounds__(256) mt_quant_kernel(const __grid_constant__ MtQuant b) {
+    const int grow = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int i = mt_owner(b.row_start, b.n, grow);
+    const int row = grow - b.row_start[i];
+    if (row < 0 || grow >= b.row_start[b.n]) return;
+    const int K = b.K[i];
+    const uint16_t* src = b.f16[i] + (size_t)row * K;
+    uint32_t m = 0;
+    for (int e = lane * 8; e < K; e += 32 * 8) {
+        const uint4 h = *reinterpret_cast<const uint4*>(src + e);
+        const uint32_t w[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) m = max(m, max(w[t] & 0x7FFFu, (w[t] >> 16) & 0x7FFFu));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float mx = __half2float(__ushort_as_half((uint16_t)m));
+    if (mx == 0.0f) mx = 1.0f;
+    const float s = __fdiv_rn(mx, 127.0f);
+    if (lane == 0) b.scales[i][row] = s;
+    int8_t* out = b.q[i] + (size_t)row * K;
+    for (int e = lane * 16; e < K; e += 32 * 16) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(src + e);
+        const uint4 hw = *reinterpret_cast<const uint4*>(src + e + 8);
+        const uint32_t hs[8] = {hv.x, hv.y, hv.z, hv.w, hw.x, hw.y, hw.z, hw.w};
+        uint32_t words[4];
+#pragma unroll
+        for (int qd = 0; qd < 4; ++qd) {
+            uint32_t acc = 0;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const uint32_t h2 = hs[2 * qd + t];
+                const float lo_v = __half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFFu)));
+                const float hi_v = __half2float(__ushort_as_half((uint16_t)(h2 >> 16)));
+                acc |= ((uint32_t)(uint8_t)int8_code(lo_v, s)) << (16 * t);
+                acc |= ((uint32_t)(uint8_t)int8_code(hi_v, s)) << (16 * t + 8);
+            }
+            words[qd] = acc;
+        }
+        *reinterpret_cast<uint4*>(out + e) = make_uint4(words[0], words[1], words[2], words[3]);
     }
 }
 
@@ -347,12 +432,68 @@ static tvb_status mt_prepare() {
 
 tvb_status merge_exact(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st);
 
+tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st);
+
+// Per-row INT8 through the tensor cores: groups of tensors are merged to F16
+// into a workspace (at most kMtI8Workspace bytes a group) and quantised per
+// row from there.  The codes are the reference's quantisation of these F16
+// weights, which are within one F16 unit in the last place of its own.
+constexpr size_t kMtI8Workspace = 512ull << 20;
+
+static tvb_status merge_tc_i8(const tvb_merge_desc* descs, int n, cudaStream_t st) {
+    size_t need = 0, total = 0;
+    for (int i = 0; i < n; ++i) {
+        TVB_REQUIRE(descs[i].row_scales, "merge_tc: descriptor %d: per-row INT8 needs row_scales", i);
+        const size_t b16 = ((size_t)descs[i].N * descs[i].K * 2 + 255) / 256 * 256;
+        need = std::max(need, b16);
+        total += b16;
+    }
+    const size_t ws_bytes = std::max(need, std::min(kMtI8Workspace, total));
+    unsigned char* ws = nullptr;
+    TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), ws_bytes, st));
+    static thread_local tvb_merge_desc f16d[kMtMaxDescs];
+    static thread_local MtQuant qb;
+    tvb_status result = TVB_OK;
+    int i = 0;
+    while (i < n && result == TVB_OK) {
+        size_t used = 0;
+        int cnt = 0, rows = 0;
+        while (i + cnt < n && cnt < kMtMaxDescs) {
+            const tvb_merge_desc& s = descs[i + cnt];
+            const size_t b16 = ((size_t)s.N * s.K * 2 + 255) / 256 * 256;
+            if (cnt > 0 && used + b16 > ws_bytes) break;
+            f16d[cnt] = s;
+            f16d[cnt].dst = ws + used;
+            f16d[cnt].row_scales = nullptr;
+            qb.f16[cnt] = reinterpret_cast<const uint16_t*>(ws + used);
+            qb.q[cnt] = static_cast<int8_t*>(s.dst);
+            qb.scales[cnt] = s.row_scales;
+            qb.K[cnt] = s.K;
+            qb.row_start[cnt] = rows;
+            rows += s.N;
+            used += b16;
+            ++cnt;
+        }
+        qb.row_start[cnt] = rows;
+        qb.n = cnt;
+        result = merge_tc(f16d, cnt, TVB_F16, st);
+        if (result != TVB_OK) break;
+        mt_quant_kernel<<<(rows + 7) / 8, 256, 0, st>>>(qb);
+        result = check_launch("mt_quant_kernel");
+        i += cnt;
+    }
+    const cudaError_t e = cudaFreeAsync(ws, st);
+    if (result == TVB_OK && e != cudaSuccess) result = cuda_error(e, "cudaFreeAsync");
+    return result;
+}
+
 tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStream_t st) {
     if (n <= 0) return TVB_OK;
     TVB_REQUIRE(descs, "merge_tc: descs is NULL");
-    bool exact = out != TVB_F16;
+    bool exact = out != TVB_F16 && out != TVB_I8_ROW;
     for (int i = 0; i < n && !exact; ++i) exact = descs[i].r > kMtRank;
-    if (exact) return merge_exact(descs, n, out, st);   // F32 / INT8 / rank > 64: bit-exact path
+    if (exact) return merge_exact(descs, n, out, st);   // F32 / per-tensor INT8 / rank > 64: bit-exact path
+    if (out == TVB_I8_ROW) return merge_tc_i8(descs, n, st);
     for (int i = 0; i < n; ++i) {
         const tvb_merge_desc& s = descs[i];
         const int ld = s.ld ? s.ld : s.K;
@@ -373,10 +514,32 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
             rows += (size_t)descs[base + i].N;
             cols += (size_t)descs[base + i].K;
         }
-        const size_t bytes = 2 * (rows + cols) * kMtRank * 2 + (rows + cols) * 4 + 256;
+        // (output tensor maps first: 128-byte aligned)
+        const size_t map_bytes = (size_t)cnt * sizeof(CUtensorMap);
+        const size_t bytes = map_bytes + 2 * (rows + cols) * kMtRank * 2 + (rows + cols) * 4 + 256;
         unsigned char* ws = nullptr;
         TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st));
-        uint16_t* bh = reinterpret_cast<uint16_t*>(ws);
+        static thread_local CUtensorMap omaps[kMtMaxDescs];
+        for (int i = 0; i < cnt; ++i) {
+            const tvb_merge_desc& sd = descs[base + i];
+            const uint64_t dims[2] = {(uint64_t)sd.K, (uint64_t)sd.N};
+            const uint64_t strides[1] = {(uint64_t)sd.K * 2};
+            const uint32_t box[2] = {32u, 32u};
+            tvb_status es = encode_f16_tiled(&omaps[i], sd.dst, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+            if (es != TVB_OK) {
+                cudaFreeAsync(ws, st);
+                return es;
+            }
+        }
+        {
+            const cudaError_t ce = cudaMemcpyAsync(ws, omaps, map_bytes, cudaMemcpyHostToDevice, st);
+            if (ce != cudaSuccess) {
+                cudaFreeAsync(ws, st);
+                return cuda_error(ce, "cudaMemcpyAsync(merge output maps)");
+            }
+        }
+        b.omaps = reinterpret_cast<const CUtensorMap*>(ws);
+        uint16_t* bh = reinterpret_cast<uint16_t*>(ws + map_bytes);
         uint16_t* bl = bh + rows * kMtRank;
         uint16_t* ah = bl + rows * kMtRank;
         uint16_t* al = ah + cols * kMtRank;

@@ -1103,7 +1103,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(tvb_status* st) {
 }
 
 tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint64_t* dims, const uint64_t* strides,
-                            const uint32_t* box) {
+                            const uint32_t* box, CUtensorMapSwizzle swizzle) {
     tvb_status st;
     auto fn = encode_fn(&st);
     if (!fn) return st;
@@ -1117,7 +1117,7 @@ tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint6
         if (i + 1 < rank) sb[i] = strides[i];
     }
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(p), d, sb, b, e,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(TVB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return TVB_OK;

@@ -99,9 +99,10 @@ tvb_status pf_attention_tc(const float* q, const float* kcache, const float* vca
                            int nkv, int hd, float scale, float* out, void* planes, int max_rows, int max_keys,
                            unsigned* status, cudaStream_t st);
 
-// Tiled TMA descriptor of an F16 tensor (128-byte swizzle, zero fill outside).
+// Tiled TMA descriptor of an F16 tensor (128-byte swizzle unless given, zero
+// fill outside).
 tvb_status encode_f16_tiled(CUtensorMap* m, const void* p, int rank, const uint64_t* dims, const uint64_t* strides,
-                            const uint32_t* box);
+                            const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // INT8 -> F16 (exact: |q| <= 127).
 tvb_status pf_i8_to_f16(const int8_t* q, size_t n, uint16_t* out, cudaStream_t st, bool pdl = false);

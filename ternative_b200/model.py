@@ -151,8 +151,9 @@ class Model:
         """Merge every projection on the device (F16, or INT8 for the layers in
         ``int8_layers``) and register the result with the fused step.  F16 layers
         take the tensor-core merge (within one F16 unit in the last place of the
-        reference's apply_lora, usually identical) unless ``exact_merge``, which
-        takes the bit-exact CUDA-core merge; INT8 codes are always exact."""
+        reference's apply_lora, usually identical; INT8 layers quantise those
+        F16 rows per row) unless ``exact_merge``, which takes the bit-exact
+        CUDA-core merge for both."""
         import torch
         cfg = synth.cfg
         be = backend or CUDABackend()
@@ -177,8 +178,8 @@ class Model:
             merge = be.merge_batch if exact_merge else be.merge_batch_tc
             merge(synth.merge_descs(f16_out, layers=f16_layers), TVB_F16)
         if int8_layers and per_row:
-            be.merge_batch(synth.merge_descs(i8_out, i8_scales, layers=sorted(int8_layers)),
-                           TVB_I8_ROW)
+            merge = be.merge_batch if exact_merge else be.merge_batch_tc
+            merge(synth.merge_descs(i8_out, i8_scales, layers=sorted(int8_layers)), TVB_I8_ROW)
         m.row_scales = [{} for _ in range(cfg.num_layers)]
         m.tensor_scales = [{} for _ in range(cfg.num_layers)]
         for li in range(cfg.num_layers):

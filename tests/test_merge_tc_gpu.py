@@ -2,8 +2,10 @@
 the tensor cores (tcgen05.mma over F16 hi/lo splits of A and B), against the
 oracle's bit-exact restatement of apply_lora (src/model.cpp:180-258): F16
 outputs within one unit in the last place (the tolerance for merged F16
-weights) and nearly always identical; outputs the tensor-core path does not
-take (F32, per-row INT8, ranks above 64) bit-identical through the exact path."""
+weights) and nearly always identical; per-row INT8 as the reference's row
+quantisation of those F16 rows (codes within one of the exact merge's); outputs
+the tensor-core path does not take (F32, ranks above 64) bit-identical through
+the exact path."""
 import numpy as np
 import pytest
 
@@ -71,9 +73,22 @@ def test_tc_merge_exact_outputs_fall_back(backend, restated):
     i2s, s, A, B = make_case(restated, K, N, r, 8)
     got = run_tc(backend, torch, [(i2s, s, K, N, A, B, r, 64.0, 0, 0)])[0][0].view(np.uint16)
     assert np.array_equal(got, restated.merge(i2s, s, K, N, A, B, 64.0)[1])
-    K, N, r = 512, 24, 16    # INT8 rows -> exact path
-    i2s, s, A, B = make_case(restated, K, N, r, 9)
-    q, sc = run_tc(backend, torch, [(i2s, s, K, N, A, B, r, 32.0, 0, 0)], out=TVB_I8_ROW)[0]
-    qr, sr = restated.quantize_int8_rows(restated.merge(i2s, s, K, N, A, B, 32.0)[1])
+
+
+@pytest.mark.parametrize("K,N,r", [(512, 24, 16), (2560, 640, 64), (6912, 130, 32)])
+def test_tc_merge_int8_rows(backend, restated, K, N, r):
+    """Per-row INT8 through the tensor cores: exactly the reference's row
+    quantisation of the tensor-core F16 rows; against the bit-exact merge's
+    codes, within one code (and identical scales wherever the row maxima agree)."""
+    import torch
+    i2s, s, A, B = make_case(restated, K, N, r, 9 + K)
+    case = [(i2s, s, K, N, A, B, r, 2.0 * r, 0, 0)]
+    q, sc = run_tc(backend, torch, case, out=TVB_I8_ROW)[0]
+    f16 = run_tc(backend, torch, case)[0][0].view(np.uint16)
+    qr, sr = restated.quantize_int8_rows(f16)
     assert np.array_equal(q, qr)
     assert np.array_equal(sc.view(np.uint32), sr.view(np.uint32))
+    qe, se = restated.quantize_int8_rows(restated.merge(i2s, s, K, N, A, B, 2.0 * r)[1])
+    assert np.abs(q.astype(np.int32) - qe.astype(np.int32)).max() <= 1
+    assert np.abs(sc / se - 1.0).max() <= 2.0 ** -10
+    assert (q == qe).mean() > 0.999
