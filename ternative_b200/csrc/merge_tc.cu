@@ -47,7 +47,7 @@ struct MtDesc {
     const int* eb;           // [N]
     const uint16_t* ath;     // [K][64] F16 hi of A^T * 2^-ea[k]
     const uint16_t* atl;
-    const int* ea;           // [K]
+    const float* fa;         // [K] 2^ea: A^T column k was stored scaled by 2^-ea[k]
     uint16_t* dst;           // [N][K] F16
     const float* A;          // LoRA A [r][ld] (whole tensor's columns)
     const float* B;          // LoRA B [N][r]
@@ -150,7 +150,7 @@ __global__ void mt_prep_a(const __grid_constant__ MtBatch b) {
         th[c] = *reinterpret_cast<const uint4*>(h);
         tl[c] = *reinterpret_cast<const uint4*>(l);
     }
-    const_cast<int*>(d.ea)[k] = e;
+    const_cast<float*>(d.fa)[k] = mt_pow2(e);
 }
 
 __device__ __forceinline__ void mt_fail(unsigned* status) {
@@ -224,9 +224,14 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
                          "l"(d.atl + off), "r"(nb)
                          : "memory");
         }
-        for (int r = tid; r < kMtCols; r += kMtThreads) {
-            const int col = t * kMtCols + r;
-            fa_s[(t % 3) * kMtCols + r] = col < d.K ? mt_pow2(d.ea[col]) : 0.f;
+        // the columns' 2^ea ride in the same group (16-byte copies, zero past K)
+        for (int r4 = tid; r4 < kMtCols / 4; r4 += kMtThreads) {
+            const int col = t * kMtCols + 4 * r4;
+            const bool in = col < d.K;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                             smem_u32(fa_s + (t % 3) * kMtCols + 4 * r4)),
+                         "l"(d.fa + (in ? col : 0)), "r"(in ? 16u : 0u)
+                         : "memory");
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -544,7 +549,8 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
         uint16_t* ah = bl + rows * kMtRank;
         uint16_t* al = ah + cols * kMtRank;
         int* eb = reinterpret_cast<int*>(al + cols * kMtRank);
-        int* ea = eb + rows;
+        // (16-byte aligned: the kernel copies it in 16-byte pieces)
+        float* fa = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(eb + rows) + 15) & ~(uintptr_t)15);
         size_t ro = 0, co = 0;
         int ctas = 0, rwarps = 0, cthreads = 0;
         for (int i = 0; i < cnt; ++i) {
@@ -556,7 +562,7 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
             d.eb = eb + ro;
             d.ath = ah + co * kMtRank;
             d.atl = al + co * kMtRank;
-            d.ea = ea + co;
+            d.fa = fa + co;
             d.dst = static_cast<uint16_t*>(s.dst);
             d.A = s.r ? s.A : nullptr;
             d.B = s.r ? s.B : nullptr;
