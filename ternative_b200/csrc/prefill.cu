@@ -1336,7 +1336,10 @@ tvb_status pf_gemm(const PfGemm& g, cudaStream_t stream) {
 // ---------------------------------------------------------------------------
 // one CTA per row: 256 threads, or 1024 when the rows alone leave most SMs idle
 
-template <int NT>
+// The row is read once into registers (at most MAXV float4 per thread), then
+// reduced twice (sum of squares, largest magnitude) and written; the sums run
+// in the same order as a strided pass over global memory would.
+template <int NT, int MAXV>
 __global__ void __launch_bounds__(NT)
 pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, int K, float eps,
                      __half* __restrict__ xh, __half* __restrict__ xl, int* __restrict__ row_exp,
@@ -1349,13 +1352,16 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     const int K4 = K >> 2;
     __shared__ float red[NT / 32];
     __shared__ float s_inv, s_max;
+    float4 v[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int k = tid + i * NT;
+        v[i] = k < K4 ? x4[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
     float inv = 1.0f;
     if (w) {
-        float ss = 0.f;
-        for (int k = tid; k < K4; k += NT) {
-            const float4 v = x4[k];
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
@@ -1378,13 +1384,15 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     }
     // the normalised row x * (inv_rms * w) (the vectorised path of tensor_rms_norm)
     float mx = 0.f;
-    for (int k = tid; k < K4; k += NT) {
-        float4 v = x4[k];
-        if (w) {
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int k = tid + i * NT;
+        if (k < K4 && w) {
             const float4 g = w4[k];
-            v = make_float4(v.x * (inv * g.x), v.y * (inv * g.y), v.z * (inv * g.z), v.w * (inv * g.w));
+            v[i] = make_float4(v[i].x * (inv * g.x), v[i].y * (inv * g.y), v[i].z * (inv * g.z),
+                               v[i].w * (inv * g.w));
         }
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
     }
     mx = warp_max(mx);
     __syncthreads();
@@ -1401,25 +1409,23 @@ pf_norm_split_kernel(const float* __restrict__ x, const float* __restrict__ w, i
     const int e = (s_max > 0.f && isfinite(s_max)) ? max(ilogbf(s_max) - 14, -100) : 0;
     if (tid == 0) row_exp[row] = e;
     const float sc = ldexpf(1.0f, -e);
-    __half2* h2 = reinterpret_cast<__half2*>(xh + (size_t)row * K);
-    __half2* l2 = reinterpret_cast<__half2*>(xl + (size_t)row * K);
-    for (int k = tid; k < K4; k += NT) {
-        float4 v = x4[k];
-        if (w) {
-            const float4 g = w4[k];
-            v = make_float4(v.x * (inv * g.x), v.y * (inv * g.y), v.z * (inv * g.z), v.w * (inv * g.w));
-        }
-        const float f[4] = {v.x * sc, v.y * sc, v.z * sc, v.w * sc};
+    uint2* h2 = reinterpret_cast<uint2*>(xh + (size_t)row * K);
+    uint2* l2 = reinterpret_cast<uint2*>(xl + (size_t)row * K);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int k = tid + i * NT;
+        if (k >= K4) continue;
+        const float f[4] = {v[i].x * sc, v[i].y * sc, v[i].z * sc, v[i].w * sc};
         __half hi[4], lo[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            hi[i] = __float2half_rn(f[i]);
-            lo[i] = __float2half_rn(f[i] - __half2float(hi[i]));
+        for (int j = 0; j < 4; ++j) {
+            hi[j] = __float2half_rn(f[j]);
+            lo[j] = __float2half_rn(f[j] - __half2float(hi[j]));
         }
-        h2[2 * k] = __halves2half2(hi[0], hi[1]);
-        h2[2 * k + 1] = __halves2half2(hi[2], hi[3]);
-        l2[2 * k] = __halves2half2(lo[0], lo[1]);
-        l2[2 * k + 1] = __halves2half2(lo[2], lo[3]);
+        const __half2 h01 = __halves2half2(hi[0], hi[1]), h23 = __halves2half2(hi[2], hi[3]);
+        const __half2 l01 = __halves2half2(lo[0], lo[1]), l23 = __halves2half2(lo[2], lo[3]);
+        h2[k] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+        l2[k] = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
     }
 }
 
@@ -1449,12 +1455,20 @@ tvb_status pf_norm_split(const float* x, const float* w, int S, int K, float eps
     TVB_REQUIRE(x && xh && xl && row_exp && S > 0 && K > 0 && K % 4 == 0, "norm_split: bad arguments");
     __half* h = reinterpret_cast<__half*>(xh);
     __half* l = reinterpret_cast<__half*>(xl);
+    // one CTA per row; 1024 threads when the rows alone leave most SMs idle.
+    // The row lives in registers: up to 16 float4 a thread with 256 threads
+    // (K <= 16384), 8 with 1024 (K <= 32768)
+    TVB_REQUIRE(K <= (S < num_sms() ? 8 * 4 * 1024 : 16 * 4 * 256), "norm_split: K=%d too long for a register row",
+                K);
     if (S < num_sms())
-        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<1024>, dim3(S), dim3(1024), 0, st, pdl, x, w, K, eps, h, l,
-                                  row_exp, ss_out));
+        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<1024, 8>, dim3(S), dim3(1024), 0, st, pdl, x, w, K, eps,
+                                  h, l, row_exp, ss_out));
+    else if (K <= 8 * 4 * 256)
+        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<256, 8>, dim3(S), dim3(256), 0, st, pdl, x, w, K, eps, h,
+                                  l, row_exp, ss_out));
     else
-        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<256>, dim3(S), dim3(256), 0, st, pdl, x, w, K, eps, h, l,
-                                  row_exp, ss_out));
+        TVB_CUDA(launch_maybe_pdl(pf_norm_split_kernel<256, 16>, dim3(S), dim3(256), 0, st, pdl, x, w, K, eps, h,
+                                  l, row_exp, ss_out));
     return check_launch("pf_norm_split_kernel");
 }
 
