@@ -370,8 +370,11 @@ tvb_status tvb_score_logprobs(tvb_context* ctx, const int* tokens_host, int T, i
  * temperature, repetition penalty over row b's seen tokens (seen + b*max_seen,
  * n_seen[b] of them), softmax, top-k, top-p, renormalisation and the draw
  * against u[b] in [0, 1) (the reference draws it from its own mt19937).
- * out[b] receives the token.  All pointers are device memory; top_p in (0, 1)
- * needs 1 <= top_k <= 1024.  Allocates a per-call workspace on `stream`. */
+ * out[b] receives the token.  All pointers are device memory.  top_p in (0, 1)
+ * with top_k 0 (the whole vocabulary) or above 1024 takes a one-CTA-per-row
+ * kernel that walks the sorted probabilities 1024 at a time (slower for flat
+ * distributions, whose nucleus holds many tokens).  Allocates a per-call
+ * workspace on `stream`. */
 typedef struct {
     float temperature;
     float top_p;

@@ -17,8 +17,10 @@
 // its own mt19937).  Sums the reference takes in index order are taken as
 // trees here: the F64 sums differ from it only far below F32 resolution, and
 // the step-7 running sum runs sequentially in index order over the entries
-// that can be nonzero, as the reference's.  Top-p works on at most 1024
-// candidates, so it requires 1 <= top_k <= 1024.
+// that can be nonzero, as the reference's.  The cluster kernel's top-p works
+// on at most 1024 candidates (1 <= top_k <= 1024); top-p with top_k 0 (the
+// whole vocabulary) or above 1024 runs on sample_kernel, which walks the
+// sorted keys 1024 at a time.
 #include <cuda_runtime.h>
 
 #include <cfloat>
@@ -118,6 +120,40 @@ __device__ __forceinline__ void radix_pick(const unsigned* hist, int need, int* 
     }
 }
 
+// The need-th largest of the keys key(i), i in [0, V), by an 8-bit radix
+// select (1 <= need <= the number of nonzero keys); block-wide, all threads
+// return it.
+template <class Key>
+__device__ __forceinline__ unsigned long long block_radix_kth(Key&& key, int V, int need, unsigned* hist,
+                                                              int* s_keep, int* s_count) {
+    const int tid = threadIdx.x;
+    unsigned long long prefix = 0ull, mask = 0ull;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0u;
+        __syncthreads();
+        // warp-aggregated counts: the probabilities crowd into few bins
+        for (int base = 0; base < V; base += kSampThreads) {
+            const int i = base + tid;
+            const unsigned long long k = i < V ? key(i) : 0ull;
+            const bool hit = i < V && (k & mask) == prefix;
+            const unsigned act = __ballot_sync(0xffffffffu, hit);
+            if (hit) {
+                const unsigned bin = (unsigned)(k >> shift) & 255u;
+                const unsigned peers = __match_any_sync(act, bin);
+                if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+            }
+        }
+        __syncthreads();
+        if (tid < 32) radix_pick(hist, need, s_keep, s_count);
+        __syncthreads();
+        prefix |= (unsigned long long)*s_keep << shift;
+        mask |= 255ull << shift;
+        need = *s_count;
+        __syncthreads();
+    }
+    return prefix;
+}
+
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_constant__ SampArgs a) {
     const int b = blockIdx.x, tid = threadIdx.x, V = a.vocab;
     const float* lg = a.logits + (size_t)b * a.ld;
@@ -164,84 +200,89 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const __grid_const
     __syncthreads();
 
     const bool topk = a.top_k > 0 && a.top_k < V;
-    const bool topp = a.top_p > 0.0f && a.top_p < 1.0f;   // (the host requires top_k <= 1024 with it)
+    const bool topp = a.top_p > 0.0f && a.top_p < 1.0f;
     if (topk) {
         // 4. the k-th largest (p, index) key by an 8-bit radix select, then
         //    everything below it set to 0
-        unsigned long long prefix = 0ull, mask = 0ull;
-        int need = a.top_k;   // rank of the wanted key among those matching the prefix
-        for (int shift = 56; shift >= 0; shift -= 8) {
-            for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0u;
-            __syncthreads();
-            // warp-aggregated counts: the probabilities crowd into few bins
-            for (int base = 0; base < V; base += kSampThreads) {
-                const int i = base + tid;
-                const unsigned long long k = i < V ? samp_key(p[i], i) : 0ull;
-                const bool hit = i < V && (k & mask) == prefix;
-                const unsigned act = __ballot_sync(0xffffffffu, hit);
-                if (hit) {
-                    const unsigned bin = (unsigned)(k >> shift) & 255u;
-                    const unsigned peers = __match_any_sync(act, bin);
-                    if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
-                }
-            }
-            __syncthreads();
-            if (tid < 32) radix_pick(hist, need, &s_keep, &s_count);
-            __syncthreads();
-            prefix |= (unsigned long long)s_keep << shift;
-            mask |= 255ull << shift;
-            need = s_count;
-            __syncthreads();
-        }
-        const unsigned long long kth = prefix;   // exactly top_k keys are >= kth
+        const unsigned long long kth =
+            block_radix_kth([&](int i) { return samp_key(p[i], i); }, V, a.top_k, hist, &s_keep, &s_count);
         for (int i = tid; i < V; i += kSampThreads)
-            if (samp_key(p[i], i) < kth) p[i] = 0.0f;
+            if (samp_key(p[i], i) < kth) p[i] = 0.0f;   // exactly top_k keys are >= kth
         __syncthreads();
     }
     if (topp) {
-        // 5. the kept p > 0 (at most top_k <= 1024 of them) sorted descending
-        if (tid == 0) s_count = 0;
-        __syncthreads();
-        for (int i = tid; i < V; i += kSampThreads)
-            if (p[i] > 0.0f) {
-                const int at = atomicAdd(&s_count, 1);
-                if (at < kSampCand) cand[at] = samp_key(p[i], i);
+        // 5. the kept p > 0 sorted by (p, index) descending, their F32 running
+        //    sum until it reaches top_p.  Taken kSampCand keys at a time: the
+        //    round's keys are the largest below `hi` (a radix select finds the
+        //    smallest of them when more remain), bitonic-sorted, and thread 0
+        //    continues the running sum over them.
+        unsigned long long hi = ~0ull;   // keys >= hi are in earlier rounds
+        unsigned long long cut = 0ull;   // the nucleus: keys >= cut
+        float cum = 0.0f;                // (thread 0)
+        for (;;) {
+            auto key_below = [&](int i) {
+                const unsigned long long k = samp_key(p[i], i);
+                return (p[i] > 0.0f && k < hi) ? k : 0ull;
+            };
+            int left = 0;
+            for (int i = tid; i < V; i += kSampThreads) left += key_below(i) != 0ull;
+            left = block_reduce(left, [](int x, int y) { return x + y; }, reinterpret_cast<int*>(red_f));
+            if (left == 0) break;   // every kept key is in (the sum never reached top_p)
+            const unsigned long long lo =
+                left > kSampCand ? block_radix_kth(key_below, V, kSampCand, hist, &s_keep, &s_count) : 1ull;
+            if (tid == 0) s_count = 0;
+            __syncthreads();
+            for (int i = tid; i < V; i += kSampThreads) {
+                const unsigned long long k = key_below(i);
+                if (k != 0ull && k >= lo) {
+                    const int at = atomicAdd(&s_count, 1);
+                    if (at < kSampCand) cand[at] = k;
+                }
             }
-        __syncthreads();
-        const int n = min(s_count, kSampCand);
-        for (int i = n + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
-        __syncthreads();
-        // bitonic sort, descending
-        for (int size = 2; size <= kSampCand; size <<= 1) {
-            for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                const int i = tid, j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const unsigned long long x = cand[i], y = cand[j];
-                    if (desc ? (x < y) : (x > y)) {
-                        cand[i] = y;
-                        cand[j] = x;
+            __syncthreads();
+            const int n = min(s_count, kSampCand);
+            for (int i = n + tid; i < kSampCand; i += kSampThreads) cand[i] = 0ull;
+            __syncthreads();
+            // bitonic sort, descending
+            for (int size = 2; size <= kSampCand; size <<= 1) {
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    const int i = tid, j = i ^ stride;
+                    if (j > i) {
+                        const bool desc = (i & size) == 0;
+                        const unsigned long long x = cand[i], y = cand[j];
+                        if (desc ? (x < y) : (x > y)) {
+                            cand[i] = y;
+                            cand[j] = x;
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            if (tid == 0) {
+                int m = 0;
+                bool reached = false;
+                while (m < n) {
+                    cum += __uint_as_float((unsigned)(cand[m] >> 32));
+                    ++m;
+                    if (cum >= a.top_p) {
+                        reached = true;
+                        break;
                     }
                 }
-                __syncthreads();
+                s_keep = reached ? 1 : 0;
+                red_k[0] = cand[m - 1];   // the smallest key taken so far
             }
+            __syncthreads();
+            cut = red_k[0];
+            const bool reached = s_keep != 0;
+            __syncthreads();
+            if (reached) break;
+            hi = cut;
         }
-        if (tid == 0) {
-            float cum = 0.0f;
-            int m = 0;
-            while (m < n) {
-                cum += __uint_as_float((unsigned)(cand[m] >> 32));
-                ++m;
-                if (cum >= a.top_p) break;
-            }
-            s_keep = m;   // the nucleus is cand[0, m)
-        }
-        __syncthreads();
-        const int m = s_keep;
-        // zero every p outside the nucleus (the nucleus keys are the m largest)
-        const unsigned long long lo = m > 0 ? cand[m - 1] : ~0ull;
-        for (int i = tid; i < V; i += kSampThreads)
-            if (p[i] > 0.0f && samp_key(p[i], i) < lo) p[i] = 0.0f;
+        // zero every p outside the nucleus (its keys are the largest ones)
+        if (cut != 0ull)
+            for (int i = tid; i < V; i += kSampThreads)
+                if (p[i] > 0.0f && samp_key(p[i], i) < cut) p[i] = 0.0f;
         __syncthreads();
     }
     // 6. renormalise
@@ -703,8 +744,10 @@ extern "C" tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, 
     TVB_REQUIRE(!(cfg->repetition_penalty > 1.0f) || (seen && n_seen && max_seen >= 0),
                 "sample: repetition penalty needs the seen tokens");
     const bool topp = cfg->top_p > 0.0f && cfg->top_p < 1.0f;
-    TVB_REQUIRE(!topp || (cfg->top_k >= 1 && cfg->top_k <= kSampCand),
-                "sample: top_p %g needs top_k in [1, %d] (got %d)", cfg->top_p, kSampCand, cfg->top_k);
+    // top-p over more than kSampCand candidates (top_k 0 = the whole vocabulary,
+    // or top_k above kSampCand): the one-CTA kernel, whose nucleus search takes
+    // kSampCand keys a round
+    const bool wide_nucleus = topp && !(cfg->top_k >= 1 && cfg->top_k <= kSampCand);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     SampArgs a;
     a.logits = logits;
@@ -722,7 +765,7 @@ extern "C" tvb_status tvb_sample(const float* logits, int B, int vocab, int ld, 
     a.work = nullptr;
     a.bits = nullptr;
     const int S = ((vocab + kClu - 1) / kClu + 31) / 32 * 32;   // entries per CTA of a row's cluster
-    if (S <= kCluMaxSlice) {
+    if (S <= kCluMaxSlice && !wide_nucleus) {
         const size_t smem = (size_t)S * 8 + ((size_t)S / 32 + 1) * 4;
         static size_t smem_set = 0;
         if (smem > smem_set) {

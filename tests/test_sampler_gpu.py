@@ -5,7 +5,8 @@ boundary between the restated token and its neighbour in the cumulative
 distribution, which may draw that neighbour (the device's expf and tree sums
 may move a boundary by a few F32 ulps).  Rows up to 196,608 entries run on one
 8-CTA cluster per row (100, 1000 and 128,256 here, the first with CTAs whose
-slice is empty); the 200,000-entry rows take the single-CTA kernel."""
+slice is empty); the 200,000-entry rows take the single-CTA kernel, and so does
+top-p with top_k 0 or above 1024 (the nucleus searched 1024 keys at a time)."""
 import ctypes as C
 
 import numpy as np
@@ -68,10 +69,31 @@ def test_device_sampler_matches_restatement(V, cfg):
         assert neighbours and near, (b, g, tok, float(u[b]), float(cdf[lo]))
 
 
-def test_device_sampler_rejects_top_p_without_top_k():
+@pytest.mark.parametrize("V", [1000, 128256])
+@pytest.mark.parametrize("cfg,scale", [((0.8, 0.9, 0, 1.1), 2.5), ((1.0, 0.95, 5000, 1.0), 2.5),
+                                       ((1.0, 0.9, 0, 1.0), 0.05)])
+def test_device_sampler_top_p_over_the_whole_vocabulary(V, cfg, scale):
+    """top_p with top_k 0 (the nucleus over every token) or above 1024: the
+    one-CTA kernel takes the sorted probabilities 1024 at a time; scale 0.05
+    makes the distribution nearly flat, so the nucleus holds ~90% of the
+    vocabulary (over a hundred rounds at 128,256 entries)."""
     import torch
     from ternative_b200 import load
     lib = load()
-    logits = np.zeros((1, 100), np.float32)
-    st, _ = run(lib, torch, logits, (0.8, 0.9, 0, 1.0), [[]], [0.5])
-    assert st != 0 and b"top_k" in lib.tvb_last_error()
+    rng = np.random.default_rng(V + int(cfg[2]) + int(100 * scale))
+    B = 4
+    logits = (rng.standard_normal((B, V)) * scale).astype(np.float32)
+    seen = [rng.integers(0, V, n).tolist() for n in (0, 5, 40, 3)]
+    u = rng.random(B).astype(np.float32)
+    st, got = run(lib, torch, logits, cfg, seen, u)
+    assert st == 0, lib.tvb_last_error()
+    T, tp, tk, pen = cfg
+    for b in range(B):
+        tok, cdf = sample_token(logits[b], T, tp, tk, pen, seen[b], u=float(u[b]), return_cdf=True)
+        if got[b] == tok:
+            continue
+        g = int(got[b])
+        lo, hi = min(g, tok), max(g, tok)
+        neighbours = float(cdf[hi - 1]) == float(cdf[lo])
+        near = abs(float(u[b]) - float(cdf[lo])) <= 1e-5
+        assert neighbours and near, (b, g, tok, float(u[b]), float(cdf[lo]))
