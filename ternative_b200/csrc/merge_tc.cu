@@ -301,31 +301,38 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
                 if (!rowok) continue;
                 // column 32 * slot + j of the block: byte j, bits shift + 1 .. shift
                 const int shift = 6 - 2 * (((colh & 127) >> 5) + c);
-                uint32_t packed[16];
+                // merged = map(code) * scale + acc * 2^ea * (alpha / r) * 2^eb; the
+                // column and row factors are powers of two apart from alpha / r,
+                // so 2^ea * g is exact and one fused multiply-add does the rest
+                // (one rounding where the exact merge has two: the F16 result
+                // stays within one unit in the last place)
+                float mv[32];
+                float mx = 0.f;
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 fa = fa4[c * 8 + j4];
-                    const float fav[4] = {fa.x, fa.y, fa.z, fa.w};
-                    float mv[4];
+                    const float fg[4] = {fa.x * g, fa.y * g, fa.z * g, fa.w * g};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int j = 4 * j4 + i;
                         const uint32_t code = (words[j >> 2] >> (8 * (j & 3) + shift)) & 3u;
                         // map2bit {-1, 0, +1, 0} times the scale (tensor.cpp:1020)
                         const float bv = (code & 1u) ? 0.0f : (code ? sp : sn);
-                        mv[i] = __fadd_rn(bv, __fmul_rn(__fmul_rn(__uint_as_float(acc[j]), fav[i]), g));
+                        mv[j] = __fmaf_rn(__uint_as_float(acc[j]), fg[i], bv);
+                        mx = fmaxf(mx, fabsf(mv[j]));
                     }
+                }
+                uint32_t packed[16];
+                if (mx < 65536.0f) {
+                    // round toward zero = the reference's truncation in this range
 #pragma unroll
-                    for (int i = 0; i < 4; i += 2) {
-                        uint32_t h2;
-                        if (fabsf(mv[i]) < 65536.0f && fabsf(mv[i + 1]) < 65536.0f) {
-                            // round toward zero = the reference's truncation in this range
-                            asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(mv[i + 1]), "f"(mv[i]));
-                        } else {
-                            h2 = (uint32_t)f32_to_f16_trunc(mv[i]) | ((uint32_t)f32_to_f16_trunc(mv[i + 1]) << 16);
-                        }
-                        packed[2 * j4 + (i >> 1)] = h2;
-                    }
+                    for (int t = 0; t < 16; ++t)
+                        asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(packed[t]) : "f"(mv[2 * t + 1]), "f"(mv[2 * t]));
+                } else {
+#pragma unroll
+                    for (int t = 0; t < 16; ++t)
+                        packed[t] = (uint32_t)f32_to_f16_trunc(mv[2 * t]) |
+                                    ((uint32_t)f32_to_f16_trunc(mv[2 * t + 1]) << 16);
                 }
                 // the warp's 32 rows x these 32 columns as one box: lane = row,
                 // 64 bytes in 16-byte chunks at their 64-byte-swizzled places
