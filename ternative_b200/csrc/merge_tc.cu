@@ -14,9 +14,10 @@
 //
 // One CTA per 128-row stripe of a tensor: the stripe's B rows (hi, lo) stay in
 // shared memory, the A^T column tiles (256 columns, hi, lo) stream through a
-// double buffer, the MMAs of tile t run while the epilogue of tile t - 1
-// (I2_S unpack, scale, F16 cast, 128-bit stores) reads the other half of a
-// 512-column TMEM accumulator.
+// double buffer with the tile's I2_S codes and column exponents, the MMAs of
+// tile t run while the epilogue of tile t - 1 (I2_S unpack, scale, F16 cast)
+// reads the other half of a 512-column TMEM accumulator and hands 32 x 32
+// boxes to TMA stores.
 #include "common.cuh"
 #include "prefill.h"
 #include "tcgen05.cuh"
@@ -38,7 +39,11 @@ constexpr int kMtBop = kMtCols * 128;         // bytes per plane of an A^T tile
 // swizzle) written by the warp and stored by TMA
 constexpr int kMtBox = 32 * 32 * 2;
 constexpr int kMtOutOff = ((2 * kMtAop + 4 * kMtBop + 3 * kMtCols * 4 + kMtRows * 4 + 64 + 1023) / 1024) * 1024;
-constexpr int kMtSmem = kMtOutOff + (kMtThreads / 32) * kMtBox + 1024;
+// then the I2_S codes of the stripe's rows for 3 tiles (rotating like the
+// exponents): 128 rows x 2 blocks x 32 bytes each
+constexpr int kMtCodes = kMtRows * 64;
+constexpr int kMtCodeOff = kMtOutOff + (kMtThreads / 32) * kMtBox;
+constexpr int kMtSmem = kMtCodeOff + 3 * kMtCodes + 1024;
 
 struct MtDesc {
     const uint8_t* i2s;      // whole tensor's codes (row pitch ld / 4 bytes)
@@ -206,10 +211,11 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
     // launch: acquire it for the tensor-map proxy before the first store
     if (lane == 0)
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(b.omaps + di) : "memory");
-    const int rloc = 32 * q + lane, n = row0 + rloc;
+    const int rloc = 32 * q + lane;
     const int src_blocks = d.ld >> 7, blk0 = d.k0 >> 7;
-    // A^T tile t (256 columns, hi and lo) into buffer `buf`: asynchronous
-    // 16-byte copies into the swizzled layout, zero-filled past K
+    // A^T tile t (256 columns, hi and lo) into buffer `buf`, and the tile's
+    // codes and column exponents into rotating slot t % 3: asynchronous 16-byte
+    // copies (the A^T planes into the swizzled layout), zero-filled past N / K
     auto load_tile = [&](int t, int buf) {
         const uint32_t dst = b_op + (uint32_t)(2 * buf) * kMtBop;
         for (int idx = tid; idx < kMtCols * 8; idx += kMtThreads) {
@@ -224,6 +230,17 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
                          "l"(d.atl + off), "r"(nb)
                          : "memory");
         }
+        // the stripe's I2_S codes of these columns (two 32-byte blocks a row),
+        // zero past N and K
+        for (int idx = tid; idx < kMtRows * 4; idx += kMtThreads) {
+            const int r = idx >> 2, j = idx & 3, blk = 2 * t + (j >> 1);
+            const bool in = row0 + r < d.N && blk * 128 < d.K;
+            const uint8_t* src = d.i2s + (in ? ((size_t)(row0 + r) * src_blocks + blk0 + blk) * 32 + (j & 1) * 16 : 0);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                             base + (uint32_t)(kMtCodeOff + (t % 3) * kMtCodes + r * 64 + j * 16)),
+                         "l"(src), "r"(in ? 16u : 0u)
+                         : "memory");
+        }
         // the columns' 2^ea ride in the same group (16-byte copies, zero past K)
         for (int r4 = tid; r4 < kMtCols / 4; r4 += kMtThreads) {
             const int col = t * kMtCols + 4 * r4;
@@ -235,19 +252,7 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // I2_S codes of this thread's 64 columns of tile u (32 bytes), one tile ahead
-    uint4 wn[2];
-    auto load_codes = [&](int u) {
-        const int colh = u * kMtCols + cq * 64;
-        wn[0] = wn[1] = make_uint4(0u, 0u, 0u, 0u);
-        if (u < ntiles && n < d.N && colh < d.K) {
-            const uint8_t* blk = d.i2s + ((size_t)n * src_blocks + blk0 + (colh >> 7)) * 32;
-            wn[0] = __ldcs(reinterpret_cast<const uint4*>(blk));
-            wn[1] = __ldcs(reinterpret_cast<const uint4*>(blk + 16));
-        }
-    };
     bool ok = true;
-    load_codes(0);
     load_tile(0, 0);
     for (int t = 0; t <= ntiles; ++t) {
         // MMA(t - 1) done: its A^T buffer is free for tile t + 1, its accumulator ready
@@ -283,10 +288,11 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
             const int u = t - 1, ubuf = u & 1;
             const int colh = u * kMtCols + cq * 64;      // first of this thread's 64 columns
             const bool rowok = ok && colh < d.K;   // (uniform over the warp)
-            // their I2_S codes (half of one 128-column block, 32 bytes) were
-            // requested during the previous tile; request the next tile's now
-            const uint32_t words[8] = {wn[0].x, wn[0].y, wn[0].z, wn[0].w, wn[1].x, wn[1].y, wn[1].z, wn[1].w};
-            load_codes(u + 1);
+            // their I2_S codes: the 32-byte block of this row that holds them
+            const uint4* cw = reinterpret_cast<const uint4*>(smem + kMtCodeOff + (u % 3) * kMtCodes + rloc * 64 +
+                                                             (cq >> 1) * 32);
+            const uint4 w0 = cw[0], w1 = cw[1];
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
             // per row: alpha / r times 2^eb (both exact powers-of-two scalings of
             // the delta, applied as (acc * 2^ea) * (sf * 2^eb): one rounding, as
             // the reference's delta * sf)
