@@ -105,7 +105,7 @@ __global__ void batch_pick_kernel(const KeySources src, int B, int* __restrict__
     if (b >= B) return;
     unsigned long long k = 0ull;
     for (int r = 0; r < src.n; ++r) k = key_max(k, __ldcg(src.p[r] + b));
-    next[b] = argmax_index(k);
+    next[b] = k ? argmax_index(k) : 0;   // every logit NaN: token 0, never index -1
 }
 
 tvb_status batch_attention(const float* q, const float* kcache, const float* vcache, size_t slot_stride,

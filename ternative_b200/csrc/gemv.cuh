@@ -796,9 +796,13 @@ __device__ __forceinline__ void lmhead_finish(const GemvArgs& a, const GemvArgma
                     a.st->tp_epoch = e;   // (the decode step's exit writes the same value)
                 }
             }
-            a.st->next_token = argmax_index(fin);
-            a.st->max_logit = argmax_value(fin);
-            a.st->token = argmax_index(fin);
+            // No key at all (every logit NaN): token 0, what a first-index
+            // argmax that skips NaN (every comparison false) returns; never the
+            // out-of-range index an empty key would decode to.
+            const int tok = fin ? argmax_index(fin) : 0;
+            a.st->next_token = tok;
+            a.st->max_logit = fin ? argmax_value(fin) : -INFINITY;
+            a.st->token = tok;
             a.st->pos = a.st->pos + 1;
             a.st->argmax_key = 0ull;
             a.st->lm_done = 0u;
