@@ -72,6 +72,7 @@ __device__ __forceinline__ bool grid_wait(StepState* st, unsigned target) {
         }
         s_ok = ok;
     }
+    trace_stamp(7);   // (thread 0: its poll saw the last arrival)
     __syncthreads();
     return s_ok != 0;
 }

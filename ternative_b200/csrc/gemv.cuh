@@ -38,7 +38,8 @@ enum GemvMode { GM_PLAIN = 0, GM_QKV = 1, GM_RESID = 2, GM_GATEUP = 3, GM_LMHEAD
 // fixed points of each phase into the buffer given to tvb_trace_set, laid out
 // [phase][CTA][kTraceEvents].  Events: 0 phase start, 1 inputs staged (GEMV
 // prologue done / attention item done), 2 weight stream done, 3 epilogue done,
-// 6 barrier arrival made, 4 next phase prepared, 5 barrier passed.
+// 6 barrier arrival made, 4 next phase prepared, 7 thread 0's barrier poll
+// succeeded, 5 barrier passed (every warp of the CTA past it).
 constexpr int kTraceEvents = 8;
 #ifdef TVB_PHASE_TRACE
 static __device__ unsigned long long* g_trace_buf;

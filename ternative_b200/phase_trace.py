@@ -16,6 +16,10 @@ prints, per phase kind averaged over the layers:
   last_arrive  slowest CTA's arrival minus the median CTA's (straggling)
   bar_us       last arrival -> first CTA out of the barrier (barrier latency)
   exit_spread  first -> last CTA out of the barrier
+  poll_us      last arrival -> thread 0's poll saw it (median CTA); poll_spread:
+               first -> last CTA whose poll saw it
+  after_poll   thread 0's poll -> every warp of its CTA past the barrier (the
+               other warps still staging / requesting the next phase)
 
 Usage:  python -m ternative_b200.phase_trace [--config bitnet-2b] [--layers N]
         [--prompt 32] [--steps 8] [--json out.json] [--lib path/to/trace/build.so]
@@ -66,6 +70,12 @@ def summarize(T, kinds):
             r["last_arrive_us"] = (np.max(t[:, 6]) - np.median(t[:, 6])) / 1e3
             r["bar_us"] = (np.min(t[:, 5]) - np.max(t[:, 6])) / 1e3
             r["exit_spread_us"] = (np.max(t[:, 5]) - np.min(t[:, 5])) / 1e3
+            # thread 0's poll saw the last arrival (median CTA) and the wait
+            # from there until every warp of the CTA was past the barrier
+            r["poll_us"] = (np.median(t[:, 7]) - np.max(t[:, 6])) / 1e3
+            r["poll_spread_us"] = (np.max(t[:, 7]) - np.min(t[:, 7])) / 1e3
+            r["after_poll_us"] = np.median(t[:, 5] - t[:, 7]) / 1e3
+            r["after_poll_max_us"] = np.max(t[:, 5] - t[:, 7]) / 1e3
         rows.setdefault(k, []).append(r)
     out = {}
     for k, lst in rows.items():
@@ -133,7 +143,8 @@ def main(argv=None):
         "kinds": summarize(T, phase_kinds(cfg.num_layers)),
     }
     hdr = ["phases", "step_us", "inputs_us", "inputs_max_us", "stream_us", "stream_max_us", "epi_us",
-           "arrive_us", "prep_us", "last_arrive_us", "bar_us", "exit_spread_us"]
+           "arrive_us", "prep_us", "last_arrive_us", "bar_us", "exit_spread_us", "poll_us", "poll_spread_us",
+           "after_poll_us", "after_poll_max_us"]
     print(f"{args.config}{' INT8' if args.int8 else ''}, {cfg.num_layers} layers, {G} CTAs, kv_len {pos + 2}: "
           f"step {step_us:.1f} us "
           f"(CUDA events), traced span {summary['traced_span_us']:.1f} us, timer resolution "
