@@ -158,6 +158,23 @@ __global__ void mt_prep_a(const __grid_constant__ MtBatch b) {
     const_cast<float*>(d.fa)[k] = mt_pow2(e);
 }
 
+// Packed F32 pairs (one instruction for two IEEE-rounded lanes).
+__device__ __forceinline__ float2 mt_mul2(float2 a, float2 b) {
+    uint64_t d;
+    const uint64_t ua = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
+    const uint64_t ub = (uint64_t)__float_as_uint(b.x) | ((uint64_t)__float_as_uint(b.y) << 32);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
+    return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+__device__ __forceinline__ float2 mt_fma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    const uint64_t ua = (uint64_t)__float_as_uint(a.x) | ((uint64_t)__float_as_uint(a.y) << 32);
+    const uint64_t ub = (uint64_t)__float_as_uint(b.x) | ((uint64_t)__float_as_uint(b.y) << 32);
+    const uint64_t uc = (uint64_t)__float_as_uint(c.x) | ((uint64_t)__float_as_uint(c.y) << 32);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(ua), "l"(ub), "l"(uc));
+    return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+
 __device__ __forceinline__ void mt_fail(unsigned* status) {
     if (status) atomicOr(status, kStatusTimeout);
 }
@@ -298,7 +315,9 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
             // the reference's delta * sf)
             const float g = d.sf * mt_pow2(eb_s[rloc]);
             const float4* fa4 = reinterpret_cast<const float4*>(fa_s + (u % 3) * kMtCols + cq * 64);
-            const float sp = d.scale, sn = -d.scale;
+            // bits of map2bit(code) * scale (tensor.cpp:1020): code 0 -> -scale,
+            // 2 -> +scale (the sign bit flipped by the code's bit 1), 1 and 3 -> +0
+            const uint32_t sn_bits = __float_as_uint(-d.scale);
             for (int c = 0; c < 2; ++c) {
                 __syncwarp();
                 uint32_t acc[32];
@@ -317,16 +336,25 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 fa = fa4[c * 8 + j4];
-                    const float fg[4] = {fa.x * g, fa.y * g, fa.z * g, fa.w * g};
+                    // column j = 4 j4 + i: its code is bits [8 i + 1, 8 i] of cw
+                    const uint32_t cw = words[j4] >> shift;
+                    float bv[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const int j = 4 * j4 + i;
-                        const uint32_t code = (words[j >> 2] >> (8 * (j & 3) + shift)) & 3u;
-                        // map2bit {-1, 0, +1, 0} times the scale (tensor.cpp:1020)
-                        const float bv = (code & 1u) ? 0.0f : (code ? sp : sn);
-                        mv[j] = __fmaf_rn(__uint_as_float(acc[j]), fg[i], bv);
-                        mx = fmaxf(mx, fabsf(mv[j]));
+                        uint32_t odd;
+                        asm("bfe.s32 %0, %1, %2, 1;" : "=r"(odd) : "r"(cw), "r"(8 * i));   // -1 for codes 1, 3
+                        bv[i] = __uint_as_float((sn_bits ^ ((cw << (30 - 8 * i)) & 0x80000000u)) & ~odd);
                     }
+                    const float2 gg = make_float2(g, g);
+                    const float2 m01 = mt_fma2(make_float2(__uint_as_float(acc[4 * j4]), __uint_as_float(acc[4 * j4 + 1])),
+                                               mt_mul2(make_float2(fa.x, fa.y), gg), make_float2(bv[0], bv[1]));
+                    const float2 m23 = mt_fma2(make_float2(__uint_as_float(acc[4 * j4 + 2]), __uint_as_float(acc[4 * j4 + 3])),
+                                               mt_mul2(make_float2(fa.z, fa.w), gg), make_float2(bv[2], bv[3]));
+                    mv[4 * j4] = m01.x;
+                    mv[4 * j4 + 1] = m01.y;
+                    mv[4 * j4 + 2] = m23.x;
+                    mv[4 * j4 + 3] = m23.y;
+                    mx = fmaxf(fmaxf(mx, fmaxf(fabsf(m01.x), fabsf(m01.y))), fmaxf(fabsf(m23.x), fabsf(m23.y)));
                 }
                 uint32_t packed[16];
                 if (mx < 65536.0f) {
