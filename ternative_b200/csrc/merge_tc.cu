@@ -59,11 +59,14 @@ struct MtDesc {
     float scale;             // I2_S per-tensor scale
     float sf;                // alpha / r
     int K, N, r, k0, ld;
+    int a_row0;              // first row of ath / atl in the launch's plane maps
 };
 
 struct MtBatch {
     MtDesc d[kMtMaxDescs];
     const CUtensorMap* omaps;   // [n] output maps (device memory): dst [N][K] F16, 32 x 32 boxes
+    const CUtensorMap* amaps;   // [2] the A^T hi and lo planes of every tensor of the launch
+                                // ([columns][64] F16, 256-row boxes, 128-byte swizzle)
     int cta_start[kMtMaxDescs + 1];   // merge CTAs (128-row stripes)
     int row_start[kMtMaxDescs + 1];   // prep warps (rows of B)
     int col_start[kMtMaxDescs + 1];   // prep threads (columns of A)
@@ -189,8 +192,8 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
     const uint32_t b_op = base + 2 * kMtAop;                    // [buf][plane] tiles of kMtBop
     float* fa_s = reinterpret_cast<float*>(smem + 2 * kMtAop + 4 * kMtBop);   // [3][256] 2^ea, tile % 3
     int* eb_s = reinterpret_cast<int*>(fa_s + 3 * kMtCols);                   // [128]
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(eb_s + kMtRows);        // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 2);
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(eb_s + kMtRows);        // [2] MMA done, [2] A^T tile landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int di = mt_find(b, blockIdx.x);
@@ -210,8 +213,7 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
     }
     for (int r = tid; r < kMtRows; r += kMtThreads) eb_s[r] = row0 + r < d.N ? d.eb[row0 + r] : 0;
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
+        for (int i = 0; i < 4; ++i) mbar_init(&mbar[i], 1);
         fence_barrier_init();
     }
     if (warp == 0) tmem_alloc(tmem_slot, 512);
@@ -228,24 +230,23 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
     // launch: acquire it for the tensor-map proxy before the first store
     if (lane == 0)
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(b.omaps + di) : "memory");
+    if (tid == 0)
+        for (int i = 0; i < 2; ++i)
+            asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(b.amaps + i) : "memory");
     const int rloc = 32 * q + lane;
     const int src_blocks = d.ld >> 7, blk0 = d.k0 >> 7;
-    // A^T tile t (256 columns, hi and lo) into buffer `buf`, and the tile's
-    // codes and column exponents into rotating slot t % 3: asynchronous 16-byte
-    // copies (the A^T planes into the swizzled layout), zero-filled past N / K
+    // A^T tile t (256 columns, hi and lo) into buffer `buf`: two TMA loads
+    // (128-byte swizzle, the layout the MMA descriptors expect) completing on
+    // mbar[2 + buf].  Rows past this tensor's K belong to the next tensor of
+    // the launch (zeros past the last): they only reach output columns past K,
+    // which the tile's stores clip.  The tile's codes and column exponents go
+    // into rotating slot t % 3 by asynchronous 16-byte copies, zero past N / K.
     auto load_tile = [&](int t, int buf) {
-        const uint32_t dst = b_op + (uint32_t)(2 * buf) * kMtBop;
-        for (int idx = tid; idx < kMtCols * 8; idx += kMtThreads) {
-            const int r = idx >> 3, c = idx & 7, col = t * kMtCols + r;
-            const bool in = col < d.K;
-            const size_t off = in ? (size_t)col * kMtRank + c * 8 : 0;
-            const uint32_t nb = in ? 16u : 0u;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + sw128_offset(r, c)),
-                         "l"(d.ath + off), "r"(nb)
-                         : "memory");
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst + kMtBop + sw128_offset(r, c)),
-                         "l"(d.atl + off), "r"(nb)
-                         : "memory");
+        if (tid == 0) {
+            const uint32_t dst = b_op + (uint32_t)(2 * buf) * kMtBop;
+            mbar_expect_tx(&mbar[2 + buf], 2u * kMtBop);
+            tma_load_2d(dst, b.amaps, 0, d.a_row0 + t * kMtCols, &mbar[2 + buf]);
+            tma_load_2d(dst + kMtBop, b.amaps + 1, 0, d.a_row0 + t * kMtCols, &mbar[2 + buf]);
         }
         // the stripe's I2_S codes of these columns (two 32-byte blocks a row),
         // zero past N and K
@@ -286,6 +287,10 @@ merge_tc_kernel(const __grid_constant__ MtBatch b, unsigned* status) {
             tc_fence_before();
             __syncthreads();
             tc_fence_after();
+            if (tid == 0 && ok && !mbar_wait_bounded(&mbar[2 + buf], (uint32_t)((t >> 1) & 1))) {
+                ok = false;
+                mt_fail(status);
+            }
             if (tid == 0 && ok) {
                 constexpr uint32_t idesc = umma_idesc_f16(kMtRows, kMtCols);
                 const uint32_t dcol = tmem + (uint32_t)(buf * kMtCols);
@@ -560,18 +565,33 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
             rows += (size_t)descs[base + i].N;
             cols += (size_t)descs[base + i].K;
         }
-        // (output tensor maps first: 128-byte aligned)
-        const size_t map_bytes = (size_t)cnt * sizeof(CUtensorMap);
+        // (output tensor maps, then the two A^T plane maps, first: 128-byte aligned)
+        const size_t map_bytes = (size_t)(cnt + 2) * sizeof(CUtensorMap);
         const size_t bytes = map_bytes + 2 * (rows + cols) * kMtRank * 2 + (rows + cols) * 4 + 256;
         unsigned char* ws = nullptr;
         TVB_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st));
-        static thread_local CUtensorMap omaps[kMtMaxDescs];
+        static thread_local CUtensorMap omaps[kMtMaxDescs + 2];
         for (int i = 0; i < cnt; ++i) {
             const tvb_merge_desc& sd = descs[base + i];
             const uint64_t dims[2] = {(uint64_t)sd.K, (uint64_t)sd.N};
             const uint64_t strides[1] = {(uint64_t)sd.K * 2};
             const uint32_t box[2] = {32u, 32u};
             tvb_status es = encode_f16_tiled(&omaps[i], sd.dst, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+            if (es != TVB_OK) {
+                cudaFreeAsync(ws, st);
+                return es;
+            }
+        }
+        uint16_t* bh = reinterpret_cast<uint16_t*>(ws + map_bytes);
+        uint16_t* bl = bh + rows * kMtRank;
+        uint16_t* ah = bl + rows * kMtRank;
+        uint16_t* al = ah + cols * kMtRank;
+        for (int i = 0; i < 2; ++i) {
+            const uint64_t dims[2] = {(uint64_t)kMtRank, (uint64_t)cols};
+            const uint64_t strides[1] = {(uint64_t)kMtRank * 2};
+            const uint32_t box[2] = {(uint32_t)kMtRank, (uint32_t)kMtCols};
+            tvb_status es = encode_f16_tiled(&omaps[cnt + i], i ? al : ah, 2, dims, strides, box,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
             if (es != TVB_OK) {
                 cudaFreeAsync(ws, st);
                 return es;
@@ -585,10 +605,7 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
             }
         }
         b.omaps = reinterpret_cast<const CUtensorMap*>(ws);
-        uint16_t* bh = reinterpret_cast<uint16_t*>(ws + map_bytes);
-        uint16_t* bl = bh + rows * kMtRank;
-        uint16_t* ah = bl + rows * kMtRank;
-        uint16_t* al = ah + cols * kMtRank;
+        b.amaps = b.omaps + cnt;
         int* eb = reinterpret_cast<int*>(al + cols * kMtRank);
         // (16-byte aligned: the kernel copies it in 16-byte pieces)
         float* fa = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(eb + rows) + 15) & ~(uintptr_t)15);
@@ -614,6 +631,7 @@ tvb_status merge_tc(const tvb_merge_desc* descs, int n, tvb_dtype out, cudaStrea
             d.r = s.r;
             d.k0 = s.k0;
             d.ld = s.ld ? s.ld : s.K;
+            d.a_row0 = (int)co;
             b.cta_start[i] = ctas;
             b.row_start[i] = rwarps;
             b.col_start[i] = cthreads;
