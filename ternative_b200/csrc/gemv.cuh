@@ -112,9 +112,6 @@ __device__ __forceinline__ float* tp_slot(float* buf, const TpArgs& t, unsigned 
     return buf + kTpSlots + (size_t)(epoch & 1u) * t.world * t.ld;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -167,11 +164,17 @@ __device__ __forceinline__ bool tp_flag_wait(const TpArgs& t, unsigned n, int G,
 }
 
 // Tell every rank that this rank's writes for argmax exchange `epoch` are done
-// (one thread; the writes it covers were ordered before it at system scope).
+// (one thread): one system-scope fence orders them before the flag stores
+// (with the relaxed stores, a release pattern), which then go to every rank
+// without waiting for each other (a release store per rank waited for the
+// previous rank's store to be acknowledged over NVLink).
 __device__ __forceinline__ void tp_signal(const TpArgs& t, unsigned epoch) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int r = 0; r < t.world; ++r)
-        st_release_sys(reinterpret_cast<unsigned*>(t.peer[r] + kTpFlags) + t.rank, epoch);
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(reinterpret_cast<unsigned*>(t.peer[r] + kTpFlags) +
+                                                               t.rank),
+                     "r"(epoch)
+                     : "memory");
 }
 
 // Wait (one thread, bounded by about a second) until every rank has signalled

@@ -37,37 +37,52 @@ __global__ void tp_sync_kernel(const __grid_constant__ TpArgs t, StepState* st) 
 
 // Row s of x [S][H] += inv_s * (sum over ranks, in rank order, of their partial
 // row s at float offset `off`), inv_s = 1/sqrt(sum_r ss_r[s] / norm_n + eps)
-// (tensor.cpp:672-673) or 1 without a sub-norm (norm_n == 0).
+// (tensor.cpp:672-673) or 1 without a sub-norm (norm_n == 0).  Block (s, y)
+// takes float4 y * blockDim.x + tid of row s.  The partials live in every
+// rank's own buffer and are read over NVLink: a thread issues all ranks' loads
+// (and thread 0 all ranks' sums of squares) before it uses any, so the kernel
+// waits one remote round trip, where a loop of load-then-add waited one per
+// rank and per float4.
 __global__ void tp_reduce_rows_kernel(const __grid_constant__ TpArgs t, size_t off, int S, int H, int norm_n,
                                       float eps, float* __restrict__ x) {
     pdl_wait();   // launched after the kernel that writes this one's inputs
     pdl_launch_dependents();
     const int row = blockIdx.x, tid = threadIdx.x;
+    const int k = blockIdx.y * blockDim.x + tid;
+    const bool in = k < (H >> 2);
+    const size_t base = off + (size_t)row * H;
+    float4* x4 = reinterpret_cast<float4*>(x + (size_t)row * H);
+    float4 p[kMaxTp];
+    float ssr[kMaxTp];
+#pragma unroll
+    for (int r = 0; r < kMaxTp; ++r) {
+        p[r] = (r < t.world && in) ? __ldcg(reinterpret_cast<const float4*>(t.peer[r] + base) + k)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        ssr[r] = (tid == 0 && norm_n > 0 && r < t.world) ? __ldcg(t.peer[r] + off + (size_t)S * H + row) : 0.f;
+    }
+    float4 v = in ? x4[k] : make_float4(0.f, 0.f, 0.f, 0.f);
     __shared__ float s_inv;
     if (tid == 0) {
         float inv = 1.0f;
         if (norm_n > 0) {
             float ss = 0.f;
-            for (int r = 0; r < t.world; ++r) ss += __ldcg(t.peer[r] + off + (size_t)S * H + row);
+#pragma unroll
+            for (int r = 0; r < kMaxTp; ++r)
+                if (r < t.world) ss += ssr[r];
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)norm_n), eps)));
         }
         s_inv = inv;
     }
     __syncthreads();
+    if (!in) return;
     const float inv = s_inv;
-    const size_t base = off + (size_t)row * H;
-    float4* x4 = reinterpret_cast<float4*>(x + (size_t)row * H);
-    for (int k = tid; k < (H >> 2); k += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < t.world; ++r) {
-            const float4 p = __ldcg(reinterpret_cast<const float4*>(t.peer[r] + base) + k);
-            acc = make_float4(acc.x + p.x, acc.y + p.y, acc.z + p.z, acc.w + p.w);
-        }
-        float4 v = x4[k];
-        v = make_float4(__fadd_rn(v.x, acc.x * inv), __fadd_rn(v.y, acc.y * inv), __fadd_rn(v.z, acc.z * inv),
-                        __fadd_rn(v.w, acc.w * inv));
-        x4[k] = v;
-    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxTp; ++r)
+        if (r < t.world) acc = make_float4(acc.x + p[r].x, acc.y + p[r].y, acc.z + p[r].z, acc.w + p[r].w);
+    v = make_float4(__fadd_rn(v.x, acc.x * inv), __fadd_rn(v.y, acc.y * inv), __fadd_rn(v.z, acc.z * inv),
+                    __fadd_rn(v.w, acc.w * inv));
+    x4[k] = v;
 }
 
 size_t tp_prefill_region_floats(int rows, int H) {
@@ -82,7 +97,9 @@ tvb_status tp_sync(const TpArgs& t, StepState* st, cudaStream_t stream, bool pdl
 tvb_status tp_reduce_rows(const TpArgs& t, size_t off, int S, int H, int norm_n, float eps, float* x,
                           cudaStream_t stream, bool pdl) {
     TVB_REQUIRE(S > 0 && H % 4 == 0 && off % 4 == 0, "tp_reduce_rows: bad arguments");
-    TVB_CUDA(launch_maybe_pdl(tp_reduce_rows_kernel, dim3(S), dim3(256), 0, stream, pdl, t, off, S, H, norm_n, eps, x));
+    const int n4 = H >> 2;
+    TVB_CUDA(launch_maybe_pdl(tp_reduce_rows_kernel, dim3(S, (n4 + 255) / 256), dim3(256), 0, stream, pdl, t, off, S, H,
+                              norm_n, eps, x));
     return check_launch("tp_reduce_rows_kernel");
 }
 
