@@ -6,8 +6,9 @@ cudaMalloc/cudaFree can imply).
 
 Checked through the C ABI against tvb_attention_decode on the same inputs,
 twice in a row (the shared scratch keeps the previous call's contents), with
-the tolerance of the other attention tests.  Kept in its own file, named to be
-collected last."""
+the tolerance of the other attention tests, and against the oracle's
+restatement of the reference's decode attention (cuda/ops_cuda.cu:205-259).
+Kept in its own file, named to be collected last."""
 import ctypes as C
 
 import numpy as np
@@ -39,18 +40,18 @@ def attention_pair(lib, torch, nh, nkv, kv_len, seed):
                                             got.data_ptr(), nh, nkv, hd, scale, None) == 0, \
         lib.tvb_last_error()
     torch.cuda.synchronize()
-    return got.cpu().numpy(), ref.cpu().numpy()
+    return got.cpu().numpy(), ref.cpu().numpy(), (q.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy())
 
 
-def test_noalloc_attention_matches_attention_decode(cuda):
+def test_noalloc_attention_matches_attention_decode(cuda, restated):
     import torch
     from ternative_b200 import load
     lib = load()
     # two calls in a row: a long context (8 splits), then a short one (1 split)
-    got, ref = attention_pair(lib, torch, 32, 8, 1000, 1)
-    close(got, ref)
-    got, ref = attention_pair(lib, torch, 20, 5, 37, 2)
-    close(got, ref)
+    for nh, nkv, kv_len, seed in ((32, 8, 1000, 1), (20, 5, 37, 2)):
+        got, ref, (q, kc, vc) = attention_pair(lib, torch, nh, nkv, kv_len, seed)
+        close(got, ref)
+        close(got, restated.attention_decode(q, kc, vc, kv_len, nh, nkv, 128))
 
 
 def test_noalloc_attention_rejects_oversize(cuda):
